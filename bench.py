@@ -1,0 +1,379 @@
+"""Benchmark: NeuralScript CUDA-backend hot path on B200.
+
+Default workload (configs[1] of BASELINE.json): the config-2 transformer block
+forward through ns_eval_infer, tokens [64, 256] per GPU, bf16 tensor cores,
+random-init weights N(0, 0.02), synthetic token ids (seeded). With
+--config c4 it times the config-4 AOT train step (block + 512->8192 head, CE,
+AdamW, cosine schedule) instead.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c4] [--impl b200|reference]
+
+N > 1 runs under torchrun, one process per GPU: inference is replicated
+(each rank its own batch, no collective; "scaling": "weak"); the train step
+all-reduces gradients over NCCL. Timing: per-step CUDA events on the stream
+the engine is driven from, L2 flushed between steps (a 512 MB write outside
+the timed events), max over ranks. `e2e` times the reference-facing C-ABI
+call (ns_eval_infer / ns_runtime_train_step) with host buffers, copies
+included. `--impl reference` times the reference's own CPU code
+(oracle/_ref, emitted by the reference compiler) on this host's cores.
+"""
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def config_shapes(cfg):
+    from neuralscript_b200.spec import CONFIGS
+    return CONFIGS[cfg]
+
+
+def c2_flops_per_token():
+    D, F, S = 512, 2048, 256
+    gemm = 2 * D * 3 * D + 2 * D * D + 2 * D * F * 2
+    attn = 4 * S * D  # QK^T and PV per token (H * dh = D)
+    return gemm + attn
+
+
+def c4_flops_per_token():
+    D, F, V = 512, 2048, 8192
+    fwd = c2_flops_per_token() + 2 * D * V
+    return 3 * fwd  # forward + backward (2x)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([s.strip() for s in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 3 + i and
+                          s[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# reference CPU arm
+# ---------------------------------------------------------------------------
+def _ref_worker(args):
+    import ctypes as C
+    lib_path, seqs, seed = args
+    L = C.CDLL(lib_path)
+    L.ns_runtime_init.restype = C.c_void_p
+    L.ns_runtime_init.argtypes = [C.c_void_p, C.c_size_t]
+    L.ns_eval_infer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]
+    from neuralscript_b200 import synth
+    from neuralscript_b200.spec import C2, parse
+    s = parse(C2)
+    w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
+    m = L.ns_runtime_init(w.ctypes.data, w.size)
+    out = np.empty(256 * 512, np.float32)
+    t0 = time.perf_counter()
+    for q in range(seqs):
+        tok = synth.tokens(256, seed + q, 8192)
+        L.ns_eval_infer(m, tok.ctypes.data, out.ctypes.data, 256)
+    return time.perf_counter() - t0
+
+
+def ref_lib_path():
+    p = os.path.join(ROOT, "oracle", "_ref", "libref_c2.so")
+    return p if os.path.exists(p) else None
+
+
+def cpu_reference_throughput(seqs_per_worker, workers):
+    """tokens/s of the reference's emitted CPU code for config 2, one call
+    per 256-token sequence (the reference attends over the whole call)."""
+    path = ref_lib_path()
+    if path is None:
+        return None
+    if workers == 1:
+        dt = _ref_worker((path, seqs_per_worker, 9001))
+        return 256 * seqs_per_worker / dt
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers) as pool:
+        t0 = time.perf_counter()
+        pool.map(_ref_worker, [(path, seqs_per_worker, 9001 + 100 * i) for i in range(workers)])
+        dt = time.perf_counter() - t0
+    return 256 * seqs_per_worker * workers / dt
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    metric, unit = "tokens_per_s_ns_eval_infer_c2", "tokens/s"
+    path = ref_lib_path()
+    if path is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
+        return 0
+    cores = os.cpu_count() or 1
+    # one step = one 256-token sequence per core (a bounded sample of the batch)
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_reference_throughput(1, 1)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(cpu_reference_throughput(1, cores))
+    dt = time.perf_counter() - t0
+    v = float(np.median(vals))
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * dt / max(args.steps, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config 2 transformer block forward, reference CPU emit (nsc --cpp --runtime), "
+                                   "one ns_eval_infer call per 256-token sequence", "seq_len": 256,
+                       "tokens_per_step": 256 * cores},
+            "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": "reference",
+                             "sample": f"{cores} sequences of 256 tokens per step, one process per core"},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def time_gemm(O, torch, M, N, K, act, steps, stream_ptr):
+    """Average device time of one GEMM launch with the engine's operand
+    layouts (A K-major bf16, W [K,N] as MN-major B)."""
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = torch.randn(K, N, device="cuda").bfloat16()
+    C16 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        O.gemm(A, B, M, N, K, K, 0, N, 1, act=act, c16=C16)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        O.gemm(A, B, M, N, K, K, 0, N, 1, act=act, c16=C16)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps / 1e3
+
+
+def run_b200(args):
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    import neuralscript_b200 as nsb
+    from neuralscript_b200 import ops as O
+    from neuralscript_b200 import synth
+    from neuralscript_b200.spec import CONFIGS, parse
+
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    cfg = args.config
+    spec = CONFIGS[cfg]
+    s = parse(spec)
+    w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
+    model = nsb.Model(spec, w, precision=args.precision)
+    B, S = 64, 256
+    M = B * S
+    tok = torch.from_numpy(synth.tokens(M, 301 + 7919 * rank, 8192)).cuda()
+    train = cfg == "c4"
+    if train:
+        if world > 1:
+            uid = nsb.dist_unique_id() if rank == 0 else bytes(128)
+            obj = [uid]
+            dist.broadcast_object_list(obj, src=0)
+            model.dist_init(rank, world, obj[0], 120000)
+        tgt = torch.from_numpy(synth.tokens(M, 401 + 7919 * rank, 8192).astype(np.int32)).cuda()
+        labels = None
+        if args.one_hot:
+            labels = torch.zeros(M, 8192, device="cuda")
+            labels[torch.arange(M), tgt.long()] = 1.0
+    out = torch.empty(M, s.out_cols if hasattr(s, "out_cols") else 512, device="cuda")
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        if train:
+            model.train_step_device(tok, labels=labels, targets=None if labels is not None else tgt, lr=3e-4,
+                                    stream=sp, want_loss=False)
+        else:
+            model.infer_device(tok, out, stream=sp)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches = model.last_launch_count()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()  # evict L2 (126 MB) between timed steps; outside the events
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    clk = clocks.stop()
+    ms_step = ms / args.steps
+    tokens_step = M * world
+    value = tokens_step / (ms_step / 1e3)
+
+    # end to end through the reference-facing ABI with host buffers
+    tok_h = tok.cpu().numpy()
+    if train:
+        tgt_h = tgt.cpu().numpy()
+        y1h = None
+        if args.e2e_one_hot:
+            y1h = np.zeros((M, 8192), np.float32)
+            y1h[np.arange(M), tgt_h] = 1.0
+        e2e_fn = (lambda: model.train_step(tok_h, y1h, 3e-4)) if y1h is not None else \
+            (lambda: model.train_step_idx(tok_h, tgt_h, 3e-4))
+        h2d = tok_h.nbytes + (y1h.nbytes if y1h is not None else tgt_h.nbytes)
+        d2h = 4
+    else:
+        e2e_fn = lambda: model.infer(tok_h)
+        h2d = tok_h.nbytes
+        d2h = M * 512 * 4
+    for _ in range(2):
+        e2e_fn()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    n_e2e = max(3, min(args.steps, 10))
+    for _ in range(n_e2e):
+        e2e_fn()
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": tokens_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h)}
+
+    # roofline of the dominant GEMM (ff1: 16384 x 2048 x 512, GELU epilogue)
+    pk, pk_kind = peaks()
+    t_ff1 = time_gemm(O, torch, M, 2048, 512, 6, 20, sp)
+    flops_ff1 = 2.0 * M * 2048 * 512
+    ach = flops_ff1 / t_ff1 / 1e12
+    roof = {"kernel": "gemm_tc_kernel bf16 ff1 16384x2048x512 (+GELU)", "bound": "tensor",
+            "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+            "peak_kind": f"{pk_kind} bf16 burst", "traffic": None}
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if args.cpu_baseline and not train:
+            v = cpu_reference_throughput(2, 1)
+            if v is not None:
+                cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                       "sample": "2 sequences x 256 tokens through the reference CPU emit (libref_c2.so)"}
+        fl = c4_flops_per_token() if train else c2_flops_per_token()
+        result = {
+            "metric": "tokens_per_s_ns_runtime_train_step_c4" if train else "tokens_per_s_ns_eval_infer_c2",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.precision, "data": "synthetic",
+            "config": {"workload": ("config 4 AOT train step (c2 block + 512->8192 head, CE, AdamW, cosine)"
+                                    if train else "config 2 transformer block forward (ns_eval_infer)"),
+                       "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
+                       "labels": ("one-hot" if args.one_hot else "int32 targets") if train else None,
+                       "l2": "flushed between steps (512 MB write outside timing)"},
+            "model_tflops": fl * value / 1e12,
+            "step_frac_of_bf16_peak": fl * value / world / 1e12 / pk["bf16_tflops"],
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": int(launches) * args.steps,
+        }
+        print(json.dumps(result))
+    if world > 1:
+        dist.barrier()
+        model.close()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c4"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--one-hot", action="store_true", help="c4: dense one-hot labels on the device path")
+    ap.add_argument("--e2e-one-hot", action="store_true", help="c4: e2e through the one-hot ABI")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,106 @@
+/* Kernel-level C-ABI of libns_b200.so: the hot-path kernels on caller-owned
+ * DEVICE pointers, one call per kernel family, for tests, benchmarks and
+ * integrators that drive their own buffers. Each entry names the reference
+ * computation it replaces (file:line in MrModelOS/NeuralScript). `stream` is
+ * a cudaStream_t (NULL = legacy default stream). Returns 0 on success, a
+ * negative value on a bad argument or launch failure. Nothing here
+ * allocates device memory: scratch, where a kernel needs it, is passed in
+ * and its size is given by the matching *_scratch_bytes query.
+ */
+#ifndef NS_B200_OPS_H
+#define NS_B200_OPS_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define NSB_F32 0
+#define NSB_BF16 1
+
+/* engine codes */
+#define NSB_ENGINE_AUTO 0   /* tcgen05 when operands allow, else SIMT */
+#define NSB_ENGINE_SIMT 1   /* exact fp32 FMA, sequential in k */
+#define NSB_ENGINE_TENSOR 2 /* tcgen05 only (error if not possible) */
+
+/* C[M,N] = act(alpha * A[M,K] B[N,K]^T + add) with
+ *   A element (i,k) at A[i*lda + k] (a_mn = 0) or A[k*lda + i] (a_mn = 1),
+ *   B element (n,k) at B[n*ldb + k] (b_mn = 0) or B[k*ldb + n] (b_mn = 1).
+ * Replaces ns_gemm_kernel / ns_grad_a_kernel / ns_grad_w_kernel
+ * (src/codegen/cuda_backend.cpp:58-79, 446-467) and ns_matmul /
+ * ns_matmul_grad_a / ns_matmul_grad_w (src/codegen/codegen.cpp:1257-1337).
+ * act: 0 identity .. 6 GELU (codegen.cpp:1244-1255). add (fp32, ld_add) may be
+ * NULL. c32 / c16 outputs (either may be NULL). workspace: fp32 scratch of
+ * nsb_op_gemm_workspace_floats(...) floats (may be NULL when that is 0). */
+int nsb_op_gemm(int M, int N, int K, const void* A, int a_dtype, long long lda, int a_mn, const void* B, int b_dtype,
+                long long ldb, int b_mn, float alpha, const float* add, long long ld_add, int act, float* c32,
+                long long ldc32, void* c16, long long ldc16, int engine, float* workspace, size_t workspace_floats,
+                int* dev_err, void* stream);
+size_t nsb_op_gemm_workspace_floats(int M, int N, int K, const void* A, int a_dtype, long long lda, int a_mn,
+                                    const void* B, int b_dtype, long long ldb, int b_mn, int engine);
+/* 1 when nsb_op_gemm would run on tcgen05 tensor cores for these operands. */
+int nsb_op_gemm_uses_tensor_cores(int M, int N, int K, const void* A, int a_dtype, long long lda, int a_mn,
+                                  const void* B, int b_dtype, long long ldb, int b_mn, int engine);
+
+/* out = W[(int)ids[r]] (ids fp32; out-of-range -> row 0).
+ * Replaces ns_embedding_kernel (cuda_backend.cpp:172-181), ns_embedding
+ * (codegen.cpp:1711-1718). */
+int nsb_op_embedding_fwd(const float* W, const float* ids, int M, int V, int D, float* out32, void* out16,
+                         void* stream);
+/* dW = deterministic sort-then-segment scatter-add of dout rows by id
+ * (rows in increasing order; out-of-range ids skipped). Replaces
+ * ns_embedding_grad_w_kernel (cuda_backend.cpp:500-512) and
+ * ns_embedding_grad_w (codegen.cpp:1374-1383). */
+size_t nsb_op_embedding_bwd_scratch_bytes(int M, int V);
+int nsb_op_embedding_bwd(const float* dout, const float* ids, int M, int V, int D, float* dW, void* scratch,
+                         void* stream);
+
+/* LayerNorm, no affine, eps 1e-5. Replaces ns_layernorm_kernel /
+ * ns_layernorm_grad_kernel (cuda_backend.cpp:420-431, 473-499),
+ * ns_layernorm / ns_layernorm_grad (codegen.cpp:1280-1291, 1346-1371). */
+int nsb_op_layernorm_fwd(const float* x, int M, int D, float* out32, void* out16, void* stream);
+int nsb_op_layernorm_bwd(const float* dy, const float* x, const float* add, int M, int D, float* dx32, void* dx16,
+                         void* stream);
+
+/* Attention core on qkv [B*S, ld_qkv] (Q | K | V column blocks, heads
+ * concatenated) -> ctx [B*S, ld_ctx]; lse [B*H*S] saved for the backward.
+ * Replaces ns_attention_core_kernel / ns_attention_grad_kernel
+ * (cuda_backend.cpp:186-366) and the per-head core of ns_attention_fwd /
+ * ns_attention_bwd (codegen.cpp:1724-1907). dvec: [B*H*S] fp32 scratch. */
+int nsb_op_attention_fwd(int B, int S, int H, int D, int dtype, const void* qkv, long long ld_qkv, void* ctx,
+                         long long ld_ctx, float* lse, void* stream);
+int nsb_op_attention_bwd(int B, int S, int H, int D, int dtype, const void* qkv, long long ld_qkv, const void* ctx,
+                         long long ld_ctx, const float* lse, const void* dctx, long long ld_dctx, void* dqkv,
+                         long long ld_dqkv, float* dvec, void* stream);
+
+/* Softmax cross-entropy forward + seed gradient: row_loss[r] and
+ * d = (softmax - y) / denom. labels one-hot [M,C] fp32, or targets int32 [M]
+ * when labels is NULL. Replaces ns_ce_row_kernel + ns_loss_grad_kernel
+ * (cuda_backend.cpp:690-719), ns_cross_entropy / ns_loss_grad
+ * (codegen.cpp:1582-1613). */
+int nsb_op_cross_entropy(const float* logits, const float* labels, const int* targets, int M, int C, float denom,
+                         float* row_loss, float* d32, void* d16, void* stream);
+/* out[0] = scale * sum(x[0..n)), fixed reduction order. */
+int nsb_op_reduce_sum(const float* x, int n, float scale, float* out, void* stream);
+
+/* One AdamW step of one tensor (step counter t >= 1). Replaces
+ * ns_adamw_kernel (cuda_backend.cpp:720-733) / codegen.cpp:3108-3120. */
+int nsb_op_adamw(float* w, const float* g, float* m, float* v, long long n, long long t, float lr, float beta1,
+                 float beta2, float one_minus_beta1, float one_minus_beta2, float eps, float decay, void* stream);
+/* Modified Gram-Schmidt in place on an r x c matrix (columns if r >= c, rows
+ * otherwise). Replaces ns_orthonom_kernel (cuda_backend.cpp:747-773) /
+ * ns_orthonom (codegen.cpp:1617-1633). */
+int nsb_op_mgs(float* G, int r, int c, void* stream);
+
+/* Activation forward / derivative product. Replaces ns_act_kernel /
+ * ns_act_grad_kernel (cuda_backend.cpp:80-84, 468-472). */
+int nsb_op_act_fwd(const float* x, size_t n, int act, float* out32, void* out16, void* stream);
+int nsb_op_act_bwd(const float* dy, const float* z, int act, size_t n, float* out32, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NS_B200_OPS_H */

@@ -1,0 +1,1517 @@
+// NeuralScript B200 engine: plans buffers for a spec'd network once per row
+// count, runs its forward pass, reverse-mode backward and optimizer step on
+// one CUDA stream, all-reduces gradients over NCCL when data-parallel, and
+// implements every ns_runtime.h entry point on top (the nsb_* functions).
+//
+// Reference behaviour followed (file:line in MrModelOS/NeuralScript):
+//   forward launcher + C-ABI driver     src/codegen/codegen.cpp:552-1126
+//   train core (fwd, grads, OPT_STEP)   src/codegen/codegen.cpp:3249-3653
+//   CPU twin of both (the oracle)       src/codegen/codegen.cpp:2262-2657, 2755-3157
+//   optimizer constants / LR schedule   include/ns/optim/optim_params.hpp:20-62
+// Deliberate differences: per-sequence attention (`seq`), gradient SUM for
+// values consumed twice (residuals), per-weight AdamW step counters on the
+// device path too, no weight copy-back per step (lazy host mirror), checked
+// CUDA errors (-1 through the unchanged ABI).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <nccl.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <chrono>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/ns_b200.h"
+#include "attention.h"
+#include "engine.h"
+#include "gemm.h"
+#include "kernels.h"
+#include "moe.h"
+
+using nsb::Op;
+using nsb::Val;
+
+namespace nsb {
+
+long long& launch_counter() {
+    static thread_local long long n = 0;
+    return n;
+}
+
+static thread_local std::string g_err;
+
+static int fail(const std::string& msg) {
+    g_err = msg;
+    return -1;
+}
+
+// NCCL is resolved at run time, only when data parallelism is requested:
+// linking it would pin whichever libnccl.so.2 loads first for the whole
+// process (PyTorch needs its own bundled build). An already-loaded copy is
+// preferred.
+struct Nccl {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+static const Nccl& nccl() {
+    static Nccl n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        n.CommInitRankConfig = (decltype(n.CommInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
+        n.CommGetAsyncError = (decltype(n.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+        n.CommAbort = (decltype(n.CommAbort))dlsym(h, "ncclCommAbort");
+        n.CommDestroy = (decltype(n.CommDestroy))dlsym(h, "ncclCommDestroy");
+        n.AllReduce = (decltype(n.AllReduce))dlsym(h, "ncclAllReduce");
+        n.GetErrorString = (decltype(n.GetErrorString))dlsym(h, "ncclGetErrorString");
+        n.ok = n.GetUniqueId && n.CommInitRankConfig && n.CommGetAsyncError && n.CommAbort && n.CommDestroy &&
+               n.AllReduce && n.GetErrorString;
+    });
+    return n;
+}
+
+void* plan_alloc(ns_model* m, size_t bytes) {
+    void* p = nullptr;
+    // 4 KB of slack past every buffer: TMA boxes may read up to one 128-byte
+    // swizzle row past a tensor's logical end.
+    if (cudaMalloc(&p, bytes + 4096) != cudaSuccess) return nullptr;
+    m->plan_allocs.push_back(p);
+    return p;
+}
+
+static void* persist_alloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes + 4096) != cudaSuccess) return nullptr;
+    cudaMemset(p, 0, bytes + 4096);
+    return p;
+}
+
+}  // namespace nsb
+
+using namespace nsb;
+
+// ---------------------------------------------------------------------------
+// graph construction
+// ---------------------------------------------------------------------------
+static int find_val(ns_model* m, const std::string& n) {
+    for (size_t i = 0; i < m->vals.size(); i++)
+        if (m->vals[i].name == n) return (int)i;
+    return -1;
+}
+
+static bool build_graph(ns_model* m, std::string& err) {
+    Spec& s = m->spec;
+    m->vals.clear();
+    m->ops.clear();
+    Val x;
+    x.name = "x";
+    x.cols = s.in_cols;
+    m->vals.push_back(x);
+    for (auto& so : s.ops) {
+        Op op;
+        if (so.fn == "add") op.kind = OP_ADD;
+        else if (so.fn == "sub") op.kind = OP_SUB;
+        else if (so.fn == "mul") op.kind = OP_MUL;
+        else if (so.fn == "softmax") op.kind = OP_SOFTMAX;
+        else if (act_code(so.fn) >= 0) {
+            op.kind = OP_ACT;
+            op.act = act_code(so.fn);
+        } else {
+            op.layer = s.layer_index(so.fn);
+            const LayerSpec& l = s.layers[op.layer];
+            if (l.kind == "dense") {
+                op.kind = OP_DENSE;
+                op.act = act_code(l.gets("act", "identity"));
+            } else if (l.kind == "embedding") op.kind = OP_EMB;
+            else if (l.kind == "attention") op.kind = OP_ATTN;
+            else if (l.kind == "layernorm") op.kind = OP_LN;
+            else if (l.kind == "moe") op.kind = OP_MOE;
+            else if (l.kind == "dropout") op.kind = OP_DROPOUT;
+            for (size_t wi = 0; wi < s.weights.size(); wi++)
+                if (s.weights[wi].layer == op.layer) {
+                    op.widx = (int)wi;
+                    break;
+                }
+        }
+        op.in = find_val(m, so.args[0]);
+        if (so.args.size() > 1) op.in2 = find_val(m, so.args[1]);
+        if (find_val(m, so.out) >= 0) {
+            err = "value " + so.out + " assigned twice";
+            return false;
+        }
+        Val v;
+        v.name = so.out;
+        v.cols = s.width[so.out];
+        v.producer = (int)m->ops.size();
+        m->vals.push_back(v);
+        op.out = op.self_out = (int)m->vals.size() - 1;
+        m->vals[op.in].consumers.push_back((int)m->ops.size());
+        if (op.in2 >= 0) m->vals[op.in2].consumers.push_back((int)m->ops.size());
+        m->ops.push_back(op);
+    }
+    m->out_val = find_val(m, s.output);
+    // Fold `add(dense_or_attention_out, r)` into the producer's epilogue when
+    // the product has no other consumer and no activation.
+    for (size_t i = 0; i < m->ops.size(); i++) {
+        Op& a = m->ops[i];
+        if (a.kind != OP_ADD) continue;
+        for (int side = 0; side < 2; side++) {
+            int pv = side == 0 ? a.in : a.in2;
+            int rv = side == 0 ? a.in2 : a.in;
+            int pi = m->vals[pv].producer;
+            if (pi < 0) continue;
+            Op& p = m->ops[pi];
+            if (!(p.kind == OP_DENSE && p.act == 0) && p.kind != OP_ATTN) continue;
+            if (m->vals[pv].consumers.size() != 1 || pv == m->out_val) continue;
+            if (m->vals[rv].producer >= pi) continue;  // residual must exist already
+            if (pv == rv) continue;
+            p.out = a.out;
+            p.fused_res = rv;
+            m->vals[pv].materialized = false;
+            m->vals[a.out].producer = pi;
+            a.skip = true;
+            break;
+        }
+    }
+    // Dropout shares its input's storage (identity: no training-time mask
+    // in this backend; see DESIGN notes on dropout).
+    for (auto& op : m->ops)
+        if (op.kind == OP_DROPOUT) m->vals[op.out].alias_of = op.in;
+    return true;
+}
+
+// Which forms each value must be stored in.
+static void decide_storage(ns_model* m) {
+    const bool bf = m->precision == 2;
+    for (size_t vi = 0; vi < m->vals.size(); vi++) {
+        Val& v = m->vals[vi];
+        v.need_f32 = (int)vi == m->out_val || vi == 0;
+        v.need_h16 = false;
+        for (int ci : v.consumers) {
+            const Op& c = m->ops[ci];
+            if (c.skip) {
+                // consumed as the residual of a fused add
+                v.need_f32 = true;
+                continue;
+            }
+            bool gemm_in = (c.kind == OP_DENSE || c.kind == OP_ATTN) && c.in == (int)vi;
+            if (gemm_in && bf) v.need_h16 = true;
+            else v.need_f32 = true;
+            if (c.kind == OP_DENSE || c.kind == OP_ATTN || c.kind == OP_MOE) {
+                if (c.fused_res == (int)vi) v.need_f32 = true;
+            }
+        }
+        // a fused producer's residual operand is read in fp32
+    }
+    for (auto& op : m->ops)
+        if (!op.skip && op.fused_res >= 0) m->vals[op.fused_res].need_f32 = true;
+    // MoE reads its input in fp32 (exact router) and, in bf16 mode, in bf16
+    for (auto& op : m->ops)
+        if (op.kind == OP_MOE) {
+            m->vals[op.in].need_f32 = true;
+            if (bf) m->vals[op.in].need_h16 = true;
+        }
+}
+
+// ---------------------------------------------------------------------------
+// working copies of the weights (GEMM operand dtype / packing)
+// ---------------------------------------------------------------------------
+static void free_working(ns_model* m) {
+    for (size_t i = 0; i < m->wk.size(); i++)
+        if (m->wk_owned[i] && m->wk[i]) cudaFree(m->wk[i]);
+    m->wk.assign(m->spec.weights.size(), nullptr);
+    m->wk_owned.assign(m->spec.weights.size(), false);
+}
+
+static int alloc_working(ns_model* m) {
+    free_working(m);
+    const Spec& s = m->spec;
+    const bool bf = m->precision == 2;
+    const size_t es = bf ? 2 : 4;
+    for (size_t li = 0; li < s.layers.size(); li++) {
+        const LayerSpec& l = s.layers[li];
+        int w0 = -1;
+        for (size_t wi = 0; wi < s.weights.size(); wi++)
+            if (s.weights[wi].layer == (int)li) {
+                w0 = (int)wi;
+                break;
+            }
+        if (w0 < 0) continue;
+        auto own = [&](int wi, size_t count) -> bool {
+            void* p = persist_alloc(count * es);
+            if (!p) return false;
+            m->wk[wi] = p;
+            m->wk_owned[wi] = true;
+            return true;
+        };
+        auto alias_or_own = [&](int wi) -> bool {
+            if (!bf) {
+                m->wk[wi] = m->d_w + s.weights[wi].off;
+                return true;
+            }
+            return own(wi, s.weights[wi].count);
+        };
+        if (l.kind == "dense") {
+            if (!alias_or_own(w0)) return -1;
+        } else if (l.kind == "attention") {
+            long long d = l.geti("dim", 0);
+            if (!own(w0, (size_t)3 * d * d)) return -1;  // packed [D, 3D] q|k|v
+            if (!alias_or_own(w0 + 3)) return -1;        // o
+        } else if (l.kind == "moe") {
+            // router stays fp32 (read from the master blob); experts in the GEMM dtype
+            if (!alias_or_own(w0 + 1)) return -1;
+            if (l.gets("expert", "ffn") != "linear" && !alias_or_own(w0 + 2)) return -1;
+        }
+    }
+    return 0;
+}
+
+// Refresh the working copies from the fp32 master blob.
+static int refresh_working(ns_model* m) {
+    const Spec& s = m->spec;
+    const int dt = m->wdt;
+    for (size_t li = 0; li < s.layers.size(); li++) {
+        const LayerSpec& l = s.layers[li];
+        int w0 = -1;
+        for (size_t wi = 0; wi < s.weights.size(); wi++)
+            if (s.weights[wi].layer == (int)li) {
+                w0 = (int)wi;
+                break;
+            }
+        if (w0 < 0) continue;
+        auto copy = [&](int wi) -> int {
+            if (!m->wk_owned[wi]) return 0;
+            const WeightInfo& w = s.weights[wi];
+            launch_counter() += 1;
+            return pack_weight(m->d_w + w.off, 1, (int)w.count, m->wk[wi], dt, (long long)w.count, 0, m->stream);
+        };
+        if (l.kind == "dense") {
+            if (copy(w0)) return -1;
+        } else if (l.kind == "attention") {
+            int d = (int)l.geti("dim", 0);
+            for (int g = 0; g < 3; g++) {
+                launch_counter() += 1;
+                if (pack_weight(m->d_w + s.weights[w0 + g].off, d, d, m->wk[w0], dt, 3LL * d, g * d, m->stream))
+                    return -1;
+            }
+            if (copy(w0 + 3)) return -1;
+        } else if (l.kind == "moe") {
+            if (copy(w0 + 1)) return -1;
+            if (l.gets("expert", "ffn") != "linear" && copy(w0 + 2)) return -1;
+        }
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// planning
+// ---------------------------------------------------------------------------
+static void free_plan(ns_model* m) {
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void* p : m->plan_allocs) cudaFree(p);
+    m->plan_allocs.clear();
+    for (auto& v : m->vals) {
+        v.f32 = nullptr;
+        v.h16 = nullptr;
+        v.gbuf = nullptr;
+        v.gcur = nullptr;
+    }
+    for (auto& op : m->ops) {
+        op.z = op.dz = op.qkv = op.ctx = op.dqkv = op.dctx = op.dout_w = nullptr;
+        op.dz32 = op.lse = op.dvec = nullptr;
+        moe_release(op);
+    }
+    m->d_in = m->d_labels = m->d_rowloss = m->d_loss = nullptr;
+    m->d_targets = nullptr;
+    m->d_ws = nullptr;
+    m->ws_floats = 0;
+    m->d_scratch = nullptr;
+    m->scratch_bytes = 0;
+    m->mmax = 0;
+    m->train_planned = false;
+}
+
+#define PA(T, n) reinterpret_cast<T*>(plan_alloc(m, sizeof(T) * (size_t)(n)))
+
+static int plan(ns_model* m, int M, bool train) {
+    if (M <= m->mmax && (!train || m->train_planned)) return 0;
+    int want = M > m->mmax ? M : m->mmax;
+    want = (want + 127) / 128 * 128;
+    free_plan(m);
+    m->mmax = want;
+    const size_t R = (size_t)want;
+    const bool bf = m->precision == 2;
+    const size_t es = bf ? 2 : 4;
+    const Spec& s = m->spec;
+    decide_storage(m);
+    m->d_in = PA(float, R * s.in_cols);
+    if (!m->d_in) return fail("device allocation failed");
+    for (size_t vi = 1; vi < m->vals.size(); vi++) {
+        Val& v = m->vals[vi];
+        if (!v.materialized || v.alias_of >= 0) continue;
+        if (v.need_f32) v.f32 = PA(float, R * v.cols);
+        if (v.need_h16) v.h16 = PA(__nv_bfloat16, R * v.cols);
+    }
+    m->vals[0].f32 = m->d_in;
+    for (size_t vi = 1; vi < m->vals.size(); vi++) {
+        Val& v = m->vals[vi];
+        if (v.alias_of >= 0) {
+            int a = v.alias_of;
+            while (m->vals[a].alias_of >= 0) a = m->vals[a].alias_of;
+            v.f32 = m->vals[a].f32;
+            v.h16 = m->vals[a].h16;
+        }
+    }
+    for (auto& op : m->ops) {
+        if (op.skip) continue;
+        const int cols = m->vals[op.self_out].cols;
+        if (op.kind == OP_DENSE) {
+            if (train && op.act) op.z = plan_alloc(m, R * cols * es);
+            if (train) {
+                if (bf) op.dz = plan_alloc(m, R * cols * 2);
+                else if (op.act) op.dz32 = PA(float, R * cols);
+            }
+        } else if (op.kind == OP_ATTN) {
+            const LayerSpec& l = s.layers[op.layer];
+            int d = (int)l.geti("dim", 0), h = (int)l.geti("heads", 1);
+            op.qkv = plan_alloc(m, R * 3 * d * es);
+            op.ctx = plan_alloc(m, R * d * es);
+            op.lse = PA(float, R * h);
+            if (train) {
+                op.dvec = PA(float, R * h);
+                op.dqkv = plan_alloc(m, R * 3 * d * es);
+                op.dctx = plan_alloc(m, R * d * es);
+                if (bf) op.dout_w = plan_alloc(m, R * d * 2);
+            }
+        } else if (op.kind == OP_MOE) {
+            if (moe_plan(m, op, want, train)) return fail("MoE plan failed: " + g_err);
+        }
+    }
+    m->d_rowloss = PA(float, R);
+    m->d_loss = PA(float, 4);
+    if (train) {
+        m->d_labels = PA(float, R * s.out_cols);
+        m->d_targets = PA(int, R);
+        for (size_t vi = 1; vi < m->vals.size(); vi++) {
+            Val& v = m->vals[vi];
+            v.gbuf = PA(float, R * v.cols);
+        }
+        for (auto& op : m->ops)
+            if (op.kind == OP_EMB) {
+                const LayerSpec& l = s.layers[op.layer];
+                size_t b = embedding_bwd_scratch_bytes(want, (int)l.geti("vocab", 1));
+                if (b > m->scratch_bytes) m->scratch_bytes = b;
+            }
+        if (m->scratch_bytes) m->d_scratch = plan_alloc(m, m->scratch_bytes);
+        m->train_planned = true;
+    }
+    for (void* p : m->plan_allocs)
+        if (!p) return fail("device allocation failed");
+    return 0;
+}
+
+// split-K workspace on demand (sized once per plan)
+static int run_gemm(ns_model* m, GemmDesc& d) {
+    if (m->precision == 0) d.engine = kEngineSimt;
+    size_t need = gemm_workspace_floats(d);
+    if (need > m->ws_floats) {
+        cudaStreamSynchronize(m->stream);
+        void* p = plan_alloc(m, need * sizeof(float));
+        if (!p) return fail("workspace allocation failed");
+        m->d_ws = reinterpret_cast<float*>(p);
+        m->ws_floats = need;
+    }
+    d.workspace = m->d_ws;
+    d.workspace_floats = m->ws_floats;
+    launch_counter() += gemm_uses_tensor_cores(d) && need ? 2 : 1;
+    int r = gemm(d, m->stream, m->d_err);
+    if (r) return fail("gemm launch failed (code " + std::to_string(r) + ")");
+    return 0;
+}
+
+static GemmOperand opnd(const void* p, int dt, long long ld, bool mn) {
+    GemmOperand o;
+    o.ptr = p;
+    o.dtype = dt;
+    o.ld = ld;
+    o.mn_major = mn;
+    return o;
+}
+
+// the value's storage in the GEMM operand dtype
+static const void* as_operand(ns_model* m, const Val& v) { return m->wdt == kBF16 ? (const void*)v.h16 : (const void*)v.f32; }
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+static int forward(ns_model* m, int M, bool train) {
+    const Spec& s = m->spec;
+    for (size_t oi = 0; oi < m->ops.size(); oi++) {
+        Op& op = m->ops[oi];
+        if (op.skip) continue;
+        Val& in = m->vals[op.in];
+        Val& out = m->vals[op.out];
+        int rc = 0;
+        switch (op.kind) {
+            case OP_DENSE: {
+                const WeightInfo& w = s.weights[op.widx];
+                GemmDesc d;
+                d.M = M;
+                d.N = w.cols;
+                d.K = w.rows;
+                d.a = opnd(as_operand(m, in), m->wdt, w.rows, false);
+                d.b = opnd(m->wk[op.widx], m->wdt, w.cols, true);
+                d.ep.act = op.act;
+                if (train && op.act) {
+                    d.ep.z = op.z;
+                    d.ep.z_dtype = m->wdt;
+                    d.ep.ld_z = w.cols;
+                }
+                if (op.fused_res >= 0) {
+                    d.ep.add = m->vals[op.fused_res].f32;
+                    d.ep.ld_add = w.cols;
+                }
+                d.ep.c32 = out.f32;
+                d.ep.ld_c32 = w.cols;
+                d.ep.c16 = out.h16;
+                d.ep.ld_c16 = w.cols;
+                rc = run_gemm(m, d);
+                break;
+            }
+            case OP_EMB: {
+                const LayerSpec& l = s.layers[op.layer];
+                const WeightInfo& w = s.weights[op.widx];
+                launch_counter() += 1;
+                rc = embedding_fwd(m->d_w + w.off, in.f32, M, (int)l.geti("vocab", 0), (int)l.geti("dim", 0), out.f32,
+                                   out.h16, m->stream);
+                break;
+            }
+            case OP_ATTN: {
+                const LayerSpec& l = s.layers[op.layer];
+                const int D = (int)l.geti("dim", 0), H = (int)l.geti("heads", 1);
+                int S = (int)l.geti("seq", 0);
+                if (S <= 0) S = M;
+                if (M % S) return fail("attention: rows not a multiple of seq");
+                GemmDesc d;
+                d.M = M;
+                d.N = 3 * D;
+                d.K = D;
+                d.a = opnd(as_operand(m, in), m->wdt, D, false);
+                d.b = opnd(m->wk[op.widx], m->wdt, 3LL * D, true);
+                if (m->wdt == kBF16) {
+                    d.ep.c16 = reinterpret_cast<__nv_bfloat16*>(op.qkv);
+                    d.ep.ld_c16 = 3 * D;
+                } else {
+                    d.ep.c32 = reinterpret_cast<float*>(op.qkv);
+                    d.ep.ld_c32 = 3 * D;
+                }
+                if ((rc = run_gemm(m, d))) break;
+                AttnArgs a;
+                a.B = M / S;
+                a.S = S;
+                a.H = H;
+                a.D = D;
+                a.dh = D / H;
+                a.scale = 1.0f / sqrtf((float)(D / H));
+                a.dtype = m->wdt;
+                a.qkv = op.qkv;
+                a.ld_qkv = 3LL * D;
+                a.ctx = op.ctx;
+                a.ld_ctx = D;
+                a.lse = op.lse;
+                launch_counter() += 1;
+                if ((rc = attention_fwd(a, m->stream))) {
+                    rc = fail("attention launch failed");
+                    break;
+                }
+                GemmDesc o;
+                o.M = M;
+                o.N = D;
+                o.K = D;
+                o.a = opnd(op.ctx, m->wdt, D, false);
+                o.b = opnd(m->wk[op.widx + 3], m->wdt, D, true);
+                if (op.fused_res >= 0) {
+                    o.ep.add = m->vals[op.fused_res].f32;
+                    o.ep.ld_add = D;
+                }
+                o.ep.c32 = out.f32;
+                o.ep.ld_c32 = D;
+                o.ep.c16 = out.h16;
+                o.ep.ld_c16 = D;
+                rc = run_gemm(m, o);
+                break;
+            }
+            case OP_LN:
+                launch_counter() += 1;
+                rc = layernorm_fwd(in.f32, M, in.cols, out.f32, out.h16, m->stream);
+                break;
+            case OP_ADD:
+                launch_counter() += 1;
+                rc = add_f32(in.f32, m->vals[op.in2].f32, (size_t)M * in.cols, out.f32, out.h16, m->stream);
+                break;
+            case OP_ACT:
+                launch_counter() += 1;
+                rc = act_fwd_f32(in.f32, (size_t)M * in.cols, op.act, out.f32, out.h16, m->stream);
+                break;
+            case OP_SOFTMAX:
+                launch_counter() += 1;
+                rc = softmax_rows(in.f32, M, in.cols, out.f32, out.h16, m->stream);
+                break;
+            case OP_DROPOUT:
+                break;
+            case OP_MOE:
+                rc = moe_forward(m, op, M, train);
+                break;
+            default:
+                return fail("operation not supported by this backend: " + s.ops[oi].fn);
+        }
+        if (rc) return rc < 0 && !g_err.empty() ? -1 : fail("kernel launch failed in " + s.ops[oi].out);
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+// Add an existing gradient buffer `src` into value v's running total.
+static int contribute_alias(ns_model* m, Val& v, const float* src, int M) {
+    if (!v.gbuf) return 0;  // input x / non-differentiable
+    if (!v.gcur) {
+        v.gcur = src;
+        return 0;
+    }
+    launch_counter() += 1;
+    int rc = add_f32(v.gcur, src, (size_t)M * v.cols, v.gbuf, nullptr, m->stream);
+    v.gcur = v.gbuf;
+    return rc;
+}
+
+// gradient (fp32) of a value -> GEMM operand dtype buffer
+static const void* grad_operand(ns_model* m, const float* g, void* tmp16, size_t n) {
+    if (m->wdt != kBF16) return g;
+    launch_counter() += 1;
+    f32_to_bf16(g, n, reinterpret_cast<__nv_bfloat16*>(tmp16), m->stream);
+    return tmp16;
+}
+
+static int backward(ns_model* m, int M) {
+    const Spec& s = m->spec;
+    for (int oi = (int)m->ops.size() - 1; oi >= 0; oi--) {
+        Op& op = m->ops[oi];
+        if (op.skip) continue;
+        Val& out = m->vals[op.out];
+        if (!out.gcur) continue;
+        const float* dv = out.gcur;
+        Val& in = m->vals[op.in];
+        int rc = 0;
+        switch (op.kind) {
+            case OP_DENSE: {
+                const WeightInfo& w = s.weights[op.widx];
+                const size_t n = (size_t)M * w.cols;
+                const void* dz;
+                if (op.act) {
+                    launch_counter() += 1;
+                    if (m->wdt == kBF16) {
+                        rc = act_bwd(dv, op.z, kBF16, op.act, nullptr, n, nullptr,
+                                     reinterpret_cast<__nv_bfloat16*>(op.dz), m->stream);
+                        dz = op.dz;
+                    } else {
+                        rc = act_bwd(dv, op.z, kF32, op.act, nullptr, n, op.dz32, nullptr, m->stream);
+                        dz = op.dz32;
+                    }
+                    if (rc) break;
+                } else {
+                    dz = grad_operand(m, dv, op.dz, n);
+                }
+                if (op.fused_res >= 0 && (rc = contribute_alias(m, m->vals[op.fused_res], dv, M))) break;
+                GemmDesc gw;
+                gw.M = w.rows;
+                gw.N = w.cols;
+                gw.K = M;
+                gw.a = opnd(as_operand(m, in), m->wdt, w.rows, true);
+                gw.b = opnd(dz, m->wdt, w.cols, true);
+                gw.ep.c32 = m->d_g + w.off;
+                gw.ep.ld_c32 = w.cols;
+                if ((rc = run_gemm(m, gw))) break;
+                if (in.gbuf) {
+                    GemmDesc gx;
+                    gx.M = M;
+                    gx.N = w.rows;
+                    gx.K = w.cols;
+                    gx.a = opnd(dz, m->wdt, w.cols, false);
+                    gx.b = opnd(m->wk[op.widx], m->wdt, w.cols, false);
+                    if (in.gcur) {
+                        gx.ep.add = in.gcur;
+                        gx.ep.ld_add = w.rows;
+                    }
+                    gx.ep.c32 = in.gbuf;
+                    gx.ep.ld_c32 = w.rows;
+                    if ((rc = run_gemm(m, gx))) break;
+                    in.gcur = in.gbuf;
+                }
+                break;
+            }
+            case OP_EMB: {
+                const LayerSpec& l = s.layers[op.layer];
+                const WeightInfo& w = s.weights[op.widx];
+                launch_counter() += 5;
+                rc = embedding_bwd(dv, in.f32, M, (int)l.geti("vocab", 0), (int)l.geti("dim", 0), m->d_g + w.off,
+                                   m->d_scratch, m->stream);
+                break;
+            }
+            case OP_ATTN: {
+                const LayerSpec& l = s.layers[op.layer];
+                const int D = (int)l.geti("dim", 0), H = (int)l.geti("heads", 1);
+                int S = (int)l.geti("seq", 0);
+                if (S <= 0) S = M;
+                const void* dout = grad_operand(m, dv, op.dout_w, (size_t)M * D);
+                if (op.fused_res >= 0 && (rc = contribute_alias(m, m->vals[op.fused_res], dv, M))) break;
+                const WeightInfo& wo = s.weights[op.widx + 3];
+                GemmDesc go;  // dWo = ctx^T dout
+                go.M = D;
+                go.N = D;
+                go.K = M;
+                go.a = opnd(op.ctx, m->wdt, D, true);
+                go.b = opnd(dout, m->wdt, D, true);
+                go.ep.c32 = m->d_g + wo.off;
+                go.ep.ld_c32 = D;
+                if ((rc = run_gemm(m, go))) break;
+                GemmDesc gc;  // dctx = dout Wo^T
+                gc.M = M;
+                gc.N = D;
+                gc.K = D;
+                gc.a = opnd(dout, m->wdt, D, false);
+                gc.b = opnd(m->wk[op.widx + 3], m->wdt, D, false);
+                if (m->wdt == kBF16) {
+                    gc.ep.c16 = reinterpret_cast<__nv_bfloat16*>(op.dctx);
+                    gc.ep.ld_c16 = D;
+                } else {
+                    gc.ep.c32 = reinterpret_cast<float*>(op.dctx);
+                    gc.ep.ld_c32 = D;
+                }
+                if ((rc = run_gemm(m, gc))) break;
+                AttnArgs a;
+                a.B = M / S;
+                a.S = S;
+                a.H = H;
+                a.D = D;
+                a.dh = D / H;
+                a.scale = 1.0f / sqrtf((float)(D / H));
+                a.dtype = m->wdt;
+                a.qkv = op.qkv;
+                a.ld_qkv = 3LL * D;
+                a.ctx = op.ctx;
+                a.ld_ctx = D;
+                a.lse = op.lse;
+                a.dctx = op.dctx;
+                a.ld_dctx = D;
+                a.dqkv = op.dqkv;
+                a.ld_dqkv = 3LL * D;
+                a.dvec = op.dvec;
+                launch_counter() += 2;
+                if ((rc = attention_bwd(a, m->stream))) {
+                    rc = fail("attention backward launch failed");
+                    break;
+                }
+                const size_t es = m->wdt == kBF16 ? 2 : 4;
+                for (int g = 0; g < 3; g++) {  // dWq, dWk, dWv = x^T dQ|dK|dV
+                    const WeightInfo& wq = s.weights[op.widx + g];
+                    GemmDesc gq;
+                    gq.M = D;
+                    gq.N = D;
+                    gq.K = M;
+                    gq.a = opnd(as_operand(m, in), m->wdt, D, true);
+                    gq.b = opnd(reinterpret_cast<const char*>(op.dqkv) + (size_t)g * D * es, m->wdt, 3LL * D, true);
+                    gq.ep.c32 = m->d_g + wq.off;
+                    gq.ep.ld_c32 = D;
+                    if ((rc = run_gemm(m, gq))) break;
+                }
+                if (rc) break;
+                if (in.gbuf) {
+                    GemmDesc gx;  // dx = dQKV [Wq|Wk|Wv]^T (+ running total)
+                    gx.M = M;
+                    gx.N = D;
+                    gx.K = 3 * D;
+                    gx.a = opnd(op.dqkv, m->wdt, 3LL * D, false);
+                    gx.b = opnd(m->wk[op.widx], m->wdt, 3LL * D, false);
+                    if (in.gcur) {
+                        gx.ep.add = in.gcur;
+                        gx.ep.ld_add = D;
+                    }
+                    gx.ep.c32 = in.gbuf;
+                    gx.ep.ld_c32 = D;
+                    if ((rc = run_gemm(m, gx))) break;
+                    in.gcur = in.gbuf;
+                }
+                break;
+            }
+            case OP_LN:
+                if (!in.gbuf) break;
+                launch_counter() += 1;
+                rc = layernorm_bwd(dv, in.f32, in.gcur, M, in.cols, in.gbuf, nullptr, m->stream);
+                in.gcur = in.gbuf;
+                break;
+            case OP_ADD:
+                if ((rc = contribute_alias(m, in, dv, M))) break;
+                rc = contribute_alias(m, m->vals[op.in2], dv, M);
+                break;
+            case OP_ACT:
+                if (!in.gbuf) break;
+                launch_counter() += 1;
+                rc = act_bwd(dv, in.f32, kF32, op.act, in.gcur, (size_t)M * in.cols, in.gbuf, nullptr, m->stream);
+                in.gcur = in.gbuf;
+                break;
+            case OP_SOFTMAX:  // the reference's softmax gradient is a pass-through (code 0)
+            case OP_DROPOUT:
+                rc = contribute_alias(m, in, dv, M);
+                break;
+            case OP_MOE:
+                rc = moe_backward(m, op, M);
+                break;
+            default:
+                return fail("backward not supported for " + s.ops[oi].fn);
+        }
+        if (rc) return -1;
+    }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// loss + optimizer
+// ---------------------------------------------------------------------------
+static float lr_schedule(const ns_model* m, long long step) {
+    const Spec& s = m->spec;
+    if (s.schedule != "cosine") return 1.0f;
+    const long long warm = (long long)s.schedv("warmup", 100), total = (long long)s.schedv("total", 10000);
+    const float minf = (float)s.schedv("min", 0.05);
+    if (warm <= 0) return 1.0f;
+    if (step < warm) return (float)step / (float)warm;
+    const long long end = total > warm ? total : warm + 1;
+    const long long st = step >= end ? end : step;
+    const float t = (float)(st - warm) / (float)(end - warm);
+    return minf + 0.5f * (1.0f - minf) * (1.0f + cosf(3.14159265f * t));
+}
+
+static int loss_and_seed(ns_model* m, int M, const float* labels, const int* targets, bool want_grad) {
+    Val& o = m->vals[m->out_val];
+    const int C = o.cols;
+    const float denom = (float)M * (float)m->world;
+    float* d32 = want_grad ? o.gbuf : nullptr;
+    launch_counter() += 1;
+    int rc;
+    if (m->spec.loss == "mse") {
+        if (!labels) return fail("mse loss needs dense targets");
+        rc = mse_fwd_bwd(o.f32, labels, M, C, want_grad ? (float)M * C * m->world : 1.f, m->d_rowloss, d32, nullptr,
+                         m->stream);
+    } else {
+        rc = cross_entropy_fwd_bwd(o.f32, labels, targets, M, C, denom, m->d_rowloss, d32, nullptr, m->stream);
+    }
+    if (rc) return fail("loss kernel launch failed");
+    if (want_grad) o.gcur = o.gbuf;
+    return 0;
+}
+
+struct AdamTensorLocal {
+    float* w;
+    const float* g;
+    float* m;
+    float* v;
+    long long n;
+    float b1t, b2t;
+};
+
+static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* out);
+
+static int optimizer_step(ns_model* m, float lr) {
+    const Spec& s = m->spec;
+    const std::string& mode = s.optimizer;
+    const bool ref = mode == "reference";
+    float b1, b2, eps, dec, omb1, omb2;
+    if (ref) {
+        b1 = 0.9f; b2 = 0.999f; eps = 1e-8f; dec = 0.01f; omb1 = 0.1f; omb2 = 0.001f;
+    } else {
+        double B1 = s.optv("beta1", 0.9), B2 = s.optv("beta2", 0.999);
+        b1 = (float)B1; b2 = (float)B2;
+        eps = (float)s.optv("eps", 1e-8);
+        dec = (float)s.optv("decay", 0.01);
+        omb1 = (float)(1.0 - B1);
+        omb2 = (float)(1.0 - B2);
+    }
+    std::vector<AdamTensor> at;
+    long long maxn = 0;
+    for (size_t wi = 0; wi < s.weights.size(); wi++) {
+        const WeightInfo& w = s.weights[wi];
+        const bool matrix = w.rows > 1 && w.cols > 1;
+        const int mn = w.rows < w.cols ? w.rows : w.cols;
+        float* W = m->d_w + w.off;
+        float* G = m->d_g + w.off;
+        if ((ref || mode == "muon") && matrix && mn >= 8) {
+            const float mu = ref ? 0.95f : (float)s.optv("momentum", 0.95);
+            const float mdec = ref ? 0.01f : (float)s.optv("decay", 0.01);
+            launch_counter() += 1;
+            muon_momentum(m->d_m + w.off, G, (long long)w.count, mu, m->stream);
+            const float le = lr * sqrtf((float)mn);
+            if (ref) {
+                // reference: MGS in place on the momentum, then reset it
+                launch_counter() += 2;
+                mgs_orthonormalize(m->d_m + w.off, w.rows, w.cols, m->stream);
+                muon_apply(W, m->d_m + w.off, m->d_m + w.off, (long long)w.count, le, mdec * lr, 1, m->stream);
+            } else {
+                if (newton_schulz(m, m->d_m + w.off, w.rows, w.cols, (int)s.optv("steps", 5), m->d_o)) return -1;
+                launch_counter() += 1;
+                muon_apply(W, m->d_o, nullptr, (long long)w.count, le, mdec * lr, 0, m->stream);
+            }
+        } else {
+            long long t = ++m->adam_t[wi];
+            AdamTensor a;
+            a.w = W;
+            a.g = G;
+            a.m = m->d_m + w.off;
+            a.v = m->d_v + w.off;
+            a.n = (long long)w.count;
+            a.b1t = 1.f - powf(b1, (float)t);
+            a.b2t = 1.f - powf(b2, (float)t);
+            at.push_back(a);
+            if (a.n > maxn) maxn = a.n;
+        }
+    }
+    if (!at.empty()) {
+        if ((int)at.size() > m->adam_cap) {
+            if (m->d_adam) cudaFree(m->d_adam);
+            if (m->h_adam) cudaFreeHost(m->h_adam);
+            m->adam_cap = (int)at.size();
+            if (cudaMalloc(&m->d_adam, sizeof(AdamTensor) * at.size()) != cudaSuccess) return fail("alloc failed");
+            if (cudaMallocHost(&m->h_adam, sizeof(AdamTensor) * at.size()) != cudaSuccess) return fail("alloc failed");
+        }
+        cudaStreamSynchronize(m->stream);  // the pinned staging may still feed the previous copy
+        memcpy(m->h_adam, at.data(), sizeof(AdamTensor) * at.size());
+        cudaMemcpyAsync(m->d_adam, m->h_adam, sizeof(AdamTensor) * at.size(), cudaMemcpyHostToDevice, m->stream);
+        AdamHyper h{lr, b1, b2, omb1, omb2, eps, dec};
+        launch_counter() += 1;
+        if (adamw_multi(reinterpret_cast<AdamTensor*>(m->d_adam), (int)at.size(), maxn, h, m->stream))
+            return fail("adamw launch failed");
+    }
+    return refresh_working(m);
+}
+
+// X (r x c, fp32) -> out = NS5(X / ||X||). Uses m->d_ns as scratch.
+static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* out) {
+    const bool tr = r > c;
+    const int R = tr ? c : r;  // Gram size
+    float* A = m->d_ns;
+    float* B = A + (size_t)R * R;
+    float* Y0 = B + (size_t)R * R;
+    float* Y1 = Y0 + (size_t)r * c;
+    float* part = Y1 + (size_t)r * c;
+    launch_counter() += 2;
+    frob_normalize(X, (long long)r * c, 1e-7f, Y0, part, m->stream);
+    const float a = 3.4445f, b = -4.7750f, cc = 2.0315f;
+    float* cur = Y0;
+    float* nxt = Y1;
+    for (int it = 0; it < steps; it++) {
+        GemmDesc g1;  // A = Y Y^T  (or Y^T Y)
+        g1.M = R;
+        g1.N = R;
+        g1.K = tr ? r : c;
+        g1.a = opnd(cur, kF32, c, tr);
+        g1.b = opnd(cur, kF32, c, tr);
+        g1.ep.c32 = A;
+        g1.ep.ld_c32 = R;
+        if (run_gemm(m, g1)) return -1;
+        GemmDesc g2;  // B = b A + c A A (A symmetric)
+        g2.M = R;
+        g2.N = R;
+        g2.K = R;
+        g2.a = opnd(A, kF32, R, false);
+        g2.b = opnd(A, kF32, R, false);
+        g2.ep.alpha = cc;
+        g2.ep.add = A;
+        g2.ep.ld_add = R;
+        g2.ep.add_scale = b;
+        g2.ep.c32 = B;
+        g2.ep.ld_c32 = R;
+        if (run_gemm(m, g2)) return -1;
+        GemmDesc g3;  // Y' = a Y + B Y   (or a Y + Y B)
+        g3.M = r;
+        g3.N = c;
+        if (!tr) {
+            g3.K = R;
+            g3.a = opnd(B, kF32, R, false);
+            g3.b = opnd(cur, kF32, c, true);
+        } else {
+            g3.K = R;
+            g3.a = opnd(cur, kF32, c, false);
+            g3.b = opnd(B, kF32, R, false);
+        }
+        g3.ep.add = cur;
+        g3.ep.ld_add = c;
+        g3.ep.add_scale = a;
+        g3.ep.c32 = nxt;
+        g3.ep.ld_c32 = c;
+        if (run_gemm(m, g3)) return -1;
+        std::swap(cur, nxt);
+    }
+    cudaMemcpyAsync(out, cur, sizeof(float) * (size_t)r * c, cudaMemcpyDeviceToDevice, m->stream);
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// synchronisation with error / timeout checks
+// ---------------------------------------------------------------------------
+static int finish(ns_model* m) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t q = cudaStreamQuery(m->stream);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) return fail(std::string("CUDA error: ") + cudaGetErrorString(q));
+        if (m->comm) {
+            ncclResult_t ar;
+            nccl().CommGetAsyncError(m->comm, &ar);
+            if (ar != ncclSuccess && ar != ncclInProgress) {
+                nccl().CommAbort(m->comm);
+                m->comm = nullptr;
+                return fail(std::string("NCCL error: ") + nccl().GetErrorString(ar));
+            }
+            auto el = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+            if (el.count() > m->timeout_ms) {
+                nccl().CommAbort(m->comm);
+                m->comm = nullptr;
+                return fail("collective timed out");
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        } else {
+            cudaError_t e = cudaStreamSynchronize(m->stream);
+            if (e != cudaSuccess) return fail(std::string("CUDA error: ") + cudaGetErrorString(e));
+            break;
+        }
+    }
+    int herr = 0;
+    cudaMemcpy(&herr, m->d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (herr) {
+        cudaMemset(m->d_err, 0, sizeof(int));
+        return fail("device pipeline wait timed out (code " + std::to_string(herr) + ")");
+    }
+    return 0;
+}
+
+static void sync_host(const ns_model* m) {
+    if (!m->host_dirty) return;
+    cudaMemcpy(m->h_w.data(), m->d_w, sizeof(float) * m->spec.total, cudaMemcpyDeviceToHost);
+    m->host_dirty = false;
+}
+
+static int upload_weights(ns_model* m) {
+    if (cudaMemcpy(m->d_w, m->h_w.data(), sizeof(float) * m->spec.total, cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail("weight upload failed");
+    if (m->d_active && !m->moe_active.empty())
+        cudaMemcpy(m->d_active, m->moe_active.data(), m->moe_active.size(), cudaMemcpyHostToDevice);
+    if (refresh_working(m)) return -1;
+    return finish(m);
+}
+
+// ---------------------------------------------------------------------------
+// public entry points
+// ---------------------------------------------------------------------------
+namespace {
+struct SpecCache {
+    std::mutex mu;
+    std::map<std::string, std::unique_ptr<Spec>> specs;
+};
+SpecCache& spec_cache() {
+    static SpecCache c;
+    return c;
+}
+const Spec* cached_spec(const char* text) {
+    if (!text) return nullptr;
+    SpecCache& c = spec_cache();
+    std::lock_guard<std::mutex> g(c.mu);
+    auto it = c.specs.find(text);
+    if (it != c.specs.end()) return it->second.get();
+    std::unique_ptr<Spec> s(new Spec());
+    std::string err;
+    if (!parse_spec(text, *s, err)) {
+        g_err = err;
+        return nullptr;
+    }
+    const Spec* r = s.get();
+    c.specs[text] = std::move(s);
+    return r;
+}
+int env_precision(int def) {
+    const char* e = getenv("NS_B200_PRECISION");
+    if (!e) return def;
+    std::string v(e);
+    if (v == "fp32") return 0;
+    if (v == "tf32") return 1;
+    if (v == "bf16") return 2;
+    return def;
+}
+}  // namespace
+
+extern "C" {
+
+const char* nsb_last_error(void) { return g_err.c_str(); }
+const char* nsb_version(void) { return "ns-b200 0.1 (ABI " NS_RUNTIME_VERSION ")"; }
+
+size_t nsb_spec_weight_count(const char* spec) {
+    const Spec* s = cached_spec(spec);
+    return s ? s->total : 0;
+}
+
+const ns_weight_layout* nsb_spec_layout(const char* spec) {
+    const Spec* s = cached_spec(spec);
+    return s ? &s->layout : nullptr;
+}
+
+ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_floats) {
+    g_err.clear();
+    if (!spec || !weights) {
+        fail("null spec or weights");
+        return nullptr;
+    }
+    ns_model* m = new ns_model();
+    std::string err;
+    if (!parse_spec(spec, m->spec, err)) {
+        delete m;
+        fail("spec: " + err);
+        return nullptr;
+    }
+    if (num_floats != m->spec.total) {
+        delete m;
+        fail("weight count mismatch");
+        return nullptr;
+    }
+    if (!build_graph(m, err)) {
+        delete m;
+        fail("spec: " + err);
+        return nullptr;
+    }
+    m->precision = env_precision(m->spec.precision);
+    m->wdt = m->precision == 2 ? kBF16 : kF32;
+    cudaGetDevice(&m->device);
+    bool ok = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
+    const size_t n = m->spec.total;
+    ok = ok && (m->d_err = (int*)persist_alloc(sizeof(int)));
+    ok = ok && (m->d_w = (float*)persist_alloc(sizeof(float) * n));
+    ok = ok && (m->d_g = (float*)persist_alloc(sizeof(float) * (n + 1)));
+    ok = ok && (m->d_m = (float*)persist_alloc(sizeof(float) * n));
+    ok = ok && (m->d_v = (float*)persist_alloc(sizeof(float) * n));
+    ok = ok && cudaMallocHost(&m->h_loss, 16) == cudaSuccess;
+    size_t maxmat = 0, maxgram = 0;
+    for (auto& w : m->spec.weights) {
+        if (w.count > maxmat) maxmat = w.count;
+        size_t g = (size_t)(w.rows < w.cols ? w.rows : w.cols);
+        if (g * g > maxgram) maxgram = g * g;
+    }
+    ok = ok && (m->d_o = (float*)persist_alloc(sizeof(float) * (maxmat + 1)));
+    m->ns_floats = 2 * maxgram + 2 * maxmat + 1024;
+    if (m->spec.optimizer == "muon") ok = ok && (m->d_ns = (float*)persist_alloc(sizeof(float) * m->ns_floats));
+    m->adam_t.assign(m->spec.weights.size(), 0);
+    m->h_w.assign(weights, weights + n);
+    for (size_t li = 0; li < m->spec.layers.size(); li++)
+        if (m->spec.layers[li].kind == "moe") {
+            m->moe_layer = (int)li;
+            int E = (int)m->spec.layers[li].geti("experts", 1);
+            int K0 = (int)m->spec.layers[li].geti("initial", E);
+            if (K0 <= 0 || K0 > E) K0 = E;
+            m->moe_active.assign(E, 0);
+            for (int e = 0; e < K0; e++) m->moe_active[e] = 1;
+            m->moe_active_count = K0;
+            ok = ok && (m->d_active = (uint8_t*)persist_alloc(E));
+            break;
+        }
+    ok = ok && alloc_working(m) == 0;
+    if (!ok || upload_weights(m)) {
+        std::string e = g_err.empty() ? "device allocation failed" : g_err;
+        nsb_free(m);
+        fail(e);
+        return nullptr;
+    }
+    return m;
+}
+
+void nsb_free(ns_model* m) {
+    if (!m) return;
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    free_plan(m);
+    free_working(m);
+    for (void* p : {(void*)m->d_err, (void*)m->d_w, (void*)m->d_g, (void*)m->d_m, (void*)m->d_v, (void*)m->d_o,
+                    (void*)m->d_ns, (void*)m->d_active, m->d_adam})
+        if (p) cudaFree(p);
+    if (m->h_adam) cudaFreeHost(m->h_adam);
+    if (m->h_loss) cudaFreeHost(m->h_loss);
+    if (m->comm) nccl().CommDestroy(m->comm);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+size_t nsb_model_output_numel(const ns_model* m, size_t input_numel) {
+    if (!m) return 0;
+    return (input_numel / (size_t)m->spec.in_cols) * (size_t)m->spec.out_cols;
+}
+
+size_t nsb_model_weight_count(const ns_model* m) { return m ? m->spec.total : 0; }
+
+int nsb_model_get_weights(const ns_model* m, float* out, size_t n) {
+    if (!m || !out || n != m->spec.total) return -1;
+    sync_host(m);
+    memcpy(out, m->h_w.data(), n * sizeof(float));
+    return 0;
+}
+
+int nsb_set_precision(ns_model* m, int mode) {
+    if (!m || mode < 0 || mode > 2) return -1;
+    if (mode == m->precision) return 0;
+    cudaStreamSynchronize(m->stream);
+    free_plan(m);
+    m->precision = mode;
+    m->wdt = mode == 2 ? kBF16 : kF32;
+    if (alloc_working(m) || refresh_working(m)) return -1;
+    return finish(m);
+}
+
+int nsb_get_precision(const ns_model* m) { return m ? m->precision : -1; }
+
+long long nsb_last_launch_count(const ns_model* m) { return m ? m->launches : 0; }
+
+static int rows_of(const ns_model* m, size_t input_numel) {
+    return (int)(input_numel / (size_t)m->spec.in_cols);
+}
+
+int nsb_eval_infer_device(ns_model* m, const float* d_input, float* d_output, size_t input_numel, void* stream) {
+    if (!m) return -1;
+    g_err.clear();
+    const long long l0 = launch_counter();
+    const int M = rows_of(m, input_numel);
+    if (M <= 0) return 0;
+    if (plan(m, M, false)) return -1;
+    cudaStream_t us = stream ? (cudaStream_t)stream : m->stream;
+    cudaEvent_t ev;
+    if (us != m->stream) {
+        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEventRecord(ev, us);
+        cudaStreamWaitEvent(m->stream, ev, 0);
+    }
+    cudaMemcpyAsync(m->d_in, d_input, sizeof(float) * (size_t)M * m->spec.in_cols, cudaMemcpyDeviceToDevice,
+                    m->stream);
+    int rc = forward(m, M, false);
+    if (!rc)
+        cudaMemcpyAsync(d_output, m->vals[m->out_val].f32, sizeof(float) * (size_t)M * m->spec.out_cols,
+                        cudaMemcpyDeviceToDevice, m->stream);
+    if (us != m->stream) {
+        cudaEventRecord(ev, m->stream);
+        cudaStreamWaitEvent(us, ev, 0);
+        cudaEventDestroy(ev);
+    }
+    m->launches = launch_counter() - l0;
+    return rc;
+}
+
+int nsb_eval_infer(ns_model* m, const float* input, float* output, size_t input_numel) {
+    if (!m) return -1;
+    g_err.clear();
+    const long long l0 = launch_counter();
+    const int M = rows_of(m, input_numel);
+    if (M <= 0) return 0;
+    if (!input || !output) return fail("null input/output");
+    if (plan(m, M, false)) return -1;
+    cudaMemcpyAsync(m->d_in, input, sizeof(float) * (size_t)M * m->spec.in_cols, cudaMemcpyHostToDevice, m->stream);
+    if (forward(m, M, false)) {
+        finish(m);
+        return -1;
+    }
+    cudaMemcpyAsync(output, m->vals[m->out_val].f32, sizeof(float) * (size_t)M * m->spec.out_cols,
+                    cudaMemcpyDeviceToHost, m->stream);
+    m->launches = launch_counter() - l0;
+    return finish(m);
+}
+
+static int train_core(ns_model* m, int M, const float* d_labels, const int* d_targets, float* loss_out, float lr,
+                      bool train) {
+    if (forward(m, M, train)) return -1;
+    if (loss_and_seed(m, M, d_labels, d_targets, train)) return -1;
+    launch_counter() += 1;
+    const float scale = 1.0f / ((float)M * (m->spec.loss == "mse" ? (float)m->spec.out_cols : 1.f));
+    if (train) {
+        for (auto& v : m->vals) v.gcur = nullptr;
+        Val& o = m->vals[m->out_val];
+        o.gcur = o.gbuf;
+        if (backward(m, M)) return -1;
+        // the loss sum rides at the end of the gradient blob
+        reduce_sum(m->d_rowloss, M, 1.0f, m->d_g + m->spec.total, m->stream);
+        if (m->comm && m->world > 1) {
+            launch_counter() += 1;
+            ncclResult_t r = nccl().AllReduce(m->d_g, m->d_g, m->spec.total + 1, ncclFloat, ncclSum, m->comm, m->stream);
+            if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("allreduce: ") + nccl().GetErrorString(r));
+        }
+        if (optimizer_step(m, lr)) return -1;
+        m->host_dirty = true;
+        const float gscale = 1.0f / ((float)M * (float)m->world *
+                                     (m->spec.loss == "mse" ? (float)m->spec.out_cols : 1.f));
+        launch_counter() += 1;
+        reduce_sum(m->d_g + m->spec.total, 1, gscale, m->d_loss, m->stream);
+    } else {
+        reduce_sum(m->d_rowloss, M, scale, m->d_loss, m->stream);
+    }
+    if (loss_out) cudaMemcpyAsync(m->h_loss, m->d_loss, sizeof(float), cudaMemcpyDeviceToHost, m->stream);
+    return 0;
+}
+
+static int train_entry(ns_model* m, const float* input, const float* labels, const int* targets, size_t input_numel,
+                       float* loss_out, float lr, bool train, bool device_ptrs, void* stream) {
+    if (!m) return -1;
+    g_err.clear();
+    const long long l0 = launch_counter();
+    const int M = rows_of(m, input_numel);
+    if (M <= 0) return fail("empty batch");
+    if (!input || (!labels && !targets)) return fail("null input/labels");
+    if (plan(m, M, true)) return -1;
+    cudaMemcpyKind k = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    cudaStream_t us = stream ? (cudaStream_t)stream : m->stream;
+    if (device_ptrs && us != m->stream) cudaStreamSynchronize(us);
+    cudaMemcpyAsync(m->d_in, input, sizeof(float) * (size_t)M * m->spec.in_cols, k, m->stream);
+    const float* dl = nullptr;
+    const int* dt = nullptr;
+    if (labels) {
+        cudaMemcpyAsync(m->d_labels, labels, sizeof(float) * (size_t)M * m->spec.out_cols, k, m->stream);
+        dl = m->d_labels;
+    } else {
+        cudaMemcpyAsync(m->d_targets, targets, sizeof(int) * (size_t)M, k, m->stream);
+        dt = m->d_targets;
+    }
+    float lr_eff = lr;
+    if (train) {
+        long long st = m->lr_step;
+        if (st < 9223372036854775807LL) m->lr_step = st + 1;
+        lr_eff = lr * lr_schedule(m, st);
+    }
+    int rc = train_core(m, M, dl, dt, loss_out, lr_eff, train);
+    m->launches = launch_counter() - l0;
+    int rf = finish(m);
+    if (rc || rf) return -1;
+    if (loss_out) *loss_out = *m->h_loss;
+    return 0;
+}
+
+int nsb_runtime_train_step(ns_model* m, const float* input, const float* labels, size_t input_numel, float* loss_out,
+                           float lr) {
+    return train_entry(m, input, labels, nullptr, input_numel, loss_out, lr, true, false, nullptr);
+}
+
+int nsb_runtime_train_step_idx(ns_model* m, const float* input, const int* targets, size_t input_numel,
+                               float* loss_out, float lr) {
+    return train_entry(m, input, nullptr, targets, input_numel, loss_out, lr, true, false, nullptr);
+}
+
+int nsb_train_step_device(ns_model* m, const float* d_input, const float* d_labels, const int* d_targets,
+                          size_t input_numel, float* loss_out, float lr, void* stream) {
+    return train_entry(m, d_input, d_labels, d_targets, input_numel, loss_out, lr, true, true, stream);
+}
+
+int nsb_objective_loss(ns_model* m, const float* input, const float* labels, size_t input_numel, float* loss_out) {
+    return train_entry(m, input, labels, nullptr, input_numel, loss_out, 0.f, false, false, nullptr);
+}
+
+// ---- checkpoints (reference codegen.cpp:2501-2557) --------------------------
+int nsb_save_checkpoint(const ns_model* m, const char* path) {
+    if (!m || !path) return -1;
+    sync_host(m);
+    FILE* fp = fopen(path, "wb");
+    if (!fp) return -1;
+    const unsigned magic = 0x4E534D32u;
+    const size_t n = m->spec.total;
+    bool ok = fwrite(&magic, sizeof(magic), 1, fp) == 1 && fwrite(&n, sizeof(n), 1, fp) == 1 &&
+              fwrite(m->h_w.data(), sizeof(float), n, fp) == n;
+    if (ok && m->moe_layer >= 0) {
+        const unsigned nl = 1u;
+        const size_t cap = m->moe_active.size();
+        ok = fwrite(&nl, sizeof(nl), 1, fp) == 1 && fwrite(&cap, sizeof(cap), 1, fp) == 1 &&
+             fwrite(m->moe_active.data(), 1, cap, fp) == cap;
+    }
+    fclose(fp);
+    return ok ? 0 : -1;
+}
+
+int nsb_load_checkpoint(ns_model* m, const char* path) {
+    if (!m || !path) return -1;
+    FILE* fp = fopen(path, "rb");
+    if (!fp) return -1;
+    unsigned magic = 0;
+    size_t n = 0;
+    std::vector<float> w(m->spec.total);
+    bool ok = fread(&magic, sizeof(magic), 1, fp) == 1 && fread(&n, sizeof(n), 1, fp) == 1 &&
+              (magic == 0x4E534D31u || magic == 0x4E534D32u) && n == m->spec.total &&
+              fread(w.data(), sizeof(float), n, fp) == n;
+    std::vector<uint8_t> mask = m->moe_active;
+    if (ok && m->moe_layer >= 0) {
+        if (magic == 0x4E534D32u) {
+            unsigned nl = 0;
+            size_t cap = 0;
+            ok = fread(&nl, sizeof(nl), 1, fp) == 1 && fread(&cap, sizeof(cap), 1, fp) == 1 && nl == 1u &&
+                 cap == mask.size() && fread(mask.data(), 1, cap, fp) == cap;
+        } else {
+            mask.assign(mask.size(), 1);
+        }
+    }
+    fclose(fp);
+    if (!ok) return -1;
+    cudaStreamSynchronize(m->stream);
+    m->h_w = w;
+    m->host_dirty = false;
+    if (m->moe_layer >= 0) {
+        m->moe_active = mask;
+        m->moe_active_count = 0;
+        for (uint8_t a : mask) m->moe_active_count += a;
+    }
+    return upload_weights(m) ? -1 : 0;
+}
+
+// ---- MoE expert lifecycle (reference CPU emit, codegen.cpp:2559-2625) -------
+struct MoeGeom {
+    size_t cap, dim, ffn, off_g, off_e1, off_e2;
+    bool linear;
+};
+static bool moe_geom(const ns_model* m, MoeGeom& g) {
+    if (m->moe_layer < 0) return false;
+    const LayerSpec& l = m->spec.layers[m->moe_layer];
+    g.cap = (size_t)l.geti("experts", 1);
+    g.dim = (size_t)l.geti("dim", 1);
+    g.linear = l.gets("expert", "ffn") == "linear";
+    g.ffn = g.linear ? g.dim : (size_t)l.geti("ffn", 4 * (long long)g.dim);
+    for (auto& w : m->spec.weights) {
+        if (w.layer != m->moe_layer) continue;
+        if (w.name == l.name + "_g_w") g.off_g = w.off;
+        else if (w.name == l.name + "_e1_w") g.off_e1 = w.off;
+        else if (w.name == l.name + "_e2_w") g.off_e2 = w.off;
+    }
+    return true;
+}
+
+size_t nsb_expert_count(const ns_model* m) { return m ? m->moe_active_count : 0; }
+
+size_t nsb_expert_kill(ns_model* m, int k) {
+    if (!m || m->moe_layer < 0) return m ? m->moe_active_count : 0;
+    if (k < 0 || k >= (int)m->moe_active.size() || !m->moe_active[k]) return m->moe_active_count;
+    m->moe_active[k] = 0;
+    m->moe_active_count--;
+    cudaMemcpy(m->d_active, m->moe_active.data(), m->moe_active.size(), cudaMemcpyHostToDevice);
+    return m->moe_active_count;
+}
+
+size_t nsb_expert_merge(ns_model* m, int a, int b) {
+    MoeGeom g;
+    if (!m || !moe_geom(m, g)) return m ? m->moe_active_count : 0;
+    const int cap = (int)g.cap;
+    if (a < 0 || b < 0 || a == b || a >= cap || b >= cap || !m->moe_active[a] || !m->moe_active[b])
+        return m->moe_active_count;
+    sync_host(m);
+    float* w = m->h_w.data();
+    for (size_t k = 0; k < g.dim; k++)
+        w[g.off_g + k * g.cap + a] = 0.5f * (w[g.off_g + k * g.cap + a] + w[g.off_g + k * g.cap + b]);
+    const size_t n1 = g.dim * g.ffn;
+    for (size_t q = 0; q < n1; q++)
+        w[g.off_e1 + a * n1 + q] = 0.5f * (w[g.off_e1 + a * n1 + q] + w[g.off_e1 + b * n1 + q]);
+    if (!g.linear)
+        for (size_t q = 0; q < n1; q++)
+            w[g.off_e2 + a * n1 + q] = 0.5f * (w[g.off_e2 + a * n1 + q] + w[g.off_e2 + b * n1 + q]);
+    m->moe_active[b] = 0;
+    m->moe_active_count--;
+    upload_weights(m);
+    return m->moe_active_count;
+}
+
+size_t nsb_expert_birth(ns_model* m, int n) {
+    MoeGeom g;
+    if (!m || !moe_geom(m, g) || n <= 0) return m ? m->moe_active_count : 0;
+    if (m->moe_active_count >= g.cap) return m->moe_active_count;
+    sync_host(m);
+    float* w = m->h_w.data();
+    int src = (int)(m->rng() % g.cap);
+    size_t tries = 0;
+    while (tries++ < g.cap && !m->moe_active[src]) src = (int)(m->rng() % g.cap);
+    const size_t n1 = g.dim * g.ffn;
+    for (int e = 0; e < (int)g.cap && n > 0; e++) {
+        if (m->moe_active[e]) continue;
+        for (size_t k = 0; k < g.dim; k++)
+            w[g.off_g + k * g.cap + e] =
+                w[g.off_g + k * g.cap + src] + ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
+        for (size_t q = 0; q < n1; q++)
+            w[g.off_e1 + e * n1 + q] = w[g.off_e1 + src * n1 + q] + ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
+        if (!g.linear)
+            for (size_t q = 0; q < n1; q++)
+                w[g.off_e2 + e * n1 + q] =
+                    w[g.off_e2 + src * n1 + q] + ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
+        m->moe_active[e] = 1;
+        m->moe_active_count++;
+        n--;
+    }
+    upload_weights(m);
+    return m->moe_active_count;
+}
+
+// ---- data parallel ----------------------------------------------------------
+int nsb_dist_unique_id(void* id128) {
+    if (!id128) return -1;
+    if (!nccl().ok) return fail("libnccl.so.2 not loadable");
+    ncclUniqueId id;
+    if (nccl().GetUniqueId(&id) != ncclSuccess) return fail("ncclGetUniqueId failed");
+    memcpy(id128, &id, sizeof(id));
+    return 0;
+}
+
+int nsb_dist_init(ns_model* m, int rank, int world, const void* id128, int timeout_ms) {
+    if (!m || !id128 || world < 1 || rank < 0 || rank >= world) return -1;
+    m->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+    if (world == 1) {
+        m->world = 1;
+        m->rank = 0;
+        return 0;
+    }
+    if (!nccl().ok) return fail("libnccl.so.2 not loadable");
+    ncclUniqueId id;
+    memcpy(&id, id128, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = nccl().CommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("nccl init: ") + nccl().GetErrorString(r));
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st;
+        nccl().CommGetAsyncError(comm, &st);
+        if (st == ncclSuccess) break;
+        if (st != ncclInProgress) {
+            nccl().CommAbort(comm);
+            return fail(std::string("nccl init: ") + nccl().GetErrorString(st));
+        }
+        auto el = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+        if (el.count() > m->timeout_ms) {
+            nccl().CommAbort(comm);
+            return fail("nccl init timed out");
+        }
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    m->comm = comm;
+    m->rank = rank;
+    m->world = world;
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+// Engine internals shared by engine.cpp and the MoE layer (moe.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+#include <stdint.h>
+
+#include <random>
+#include <string>
+#include <vector>
+
+#include "spec.h"
+
+struct ns_model;
+
+namespace nsb {
+
+// Kernel launches issued by the calling thread (each launcher adds its own).
+long long& launch_counter();
+
+enum OpKind { OP_DENSE, OP_EMB, OP_ATTN, OP_LN, OP_MOE, OP_ADD, OP_SUB, OP_MUL, OP_ACT, OP_SOFTMAX, OP_DROPOUT };
+
+struct Val {
+    std::string name;
+    int cols = 0;
+    int producer = -1;  // op index, -1 for the input
+    std::vector<int> consumers;
+    bool need_f32 = true, need_h16 = false;
+    bool materialized = true;  // false: a dense output folded into a residual add
+    int alias_of = -1;         // dropout: storage shared with its input
+    float* f32 = nullptr;
+    __nv_bfloat16* h16 = nullptr;
+    // backward
+    float* gbuf = nullptr;
+    const float* gcur = nullptr;
+};
+
+struct MoeScratch;
+
+// allocation helper bound to a model's plan (freed on re-plan / free)
+void* plan_alloc(ns_model* m, size_t bytes);
+
+struct Op {
+    int kind = OP_DENSE;
+    int layer = -1;
+    int act = 0;
+    int in = -1, in2 = -1, out = -1;  // value indices (out = the value written)
+    int self_out = -1;                // the op's own output value (differs from out when fused)
+    bool skip = false;                // an add folded into its producer's epilogue
+    int fused_res = -1;               // residual value added in the epilogue
+    int widx = -1;                    // first weight index of the layer
+    // dense / attention scratch
+    void* z = nullptr;  // pre-activation (training)
+    void* dz = nullptr;
+    float* dz32 = nullptr;
+    void* qkv = nullptr;
+    void* ctx = nullptr;
+    void* dqkv = nullptr;
+    void* dctx = nullptr;
+    void* dout_w = nullptr;
+    float* lse = nullptr;
+    float* dvec = nullptr;
+    MoeScratch* moe = nullptr;
+};
+
+}  // namespace nsb
+
+struct ns_model {
+    nsb::Spec spec;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int* d_err = nullptr;
+    int precision = 2;
+    int wdt = 1;  // working dtype of GEMM operands (kF32 / kBF16)
+    // parameters
+    float* d_w = nullptr;    // fp32 master blob
+    float* d_g = nullptr;    // gradient blob (+1 trailing float: loss sum for the all-reduce)
+    float* d_m = nullptr;    // AdamW first moment / Muon momentum
+    float* d_v = nullptr;    // AdamW second moment
+    float* d_o = nullptr;    // orthogonalisation scratch (largest matrix x 2)
+    float* d_ns = nullptr;   // Newton-Schulz scratch
+    size_t ns_floats = 0;
+    std::vector<void*> wk;   // working copy per weight index (nullptr when unused)
+    std::vector<bool> wk_owned;
+    std::vector<long long> adam_t;
+    void* d_adam = nullptr;  // device array of AdamTensor
+    int adam_cap = 0;
+    void* h_adam = nullptr;  // pinned staging for it
+    // host mirror of the master blob
+    mutable std::vector<float> h_w;
+    mutable bool host_dirty = false;
+    // MoE liveness
+    int moe_layer = -1;
+    std::vector<uint8_t> moe_active;
+    size_t moe_active_count = 0;
+    uint8_t* d_active = nullptr;
+    std::mt19937 rng{0x9E3779B9u};
+    long long lr_step = 0;
+    // graph
+    std::vector<nsb::Val> vals;
+    std::vector<nsb::Op> ops;
+    int out_val = -1;
+    // plan (sized for mmax rows)
+    int mmax = 0;
+    bool train_planned = false;
+    std::vector<void*> plan_allocs;
+    float* d_in = nullptr;
+    float* d_labels = nullptr;
+    int* d_targets = nullptr;
+    float* d_rowloss = nullptr;
+    float* d_loss = nullptr;
+    float* h_loss = nullptr;  // pinned
+    float* d_ws = nullptr;    // split-K workspace
+    size_t ws_floats = 0;
+    void* d_scratch = nullptr;  // embedding-gradient sort scratch
+    size_t scratch_bytes = 0;
+    // data parallel
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1;
+    int timeout_ms = 60000;
+    long long launches = 0;
+};

@@ -1,0 +1,674 @@
+// Dense GEMM for sm_100a.
+//
+// Tensor-core path: persistent, warp-specialised tcgen05 kernel.
+//   warp 0      TMA producer (one elected thread): A and B tiles into a
+//               STAGES-deep shared-memory ring (128-byte swizzle, no multicast)
+//   warp 1      MMA issuer (one thread) + TMEM owner: tcgen05.mma into a
+//               double-buffered fp32 accumulator in TMEM (2 x BN columns)
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, fused epilogue
+//               (residual / act' / activation / bf16 cast), global stores
+// The accumulator double buffer lets the epilogue of tile i overlap the MMAs
+// of tile i+1. K-major and MN-major operands are both read straight from
+// their storage layout (the shared-memory descriptor encodes the major-ness),
+// so no transposed copies are needed for forward, input-gradient or
+// weight-gradient GEMMs. Split-K (for weight gradients, whose K is the row
+// count) writes fp32 partials that a second kernel sums in a fixed order, so
+// results are deterministic.
+//
+// SIMT path: fp32 FMA, each output accumulated sequentially in k, for the
+// pure-fp32 parity mode and for shapes TMA cannot describe.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "gemm.h"
+#include "ptx.cuh"
+
+namespace nsb {
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue helpers (shared by all paths)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void epi_apply(const Epilogue& ep, int row, int col, float v) {
+    v *= ep.alpha;
+    if (ep.add) v += ep.add_scale * ep.add[(size_t)row * ep.ld_add + col];
+    if (ep.row_scale) v *= ep.row_scale[row];
+    if (ep.dz) v *= act_deriv(ld_any(ep.dz, ep.dz_dtype, (size_t)row * ep.ld_dz + col), ep.dz_act);
+    if (ep.z) {
+        size_t zi = (size_t)row * ep.ld_z + col;
+        if (ep.z_dtype == kBF16) reinterpret_cast<__nv_bfloat16*>(ep.z)[zi] = f2bf(v);
+        else reinterpret_cast<float*>(ep.z)[zi] = v;
+    }
+    if (ep.act) v = act_fwd(v, ep.act);
+    int orow = ep.out_rows ? ep.out_rows[row] : row;
+    if (ep.c32) ep.c32[(size_t)orow * ep.ld_c32 + col] = v;
+    if (ep.c16) ep.c16[(size_t)orow * ep.ld_c16 + col] = f2bf(v);
+}
+
+// 32 consecutive columns of one row, 16-byte vectorised (all leading
+// dimensions multiples of 8 elements, col0 a multiple of 32, col0+32 <= N).
+__device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int col0, float* v) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] *= ep.alpha;
+    if (ep.add) {
+        const float4* a = reinterpret_cast<const float4*>(ep.add + (size_t)row * ep.ld_add + col0);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float4 t = a[j];
+            v[4 * j] += ep.add_scale * t.x;
+            v[4 * j + 1] += ep.add_scale * t.y;
+            v[4 * j + 2] += ep.add_scale * t.z;
+            v[4 * j + 3] += ep.add_scale * t.w;
+        }
+    }
+    if (ep.row_scale) {
+        float s = ep.row_scale[row];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] *= s;
+    }
+    if (ep.dz) {
+        if (ep.dz_dtype == kBF16) {
+            const uint4* a = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ep.dz) +
+                                                            (size_t)row * ep.ld_dz + col0);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                uint4 t = a[j];
+                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&t);
+#pragma unroll
+                for (int q = 0; q < 8; q++) v[8 * j + q] *= act_deriv(bf2f(h[q]), ep.dz_act);
+            }
+        } else {
+            const float4* a = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ep.dz) +
+                                                              (size_t)row * ep.ld_dz + col0);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                float4 t = a[j];
+                v[4 * j] *= act_deriv(t.x, ep.dz_act);
+                v[4 * j + 1] *= act_deriv(t.y, ep.dz_act);
+                v[4 * j + 2] *= act_deriv(t.z, ep.dz_act);
+                v[4 * j + 3] *= act_deriv(t.w, ep.dz_act);
+            }
+        }
+    }
+    if (ep.z) {
+        if (ep.z_dtype == kBF16) {
+            uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ep.z) + (size_t)row * ep.ld_z + col0);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                uint4 t;
+                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&t);
+#pragma unroll
+                for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
+                o[j] = t;
+            }
+        } else {
+            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.z) + (size_t)row * ep.ld_z + col0);
+#pragma unroll
+            for (int j = 0; j < 8; j++) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+    }
+    if (ep.act) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], ep.act);
+    }
+    int orow = ep.out_rows ? ep.out_rows[row] : row;
+    if (ep.c32) {
+        float4* o = reinterpret_cast<float4*>(ep.c32 + (size_t)orow * ep.ld_c32 + col0);
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    if (ep.c16) {
+        uint4* o = reinterpret_cast<uint4*>(ep.c16 + (size_t)orow * ep.ld_c16 + col0);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint4 t;
+            __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&t);
+#pragma unroll
+            for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
+            o[j] = t;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 kernel
+// ---------------------------------------------------------------------------
+struct TcParams {
+    int M, N, K;
+    int m_tiles, n_tiles, k_blocks, splits, kb_per_split;
+    int total_units;
+    int vec_ok;
+    Epilogue ep;
+    float* workspace;  // splits > 1: raw fp32 partials [splits][M][N]
+    int* err;
+    // grouped: group g owns rows [seg[g], seg[g+1]); B rows offset g * N
+    int groups;
+    const int* seg;
+    int max_m_tiles_per_group;
+};
+
+template <int BN, bool TF32>
+struct TcCfg {
+    static constexpr int BM = 128;
+    static constexpr int ELEM = TF32 ? 4 : 2;
+    static constexpr int BK = 128 / ELEM;  // K elements per stage: one 128-byte row
+    static constexpr int CHUNK = 128 / ELEM;  // MN elements per 128-byte chunk
+    static constexpr int KSTEP = TF32 ? 8 : 16;  // K per MMA instruction (32 bytes)
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// Decode a work unit into (m0, n0, kb0, kb1, split, group); returns false
+// for an empty grouped tile.
+__device__ __forceinline__ bool tc_decode(const TcParams& p, int u, int BN, int& m0, int& n0, int& kb0, int& kb1,
+                                          int& split, int& g, int& row_end) {
+    split = u % p.splits;
+    int tile = u / p.splits;
+    int m_blk, n_blk;
+    if (p.groups > 1) {
+        // tile -> (group, m within group, n)
+        int per_group = p.max_m_tiles_per_group * p.n_tiles;
+        g = tile / per_group;
+        int t = tile % per_group;
+        m_blk = t / p.n_tiles;
+        n_blk = t % p.n_tiles;
+        int s0 = p.seg[g], s1 = p.seg[g + 1];
+        m0 = s0 + m_blk * 128;
+        if (m0 >= s1) return false;
+        row_end = s1;
+    } else {
+        g = 0;
+        m_blk = tile / p.n_tiles;
+        n_blk = tile % p.n_tiles;
+        m0 = m_blk * 128;
+        row_end = p.M;
+    }
+    n0 = n_blk * BN;
+    kb0 = split * p.kb_per_split;
+    kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+    return true;
+}
+
+template <int BN, bool TF32, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const TcParams p) {
+    using C = TcCfg<BN, TF32>;
+    constexpr uint32_t IDESC = ptx::instr_desc(TF32 ? 2 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0, C::BM, BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* acc_full = empty + C::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            ptx::mbar_init(&acc_full[a], 1);
+            ptx::mbar_init(&acc_empty[a], 128);
+        }
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tmap(&ta);
+        ptx::prefetch_tmap(&tb);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
+                int m0, n0, kb0, kb1, split, g, row_end;
+                if (!tc_decode(p, u, BN, m0, n0, kb0, kb1, split, g, row_end)) continue;
+                const int nb = g * p.N + n0;  // B row (grouped: groups stacked along N)
+                for (int kb = kb0; kb < kb1; kb++) {
+                    if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) goto producer_done;
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    uint8_t* sb = sa + C::A_BYTES;
+                    ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    if (!A_MN) {
+                        ptx::tma_load_2d(sa, &ta, &full[stage], kb * C::BK, m0);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < C::BM / C::CHUNK; c++)
+                            ptx::tma_load_2d(sa + c * (C::BK * 128), &ta, &full[stage], m0 + c * C::CHUNK, kb * C::BK);
+                    }
+                    if (!B_MN) {
+                        ptx::tma_load_2d(sb, &tb, &full[stage], kb * C::BK, nb);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < BN / C::CHUNK; c++)
+                            ptx::tma_load_2d(sb + c * (C::BK * 128), &tb, &full[stage], nb + c * C::CHUNK, kb * C::BK);
+                    }
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain: wait until every issued load has landed before the CTA
+            // can exit (bounded).
+            for (int s = 0; s < C::STAGES; s++) {
+                // the last use of stage s completed if its empty barrier
+                // passed; wait for the consumer side to release it
+                ptx::mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer);
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
+                int m0, n0, kb0, kb1, split, g, row_end;
+                if (!tc_decode(p, u, BN, m0, n0, kb0, kb1, split, g, row_end)) continue;
+                if (!ptx::mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutMma)) goto mma_done;
+                ptx::tc_fence_after();
+                const uint32_t d = tmem_base + acc * BN;
+                for (int kb = kb0; kb < kb1; kb++) {
+                    if (!ptx::mbar_wait(&full[stage], phase, p.err, kErrTimeoutMma)) goto mma_done;
+                    ptx::tc_fence_after();
+                    const uint32_t sa = ptx::smem_u32(smem + stage * C::STAGE_BYTES);
+                    const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        uint64_t ad = A_MN ? ptx::smem_desc_sw128(sa + k * C::KSTEP * 128, C::BK * 128, 1024)
+                                           : ptx::smem_desc_sw128(sa + k * 32, 16, 1024);
+                        uint64_t bd = B_MN ? ptx::smem_desc_sw128(sb + k * C::KSTEP * 128, C::BK * 128, 1024)
+                                           : ptx::smem_desc_sw128(sb + k * 32, 16, 1024);
+                        uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+                        if (TF32) ptx::mma_tf32(d, ad, bd, IDESC, accum);
+                        else ptx::mma_bf16(d, ad, bd, IDESC, accum);
+                    }
+                    ptx::mma_commit(&empty[stage]);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                ptx::mma_commit(&acc_full[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+        mma_done:;
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int lane_grp = warp & 3;  // TMEM lanes [32*lane_grp, +32)
+        const int r_in_tile = lane_grp * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
+            int m0, n0, kb0, kb1, split, g, row_end;
+            if (!tc_decode(p, u, BN, m0, n0, kb0, kb1, split, g, row_end)) continue;
+            if (!ptx::mbar_wait(&acc_full[acc], acc_phase, p.err, kErrTimeoutEpilogue)) break;
+            ptx::tc_fence_after();
+            const int row = m0 + r_in_tile;
+            const bool row_ok = row < row_end;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + acc * BN + c, r);
+                ptx::tmem_ld_wait();
+                const int col0 = n0 + c;
+                if (!row_ok || col0 >= p.N) continue;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                if (p.splits > 1) {
+                    float* w = p.workspace + ((size_t)split * p.M + row) * p.N + col0;
+                    if (p.vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            reinterpret_cast<float4*>(w)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else {
+                        for (int j = 0; j < 32 && col0 + j < p.N; j++) w[j] = v[j];
+                    }
+                } else if (p.vec_ok && col0 + 32 <= p.N) {
+                    epi_apply32_vec(p.ep, row, col0, v);
+                } else {
+                    for (int j = 0; j < 32 && col0 + j < p.N; j++) epi_apply(p.ep, row, col0 + j, v[j]);
+                }
+            }
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&acc_empty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// Sum split-K partials in split order, then the full epilogue.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, Epilogue ep) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t total = (size_t)M * N;
+    if (idx >= total) return;
+    int row = (int)(idx / N), col = (int)(idx % N);
+    float v = 0.f;
+    for (int s = 0; s < splits; s++) v += ws[(size_t)s * total + idx];
+    epi_apply(ep, row, col, v);
+}
+
+// ---------------------------------------------------------------------------
+// SIMT fp32 kernel: 64x64 tile, 256 threads, 4x4 outputs per thread, each
+// output accumulated with fmaf in increasing k.
+// ---------------------------------------------------------------------------
+struct SimtParams {
+    int M, N, K;
+    GemmOperand a, b;
+    Epilogue ep;
+    int groups;
+    const int* seg;
+    long long b_group_stride;
+};
+
+__device__ __forceinline__ float ld_op(const GemmOperand& o, long long i, long long k) {
+    size_t idx = o.mn_major ? (size_t)(k * o.ld + i) : (size_t)(i * o.ld + k);
+    return ld_any(o.ptr, o.dtype, idx);
+}
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
+    __shared__ float As[16][64 + 1];
+    __shared__ float Bs[16][64 + 1];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    int g = 0, row_end = p.M;
+    GemmOperand b = p.b;
+    if (p.groups > 1) {
+        // blockIdx.z = group; rows [seg[g], seg[g+1])
+        g = blockIdx.z;
+        int s0 = p.seg[g], s1 = p.seg[g + 1];
+        if (s0 + m0 >= s1) return;
+        row_end = s1;
+        b.ptr = (const char*)b.ptr + (size_t)g * p.b_group_stride * (b.dtype == kBF16 ? 2 : 4);
+    }
+    const int mbase = (p.groups > 1 ? p.seg[g] : 0) + m0;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < p.K; k0 += 16) {
+        for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+            int kk = e / 64, ii = e % 64;
+            int gm = mbase + ii, gk = k0 + kk, gn = n0 + ii;
+            As[kk][ii] = (gm < row_end && gk < p.K) ? ld_op(p.a, gm, gk) : 0.f;
+            Bs[kk][ii] = (gn < p.N && gk < p.K) ? ld_op(b, gn, gk) : 0.f;
+        }
+        __syncthreads();
+        const int kmax = min(16, p.K - k0);
+        for (int kk = 0; kk < kmax; kk++) {
+            float av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) av[i] = As[kk][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) bv[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int row = mbase + ty + 16 * i;
+        if (row >= row_end) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int col = n0 + tx + 16 * j;
+            if (col < p.N) epi_apply(p.ep, row, col, acc[i][j]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+// 2D map over a row-major [outer, inner] array with leading dimension ld
+// (elements); box {box_inner, box_outer}; 128-byte swizzle.
+static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner, long long outer, long long ld,
+                     int box_inner, int box_outer) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return false;
+    const int es = dtype == kBF16 ? 2 : 4;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                     const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+static bool operand_tc_ok(const GemmOperand& o) {
+    const int es = o.dtype == kBF16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(o.ptr) & 15) != 0) return false;
+    if ((o.ld * es) % 16 != 0) return false;
+    return true;
+}
+
+bool gemm_uses_tensor_cores(const GemmDesc& d) {
+    if (d.engine == kEngineSimt) return false;
+    if (d.a.dtype != d.b.dtype) return false;
+    if (!operand_tc_ok(d.a) || !operand_tc_ok(d.b)) return false;
+    if (d.M <= 0 || d.N <= 0 || d.K <= 0) return false;
+    // very narrow outputs waste a 128-wide tile; the SIMT kernel is cheaper
+    if (d.N < 32) return false;
+    return true;
+}
+
+static int pick_bn(const GemmDesc& d) { return d.N >= 256 && d.groups == 1 ? 256 : 128; }
+
+static void pick_splits(const GemmDesc& d, int bn, int& splits, int& kb_per_split, int k_blocks) {
+    splits = 1;
+    if (d.groups == 1) {
+        const int tiles = ((d.M + 127) / 128) * ((d.N + bn - 1) / bn);
+        const int sms = num_sms();
+        if (d.splits > 0) splits = d.splits;
+        else if (tiles < sms / 2 && k_blocks >= 16) {
+            splits = (sms + tiles - 1) / tiles;
+            splits = min(splits, k_blocks / 8);
+            splits = max(splits, 1);
+        }
+    }
+    kb_per_split = (k_blocks + splits - 1) / splits;
+    splits = (k_blocks + kb_per_split - 1) / kb_per_split;
+}
+
+size_t gemm_workspace_floats(const GemmDesc& d) {
+    if (!gemm_uses_tensor_cores(d)) return 0;
+    const int bn = pick_bn(d);
+    const int bk = d.a.dtype == kBF16 ? 64 : 32;
+    int splits, kbps;
+    pick_splits(d, bn, splits, kbps, (d.K + bk - 1) / bk);
+    return splits > 1 ? (size_t)splits * d.M * d.N : 0;
+}
+
+template <int BN, bool TF32, bool A_MN, bool B_MN>
+static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t s) {
+    using C = TcCfg<BN, TF32>;
+    auto k = gemm_tc_kernel<BN, TF32, A_MN, B_MN>;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        attr = true;
+    }
+    int grid = min(p.total_units, num_sms());
+    if (grid <= 0) return cudaSuccess;
+    k<<<grid, 192, C::SMEM, s>>>(ta, tb, p);
+    return cudaGetLastError();
+}
+
+template <int BN, bool TF32>
+static cudaError_t launch_tc_majors(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, bool amn,
+                                    bool bmn, cudaStream_t s) {
+    if (!amn && !bmn) return launch_tc<BN, TF32, false, false>(ta, tb, p, s);
+    if (!amn && bmn) return launch_tc<BN, TF32, false, true>(ta, tb, p, s);
+    if (amn && !bmn) return launch_tc<BN, TF32, true, false>(ta, tb, p, s);
+    return launch_tc<BN, TF32, true, true>(ta, tb, p, s);
+}
+
+static bool ep_vec_ok(const GemmDesc& d) {
+    const Epilogue& e = d.ep;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (e.add && (e.ld_add % 4 || !al(e.add))) return false;
+    if (e.dz && (e.ld_dz % 8 || !al(e.dz))) return false;
+    if (e.z && (e.ld_z % 8 || !al(e.z))) return false;
+    if (e.c32 && (e.ld_c32 % 4 || !al(e.c32))) return false;
+    if (e.c16 && (e.ld_c16 % 8 || !al(e.c16))) return false;
+    if (d.workspace && !al(d.workspace)) return false;
+    if (d.N % 4) return false;
+    return true;
+}
+
+static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
+    const bool tf32 = d.a.dtype == kF32;
+    const int bn = pick_bn(d);
+    const int bk = tf32 ? 32 : 64;
+    const int chunk = tf32 ? 32 : 64;
+    CUtensorMap ta, tb;
+    // A: M x K. K-major -> array [M][ld] (inner K); MN-major -> [K][ld] (inner M)
+    bool ok;
+    if (!d.a.mn_major) ok = make_map(&ta, d.a.ptr, d.a.dtype, d.K, d.M, d.a.ld, bk, 128);
+    else ok = make_map(&ta, d.a.ptr, d.a.dtype, d.M, d.K, d.a.ld, chunk, bk);
+    if (!ok) return -2;
+    const long long brows = (long long)d.N * d.groups;
+    if (!d.b.mn_major) ok = make_map(&tb, d.b.ptr, d.b.dtype, d.K, brows, d.b.ld, bk, bn);
+    else ok = make_map(&tb, d.b.ptr, d.b.dtype, brows, d.K, d.b.ld, chunk, bk);
+    if (!ok) return -2;
+
+    TcParams p;
+    p.M = d.M;
+    p.N = d.N;
+    p.K = d.K;
+    p.m_tiles = (d.M + 127) / 128;
+    p.n_tiles = (d.N + bn - 1) / bn;
+    p.k_blocks = (d.K + bk - 1) / bk;
+    pick_splits(d, bn, p.splits, p.kb_per_split, p.k_blocks);
+    p.ep = d.ep;
+    p.err = dev_err;
+    p.groups = d.groups;
+    p.seg = d.seg;
+    p.max_m_tiles_per_group = p.m_tiles;
+    p.workspace = nullptr;
+    if (p.splits > 1) {
+        if (!d.workspace || d.workspace_floats < (size_t)p.splits * d.M * d.N) return -3;
+        p.workspace = d.workspace;
+    }
+    p.vec_ok = ep_vec_ok(d) ? 1 : 0;
+    if (d.groups > 1) {
+        // groups are stacked along B's rows: only a K-major B whose group
+        // stride is exactly N rows can be described by one 2D tensor map
+        if (d.b.mn_major || d.b_group_stride != (long long)d.N * d.b.ld) return -4;
+        p.total_units = d.groups * p.max_m_tiles_per_group * p.n_tiles * p.splits;
+    } else {
+        p.total_units = p.m_tiles * p.n_tiles * p.splits;
+    }
+    cudaError_t e;
+    if (bn == 256) {
+        e = tf32 ? launch_tc_majors<256, true>(ta, tb, p, d.a.mn_major, d.b.mn_major, s)
+                 : launch_tc_majors<256, false>(ta, tb, p, d.a.mn_major, d.b.mn_major, s);
+    } else {
+        e = tf32 ? launch_tc_majors<128, true>(ta, tb, p, d.a.mn_major, d.b.mn_major, s)
+                 : launch_tc_majors<128, false>(ta, tb, p, d.a.mn_major, d.b.mn_major, s);
+    }
+    if (e != cudaSuccess) return -5;
+    if (p.splits > 1) {
+        size_t total = (size_t)d.M * d.N;
+        splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(p.workspace, p.splits, d.M, d.N, d.ep);
+        if (cudaGetLastError() != cudaSuccess) return -5;
+    }
+    return 0;
+}
+
+static int gemm_simt(const GemmDesc& d, cudaStream_t s) {
+    SimtParams p;
+    p.M = d.M;
+    p.N = d.N;
+    p.K = d.K;
+    p.a = d.a;
+    p.b = d.b;
+    p.ep = d.ep;
+    p.groups = d.groups;
+    p.seg = d.seg;
+    p.b_group_stride = d.b_group_stride;
+    dim3 grid((d.N + 63) / 64, (d.M + 63) / 64, d.groups);
+    if (grid.x == 0 || grid.y == 0) return 0;
+    gemm_simt_kernel<<<grid, 256, 0, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int gemm(const GemmDesc& d, cudaStream_t s, int* dev_err) {
+    if (d.M < 0 || d.N < 0 || d.K < 0) return -1;
+    if (d.M == 0 || d.N == 0) return 0;
+    if (d.engine == kEngineTensor && !gemm_uses_tensor_cores(d)) return -1;
+    if (gemm_uses_tensor_cores(d)) return gemm_tc(d, s, dev_err);
+    return gemm_simt(d, s);
+}
+
+}  // namespace nsb

@@ -1,0 +1,738 @@
+// Memory-bound kernels of the hot path. One warp per row for row-wise ops
+// (coalesced 128-bit accesses, warp-shuffle reductions), grid-stride
+// elementwise kernels sized to the SM count, and fixed-order reductions
+// everywhere (no float atomics), so every result is run-to-run bitwise
+// reproducible.
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace nsb {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+
+// Block-wide sum in a fixed order (warp trees, then warp 0 over the partials).
+__device__ float block_sum(float v, float* sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    float r = 0.f;
+    if (w == 0) {
+        r = lane < nw ? sh[lane] : 0.f;
+        r = warp_sum(r);
+        if (lane == 0) sh[32] = r;
+    }
+    __syncthreads();
+    return sh[32];
+}
+__device__ float block_max(float v, float* sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        float r = lane < nw ? sh[lane] : -INFINITY;
+        r = warp_max(r);
+        if (lane == 0) sh[32] = r;
+    }
+    __syncthreads();
+    return sh[32];
+}
+
+inline unsigned grid_for(size_t n, int per_block) {
+    size_t g = (n + per_block - 1) / per_block;
+    size_t cap = (size_t)num_sms() * 16;
+    if (g > cap) g = cap;
+    if (g == 0) g = 1;
+    return (unsigned)g;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+inline int launch_ok() { return cudaGetLastError() == cudaSuccess ? 0 : -5; }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Embedding
+// ---------------------------------------------------------------------------
+__global__ void embedding_fwd_kernel(const float* __restrict__ W, const float* __restrict__ ids, int M, int V, int D,
+                                     float* __restrict__ out32, __nv_bfloat16* __restrict__ out16, int vec) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        long long k = (long long)ids[r];  // truncation toward zero, as the reference's (int64_t) cast
+        if (k < 0 || k >= V) k = 0;
+        const float* src = W + (size_t)k * D;
+        if (vec) {
+            for (int c = lane * 4; c < D; c += 128) {
+                float4 t = *reinterpret_cast<const float4*>(src + c);
+                if (out32) *reinterpret_cast<float4*>(out32 + (size_t)r * D + c) = t;
+                if (out16) {
+                    __nv_bfloat162 a = __floats2bfloat162_rn(t.x, t.y), b = __floats2bfloat162_rn(t.z, t.w);
+                    uint2 u;
+                    u.x = *reinterpret_cast<uint32_t*>(&a);
+                    u.y = *reinterpret_cast<uint32_t*>(&b);
+                    *reinterpret_cast<uint2*>(out16 + (size_t)r * D + c) = u;
+                }
+            }
+        } else {
+            for (int c = lane; c < D; c += 32) {
+                float t = src[c];
+                if (out32) out32[(size_t)r * D + c] = t;
+                if (out16) out16[(size_t)r * D + c] = f2bf(t);
+            }
+        }
+    }
+}
+
+int embedding_fwd(const float* W, const float* ids, int M, int V, int D, float* out32, __nv_bfloat16* out16,
+                  cudaStream_t s) {
+    if (M <= 0) return 0;
+    int vec = (D % 4 == 0) && aligned16(W) && (!out32 || aligned16(out32)) && (!out16 || (reinterpret_cast<uintptr_t>(out16) & 7) == 0);
+    embedding_fwd_kernel<<<grid_for((size_t)M, 8), 256, 0, s>>>(W, ids, M, V, D, out32, out16, vec);
+    return launch_ok();
+}
+
+size_t embedding_bwd_scratch_bytes(int M, int V) {
+    // count[V], offset[V], cursor[V], rows[M]
+    return sizeof(int) * ((size_t)3 * V + M) + 64;
+}
+
+__global__ void zero_ints_kernel(int* p, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = 0;
+}
+
+__global__ void emb_count_kernel(const float* __restrict__ ids, int M, int V, int* count) {
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
+        long long v = (long long)ids[r];
+        if (v >= 0 && v < V) atomicAdd(&count[v], 1);  // integer counts: order-independent
+    }
+}
+
+// Exclusive scan of n ints, one CTA of 1024 threads, chunked.
+__global__ void scan_kernel(const int* __restrict__ in, int* __restrict__ out, int n) {
+    __shared__ int sh[1024];
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < n; base += 1024) {
+        int i = base + threadIdx.x;
+        int v = i < n ? in[i] : 0;
+        sh[threadIdx.x] = v;
+        __syncthreads();
+        for (int off = 1; off < 1024; off <<= 1) {
+            int t = threadIdx.x >= off ? sh[threadIdx.x - off] : 0;
+            __syncthreads();
+            sh[threadIdx.x] += t;
+            __syncthreads();
+        }
+        if (i < n) out[i] = carry + sh[threadIdx.x] - v;
+        __syncthreads();
+        if (threadIdx.x == 1023) carry += sh[1023];
+        __syncthreads();
+    }
+}
+
+__global__ void emb_fill_kernel(const float* __restrict__ ids, int M, int V, const int* __restrict__ offset,
+                                int* cursor, int* rows) {
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
+        long long v = (long long)ids[r];
+        if (v >= 0 && v < V) {
+            int slot = atomicAdd(&cursor[v], 1);  // slot order is arbitrary; the reduce sorts by row
+            rows[offset[v] + slot] = r;
+        }
+    }
+}
+
+// One warp per vocabulary row: gather the rows that hit it, order them by
+// row index, and sum their gradients in that order.
+__global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, const int* __restrict__ count,
+                                  const int* __restrict__ offset, const int* __restrict__ rows,
+                                  float* __restrict__ dW, int vec) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    for (int v = blockIdx.x * warps + (threadIdx.x >> 5); v < V; v += gridDim.x * warps) {
+        const int n = count[v];
+        const int* rv = rows + offset[v];
+        float* dst = dW + (size_t)v * D;
+        if (n == 0) {
+            for (int c = lane; c < D; c += 32) dst[c] = 0.f;
+            continue;
+        }
+        if (n <= 32) {
+            int key = lane < n ? rv[lane] : 0x7fffffff;
+            // warp bitonic sort, ascending
+#pragma unroll
+            for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    int other = __shfl_xor_sync(kFull, key, j);
+                    bool up = (lane & k) == 0;
+                    bool lower = (lane & j) == 0;
+                    int mn = min(key, other), mx = max(key, other);
+                    key = (lower == up) ? mn : mx;
+                }
+            }
+            if (vec) {
+                for (int c = lane * 4; c < D; c += 128) {
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int q = 0; q < n; q++) {
+                        int r = __shfl_sync(kFull, key, q);
+                        float4 t = *reinterpret_cast<const float4*>(dout + (size_t)r * D + c);
+                        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+                    }
+                    *reinterpret_cast<float4*>(dst + c) = acc;
+                }
+            } else {
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    int c = c0 + lane;
+                    float acc = 0.f;
+                    for (int q = 0; q < n; q++) {
+                        int r = __shfl_sync(kFull, key, q);
+                        if (c < D) acc += dout[(size_t)r * D + c];
+                    }
+                    if (c < D) dst[c] = acc;
+                }
+            }
+        } else {
+            // large bucket: repeatedly take the next-smallest row index
+            for (int c = lane; c < D; c += 32) dst[c] = 0.f;
+            __syncwarp();
+            int last = -1;
+            for (int q = 0; q < n; q++) {
+                int cand = 0x7fffffff;
+                for (int i = lane; i < n; i += 32) {
+                    int r = rv[i];
+                    if (r > last && r < cand) cand = r;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(kFull, cand, o));
+                last = cand;
+                for (int c = lane; c < D; c += 32) dst[c] += dout[(size_t)cand * D + c];
+            }
+        }
+    }
+}
+
+int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, float* dW, void* scratch,
+                  cudaStream_t s) {
+    int* count = reinterpret_cast<int*>(scratch);
+    int* offset = count + V;
+    int* cursor = offset + V;
+    int* rows = cursor + V;
+    zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3);
+    if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count);
+    scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
+    if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
+    int vec = (D % 4 == 0) && aligned16(dout) && aligned16(dW);
+    emb_reduce_kernel<<<grid_for((size_t)V, 8), 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    return launch_ok();
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm (no affine, eps 1e-5) — reference ns_layernorm / ns_layernorm_grad
+// ---------------------------------------------------------------------------
+__global__ void layernorm_fwd_kernel(const float* __restrict__ x, int M, int D, float* __restrict__ out32,
+                                     __nv_bfloat16* __restrict__ out16) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        const float* xr = x + (size_t)r * D;
+        float s = 0.f;
+        for (int c = lane; c < D; c += 32) s += xr[c];
+        const float mean = warp_sum(s) / (float)D;
+        float q = 0.f;
+        for (int c = lane; c < D; c += 32) {
+            float d = xr[c] - mean;
+            q += d * d;
+        }
+        const float var = warp_sum(q) / (float)D;
+        const float inv = 1.f / sqrtf(var + 1e-5f);
+        for (int c = lane; c < D; c += 32) {
+            float y = (xr[c] - mean) * inv;
+            if (out32) out32[(size_t)r * D + c] = y;
+            if (out16) out16[(size_t)r * D + c] = f2bf(y);
+        }
+    }
+}
+
+// D a multiple of 128, D <= 1024: the row stays in registers (float4 per
+// lane per 128 columns), one HBM read and one write per element.
+template <int NV>
+__global__ void layernorm_fwd_vec_kernel(const float* __restrict__ x, int M, float* __restrict__ out32,
+                                         __nv_bfloat16* __restrict__ out16) {
+    constexpr int D = NV * 128;
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * D);
+        float4 v[NV];
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            v[i] = xr[lane + 32 * i];
+            s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        }
+        const float mean = warp_sum(s) / (float)D;
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+            q += (a * a + b * b) + (c * c + d * d);
+        }
+        const float var = warp_sum(q) / (float)D;
+        const float inv = 1.f / sqrtf(var + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            float4 y = make_float4((v[i].x - mean) * inv, (v[i].y - mean) * inv, (v[i].z - mean) * inv,
+                                   (v[i].w - mean) * inv);
+            const int c = 4 * (lane + 32 * i);
+            if (out32) *reinterpret_cast<float4*>(out32 + (size_t)r * D + c) = y;
+            if (out16) {
+                __nv_bfloat162 a = __floats2bfloat162_rn(y.x, y.y), b = __floats2bfloat162_rn(y.z, y.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&a);
+                u.y = *reinterpret_cast<uint32_t*>(&b);
+                *reinterpret_cast<uint2*>(out16 + (size_t)r * D + c) = u;
+            }
+        }
+    }
+}
+
+int layernorm_fwd(const float* x, int M, int D, float* out32, __nv_bfloat16* out16, cudaStream_t s) {
+    if (M <= 0) return 0;
+    const bool vec = D % 128 == 0 && D <= 1024 && aligned16(x) && (!out32 || aligned16(out32)) &&
+                     (!out16 || (reinterpret_cast<uintptr_t>(out16) & 7) == 0);
+    unsigned g = grid_for((size_t)M, 8);
+    if (vec) {
+        switch (D / 128) {
+            case 1: layernorm_fwd_vec_kernel<1><<<g, 256, 0, s>>>(x, M, out32, out16); break;
+            case 2: layernorm_fwd_vec_kernel<2><<<g, 256, 0, s>>>(x, M, out32, out16); break;
+            case 4: layernorm_fwd_vec_kernel<4><<<g, 256, 0, s>>>(x, M, out32, out16); break;
+            case 8: layernorm_fwd_vec_kernel<8><<<g, 256, 0, s>>>(x, M, out32, out16); break;
+            default: layernorm_fwd_kernel<<<g, 256, 0, s>>>(x, M, D, out32, out16);
+        }
+    } else {
+        layernorm_fwd_kernel<<<g, 256, 0, s>>>(x, M, D, out32, out16);
+    }
+    return launch_ok();
+}
+
+__global__ void layernorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                     const float* __restrict__ add, int M, int D, float* __restrict__ dx32,
+                                     __nv_bfloat16* __restrict__ dx16) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        const float* xr = x + (size_t)r * D;
+        const float* dr = dy + (size_t)r * D;
+        float sx = 0.f, sd = 0.f;
+        for (int c = lane; c < D; c += 32) {
+            sx += xr[c];
+            sd += dr[c];
+        }
+        const float mean_x = warp_sum(sx) / (float)D;
+        const float mean_d = warp_sum(sd) / (float)D;
+        float vq = 0.f, gq = 0.f;
+        for (int c = lane; c < D; c += 32) {
+            float xc = xr[c] - mean_x;
+            vq += xc * xc;
+            gq += xc * dr[c];
+        }
+        const float var = warp_sum(vq) / (float)D;
+        const float gamma = warp_sum(gq) / (float)D;
+        const float inv = 1.f / sqrtf(var + 1e-5f);
+        for (int c = lane; c < D; c += 32) {
+            float xc = xr[c] - mean_x;
+            float o = (dr[c] - mean_d - xc * gamma) * inv;
+            if (add) o += add[(size_t)r * D + c];
+            if (dx32) dx32[(size_t)r * D + c] = o;
+            if (dx16) dx16[(size_t)r * D + c] = f2bf(o);
+        }
+    }
+}
+
+template <int NV>
+__global__ void layernorm_bwd_vec_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                         const float* __restrict__ add, int M, float* __restrict__ dx32,
+                                         __nv_bfloat16* __restrict__ dx16) {
+    constexpr int D = NV * 128;
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * D);
+        const float4* dr = reinterpret_cast<const float4*>(dy + (size_t)r * D);
+        float4 xv[NV], dv[NV];
+        float sx = 0.f, sd = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            xv[i] = xr[lane + 32 * i];
+            dv[i] = dr[lane + 32 * i];
+            sx += (xv[i].x + xv[i].y) + (xv[i].z + xv[i].w);
+            sd += (dv[i].x + dv[i].y) + (dv[i].z + dv[i].w);
+        }
+        const float mean_x = warp_sum(sx) / (float)D;
+        const float mean_d = warp_sum(sd) / (float)D;
+        float vq = 0.f, gq = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            float a = xv[i].x - mean_x, b = xv[i].y - mean_x, c = xv[i].z - mean_x, d = xv[i].w - mean_x;
+            vq += (a * a + b * b) + (c * c + d * d);
+            gq += (a * dv[i].x + b * dv[i].y) + (c * dv[i].z + d * dv[i].w);
+        }
+        const float var = warp_sum(vq) / (float)D;
+        const float gamma = warp_sum(gq) / (float)D;
+        const float inv = 1.f / sqrtf(var + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            const int c = 4 * (lane + 32 * i);
+            float4 o;
+            o.x = (dv[i].x - mean_d - (xv[i].x - mean_x) * gamma) * inv;
+            o.y = (dv[i].y - mean_d - (xv[i].y - mean_x) * gamma) * inv;
+            o.z = (dv[i].z - mean_d - (xv[i].z - mean_x) * gamma) * inv;
+            o.w = (dv[i].w - mean_d - (xv[i].w - mean_x) * gamma) * inv;
+            if (add) {
+                float4 a = *reinterpret_cast<const float4*>(add + (size_t)r * D + c);
+                o.x += a.x; o.y += a.y; o.z += a.z; o.w += a.w;
+            }
+            if (dx32) *reinterpret_cast<float4*>(dx32 + (size_t)r * D + c) = o;
+            if (dx16) {
+                __nv_bfloat162 a = __floats2bfloat162_rn(o.x, o.y), b = __floats2bfloat162_rn(o.z, o.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&a);
+                u.y = *reinterpret_cast<uint32_t*>(&b);
+                *reinterpret_cast<uint2*>(dx16 + (size_t)r * D + c) = u;
+            }
+        }
+    }
+}
+
+int layernorm_bwd(const float* dy, const float* x, const float* add, int M, int D, float* dx32, __nv_bfloat16* dx16,
+                  cudaStream_t s) {
+    if (M <= 0) return 0;
+    const bool vec = D % 128 == 0 && D <= 1024 && aligned16(x) && aligned16(dy) && (!add || aligned16(add)) &&
+                     (!dx32 || aligned16(dx32)) && (!dx16 || (reinterpret_cast<uintptr_t>(dx16) & 7) == 0);
+    unsigned g = grid_for((size_t)M, 8);
+    if (vec) {
+        switch (D / 128) {
+            case 1: layernorm_bwd_vec_kernel<1><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
+            case 2: layernorm_bwd_vec_kernel<2><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
+            case 4: layernorm_bwd_vec_kernel<4><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
+            case 8: layernorm_bwd_vec_kernel<8><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
+            default: layernorm_bwd_kernel<<<g, 256, 0, s>>>(dy, x, add, M, D, dx32, dx16);
+        }
+    } else {
+        layernorm_bwd_kernel<<<g, 256, 0, s>>>(dy, x, add, M, D, dx32, dx16);
+    }
+    return launch_ok();
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy forward + seed gradient (reference ns_cross_entropy /
+// ns_loss_grad, src/codegen/codegen.cpp:1582-1613), one CTA per row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) ce_kernel(const float* __restrict__ logits, const float* __restrict__ labels,
+                                                 const int* __restrict__ targets, int M, int C, float denom,
+                                                 float* __restrict__ row_loss, float* __restrict__ d32,
+                                                 __nv_bfloat16* __restrict__ d16) {
+    __shared__ float sh[33];
+    for (int r = blockIdx.x; r < M; r += gridDim.x) {
+        const float* x = logits + (size_t)r * C;
+        float mx = -INFINITY;
+        for (int j = threadIdx.x; j < C; j += blockDim.x) mx = fmaxf(mx, x[j]);
+        mx = block_max(mx, sh);
+        float se = 0.f;
+        for (int j = threadIdx.x; j < C; j += blockDim.x) se += expf(x[j] - mx);
+        se = block_sum(se, sh);
+        const int t = targets ? targets[r] : -1;
+        float loss = 0.f;
+        for (int j = threadIdx.x; j < C; j += blockDim.x) {
+            const float p = expf(x[j] - mx) / se;
+            const float y = labels ? labels[(size_t)r * C + j] : (j == t ? 1.f : 0.f);
+            if (y > 0.f) loss -= logf(p);
+            const float d = (p - y) / denom;
+            if (d32) d32[(size_t)r * C + j] = d;
+            if (d16) d16[(size_t)r * C + j] = f2bf(d);
+        }
+        loss = block_sum(loss, sh);
+        if (threadIdx.x == 0) row_loss[r] = loss;
+    }
+}
+
+int cross_entropy_fwd_bwd(const float* logits, const float* labels, const int* targets, int M, int C, float denom,
+                          float* row_loss, float* d32, __nv_bfloat16* d16, cudaStream_t s) {
+    if (M <= 0) return 0;
+    unsigned g = (unsigned)min(M, num_sms() * 8);
+    ce_kernel<<<g, 256, 0, s>>>(logits, labels, targets, M, C, denom, row_loss, d32, d16);
+    return launch_ok();
+}
+
+__global__ void mse_kernel(const float* __restrict__ p, const float* __restrict__ y, int M, int C, float denom,
+                           float* __restrict__ row_loss, float* __restrict__ d32, __nv_bfloat16* __restrict__ d16) {
+    __shared__ float sh[33];
+    for (int r = blockIdx.x; r < M; r += gridDim.x) {
+        float acc = 0.f;
+        for (int j = threadIdx.x; j < C; j += blockDim.x) {
+            size_t i = (size_t)r * C + j;
+            float e = p[i] - y[i];
+            acc += e * e;
+            float d = 2.0f * e / denom;
+            if (d32) d32[i] = d;
+            if (d16) d16[i] = f2bf(d);
+        }
+        acc = block_sum(acc, sh);
+        if (threadIdx.x == 0) row_loss[r] = acc;
+    }
+}
+
+int mse_fwd_bwd(const float* p, const float* y, int M, int C, float denom, float* row_loss, float* d32,
+                __nv_bfloat16* d16, cudaStream_t s) {
+    if (M <= 0) return 0;
+    mse_kernel<<<(unsigned)min(M, num_sms() * 8), 256, 0, s>>>(p, y, M, C, denom, row_loss, d32, d16);
+    return launch_ok();
+}
+
+__global__ void reduce_sum_kernel(const float* __restrict__ x, int n, float scale, float* out) {
+    __shared__ float sh[33];
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) acc += x[i];
+    acc = block_sum(acc, sh);
+    if (threadIdx.x == 0) *out = acc * scale;
+}
+
+int reduce_sum(const float* x, int n, float scale, float* out, cudaStream_t s) {
+    reduce_sum_kernel<<<1, 1024, 0, s>>>(x, n, scale, out);
+    return launch_ok();
+}
+
+// ---------------------------------------------------------------------------
+// Elementwise
+// ---------------------------------------------------------------------------
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b, size_t n, float* __restrict__ o32,
+                           __nv_bfloat16* __restrict__ o16) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = a[i] + b[i];
+        if (o32) o32[i] = v;
+        if (o16) o16[i] = f2bf(v);
+    }
+}
+int add_f32(const float* a, const float* b, size_t n, float* out32, __nv_bfloat16* out16, cudaStream_t s) {
+    if (n == 0) return 0;
+    add_kernel<<<grid_for(n, 256), 256, 0, s>>>(a, b, n, out32, out16);
+    return launch_ok();
+}
+
+__global__ void act_fwd_kernel(const float* __restrict__ x, size_t n, int act, float* __restrict__ o32,
+                               __nv_bfloat16* __restrict__ o16) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = act_fwd(x[i], act);
+        if (o32) o32[i] = v;
+        if (o16) o16[i] = f2bf(v);
+    }
+}
+int act_fwd_f32(const float* x, size_t n, int act, float* out32, __nv_bfloat16* out16, cudaStream_t s) {
+    if (n == 0) return 0;
+    act_fwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, act, out32, out16);
+    return launch_ok();
+}
+
+__global__ void act_bwd_kernel(const float* __restrict__ dy, const void* __restrict__ z, int z_dtype, int act,
+                               const float* __restrict__ add, size_t n, float* __restrict__ o32,
+                               __nv_bfloat16* __restrict__ o16) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = dy[i] * act_deriv(ld_any(z, z_dtype, i), act);
+        if (add) v += add[i];
+        if (o32) o32[i] = v;
+        if (o16) o16[i] = f2bf(v);
+    }
+}
+int act_bwd(const float* dy, const void* z, int z_dtype, int act, const float* add, size_t n, float* out32,
+            __nv_bfloat16* out16, cudaStream_t s) {
+    if (n == 0) return 0;
+    act_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(dy, z, z_dtype, act, add, n, out32, out16);
+    return launch_ok();
+}
+
+__global__ void f2bf_kernel(const float* __restrict__ x, size_t n, __nv_bfloat16* __restrict__ o) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        o[i] = f2bf(x[i]);
+}
+int f32_to_bf16(const float* x, size_t n, __nv_bfloat16* out, cudaStream_t s) {
+    if (n == 0) return 0;
+    f2bf_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, out);
+    return launch_ok();
+}
+
+// reference ns_softmax (codegen.cpp:1293-1302), one warp per row
+__global__ void softmax_kernel(const float* __restrict__ x, int M, int C, float* __restrict__ o32,
+                               __nv_bfloat16* __restrict__ o16) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        const float* xr = x + (size_t)r * C;
+        float mx = -INFINITY;
+        for (int j = lane; j < C; j += 32) mx = fmaxf(mx, xr[j]);
+        mx = warp_max(mx);
+        float s = 0.f;
+        for (int j = lane; j < C; j += 32) s += expf(xr[j] - mx);
+        s = warp_sum(s);
+        for (int j = lane; j < C; j += 32) {
+            float v = expf(xr[j] - mx) / s;
+            if (o32) o32[(size_t)r * C + j] = v;
+            if (o16) o16[(size_t)r * C + j] = f2bf(v);
+        }
+    }
+}
+int softmax_rows(const float* x, int M, int C, float* out32, __nv_bfloat16* out16, cudaStream_t s) {
+    if (M <= 0) return 0;
+    softmax_kernel<<<grid_for((size_t)M, 8), 256, 0, s>>>(x, M, C, out32, out16);
+    return launch_ok();
+}
+
+__global__ void pack_weight_kernel(const float* __restrict__ src, int rows, int cols, void* dst, int dtype,
+                                   long long ld, int off) {
+    size_t n = (size_t)rows * cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        size_t r = i / cols, c = i % cols;
+        size_t o = r * ld + off + c;
+        if (dtype == kBF16) reinterpret_cast<__nv_bfloat16*>(dst)[o] = f2bf(src[i]);
+        else reinterpret_cast<float*>(dst)[o] = src[i];
+    }
+}
+int pack_weight(const float* src, int rows, int cols, void* dst, int dst_dtype, long long ld_dst, int col_off,
+                cudaStream_t s) {
+    size_t n = (size_t)rows * cols;
+    if (n == 0) return 0;
+    pack_weight_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, rows, cols, dst, dst_dtype, ld_dst, col_off);
+    return launch_ok();
+}
+
+// ---------------------------------------------------------------------------
+// Optimizers
+// ---------------------------------------------------------------------------
+// codegen.cpp:3108-3120 per element.
+__device__ __forceinline__ void adamw_body(const AdamTensor& t, const AdamHyper& h) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < t.n; i += (long long)gridDim.x * blockDim.x) {
+        const float gg = t.g[i];
+        const float m = h.beta1 * t.m[i] + h.one_minus_beta1 * gg;
+        const float v = h.beta2 * t.v[i] + h.one_minus_beta2 * gg * gg;
+        t.m[i] = m;
+        t.v[i] = v;
+        const float mh = m / t.b1t, vh = v / t.b2t;
+        const float w = t.w[i];
+        t.w[i] = w - ((h.lr * mh / (sqrtf(vh) + h.eps)) + (h.decay * h.lr) * w);
+    }
+}
+
+// blockIdx.y selects the tensor
+__global__ void adamw_kernel(const AdamTensor* __restrict__ ts, AdamHyper h) { adamw_body(ts[blockIdx.y], h); }
+__global__ void adamw_single_kernel(AdamTensor t, AdamHyper h) { adamw_body(t, h); }
+
+int adamw_single(AdamTensor t, AdamHyper h, cudaStream_t s) {
+    if (t.n <= 0) return 0;
+    adamw_single_kernel<<<grid_for((size_t)t.n, 256), 256, 0, s>>>(t, h);
+    return launch_ok();
+}
+
+int adamw_multi(const AdamTensor* dev_tensors, int count, long long max_n, AdamHyper h, cudaStream_t s) {
+    if (count <= 0) return 0;
+    long long blocks = (max_n + 255) / 256, cap = (long long)num_sms() * 4;
+    unsigned gx = (unsigned)(blocks < cap ? blocks : cap);
+    if (gx == 0) gx = 1;
+    dim3 grid(gx, count);
+    adamw_kernel<<<grid, 256, 0, s>>>(dev_tensors, h);
+    return launch_ok();
+}
+
+__global__ void muon_momentum_kernel(float* m, const float* g, long long n, float mu) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        m[i] = mu * m[i] + g[i];
+}
+int muon_momentum(float* m, const float* g, long long n, float momentum, cudaStream_t s) {
+    if (n <= 0) return 0;
+    muon_momentum_kernel<<<grid_for((size_t)n, 256), 256, 0, s>>>(m, g, n, momentum);
+    return launch_ok();
+}
+
+// Modified Gram-Schmidt (reference ns_orthonom, codegen.cpp:1617-1633).
+__global__ void __launch_bounds__(1024) mgs_kernel(float* G, int M, int N) {
+    __shared__ float sh[33];
+    const bool tr = M < N;
+    const int R = tr ? N : M, Cn = tr ? M : N;
+    auto at = [&](int k, int j) -> float& { return tr ? G[(size_t)j * R + k] : G[(size_t)k * N + j]; };
+    for (int j = 0; j < Cn; j++) {
+        for (int i = 0; i < j; i++) {
+            float d = 0.f;
+            for (int k = threadIdx.x; k < R; k += blockDim.x) d += at(k, i) * at(k, j);
+            d = block_sum(d, sh);
+            for (int k = threadIdx.x; k < R; k += blockDim.x) at(k, j) -= d * at(k, i);
+            __syncthreads();
+        }
+        float nr = 0.f;
+        for (int k = threadIdx.x; k < R; k += blockDim.x) nr += at(k, j) * at(k, j);
+        nr = sqrtf(block_sum(nr, sh)) + 1e-30f;
+        for (int k = threadIdx.x; k < R; k += blockDim.x) at(k, j) /= nr;
+        __syncthreads();
+    }
+}
+int mgs_orthonormalize(float* G, int r, int c, cudaStream_t s) {
+    mgs_kernel<<<1, 1024, 0, s>>>(G, r, c);
+    return launch_ok();
+}
+
+__global__ void muon_apply_kernel(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float wi = w[i];
+        w[i] = wi - (le * o[i] + decay_lr * wi);
+        if (zero_m) m[i] = 0.f;
+    }
+}
+int muon_apply(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m, cudaStream_t s) {
+    if (n <= 0) return 0;
+    muon_apply_kernel<<<grid_for((size_t)n, 256), 256, 0, s>>>(w, o, m, n, le, decay_lr, zero_m);
+    return launch_ok();
+}
+
+__global__ void sumsq_partial_kernel(const float* __restrict__ x, long long n, float* part) {
+    __shared__ float sh[33];
+    float acc = 0.f;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        acc += x[i] * x[i];
+    acc = block_sum(acc, sh);
+    if (threadIdx.x == 0) part[blockIdx.x] = acc;
+}
+__global__ void scale_by_norm_kernel(const float* __restrict__ x, long long n, const float* part, int nparts, float eps,
+                                     float* out) {
+    __shared__ float inv;
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int i = 0; i < nparts; i++) s += part[i];
+        inv = 1.f / (sqrtf(s) + eps);
+    }
+    __syncthreads();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = x[i] * inv;
+}
+int frob_normalize(const float* x, long long n, float eps, float* out, float* scratch, cudaStream_t s) {
+    const int parts = 512;
+    sumsq_partial_kernel<<<parts, 256, 0, s>>>(x, n, scratch);
+    scale_by_norm_kernel<<<grid_for((size_t)n, 256), 256, 0, s>>>(x, n, scratch, parts, eps, out);
+    return launch_ok();
+}
+
+}  // namespace nsb

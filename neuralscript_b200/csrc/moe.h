@@ -1,0 +1,13 @@
+// Top-1 mixture-of-experts layer on the engine (router, dispatch, grouped
+// expert GEMMs, combine; backward).
+#pragma once
+#include "engine.h"
+
+namespace nsb {
+
+int moe_plan(ns_model* m, Op& op, int mmax, bool train);
+int moe_forward(ns_model* m, Op& op, int M, bool train);
+int moe_backward(ns_model* m, Op& op, int M);
+void moe_release(Op& op);
+
+}  // namespace nsb

@@ -1,0 +1,274 @@
+"""Kernel-level parity on the GPU through the C-ABI (include/ns_b200_ops.h).
+
+Tensor-core GEMMs are checked tightly by feeding operands that are already
+exactly representable in the MMA input type (bf16-rounded, or tf32 with the
+low 13 mantissa bits cleared): the products are then exact and only the fp32
+accumulation order differs from an fp64 reference, so any layout,
+descriptor or pipeline error shows up as a large error, not as noise.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import oracle_lib as R  # noqa: E402
+from neuralscript_b200 import ops as O  # noqa: E402
+
+DEV = "cuda"
+
+
+def relerr(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def tf32_trunc(t):
+    return (t.view(torch.int32) & ~0x1FFF).view(torch.float32)
+
+
+def make_operand(logical, mn, dtype):
+    """logical [rows, K] -> stored tensor (K-major: as is; MN-major: transposed)."""
+    t = logical.t().contiguous() if mn else logical.contiguous()
+    return t.to(dtype)
+
+
+GEMM_SHAPES = [(256, 128, 64), (300, 200, 96), (128, 512, 512), (1000, 1536, 512), (2048, 256, 2048),
+               (512, 512, 16384)]
+
+
+@pytest.mark.parametrize("mode", ["simt", "tf32", "bf16"])
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_layouts(mode, a_mn, b_mn, M, N, K):
+    if mode == "simt" and M * N * K > 2 ** 31:
+        pytest.skip("large SIMT case covered by smaller shapes")
+    g = torch.Generator(device=DEV).manual_seed(M * 7 + N * 3 + K)
+    A = torch.randn(M, K, device=DEV, generator=g)
+    B = torch.randn(N, K, device=DEV, generator=g)
+    if mode == "bf16":
+        A, B = A.bfloat16().float(), B.bfloat16().float()
+        dt = torch.bfloat16
+    else:
+        if mode == "tf32":
+            A, B = tf32_trunc(A), tf32_trunc(B)
+        dt = torch.float32
+    As, Bs = make_operand(A, a_mn, dt), make_operand(B, b_mn, dt)
+    lda = As.stride(0)
+    ldb = Bs.stride(0)
+    engine = O.SIMT if mode == "simt" else O.AUTO
+    C = torch.empty(M, N, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    O.gemm(As, Bs, M, N, K, lda, a_mn, ldb, b_mn, c32=C, engine=engine, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = (A.double() @ B.double().t()).cpu().numpy()
+    e = relerr(C.cpu().numpy(), ref)
+    tc = O.uses_tensor_cores(As, Bs, M, N, K, lda, a_mn, ldb, b_mn, engine)
+    if mode != "simt":
+        # aligned shapes must take the tcgen05 path
+        es = 2 if mode == "bf16" else 4
+        assert tc == ((lda * es) % 16 == 0 and (ldb * es) % 16 == 0 and N >= 32)
+    assert e < 1e-5, (e, tc)
+
+
+@pytest.mark.parametrize("mode", ["simt", "bf16"])
+def test_gemm_epilogue(mode):
+    M, N, K = 384, 256, 192
+    g = torch.Generator(device=DEV).manual_seed(5)
+    A = torch.randn(M, K, device=DEV, generator=g).bfloat16().float()
+    B = torch.randn(N, K, device=DEV, generator=g).bfloat16().float()
+    add = torch.randn(M, N, device=DEV, generator=g)
+    dt = torch.bfloat16 if mode == "bf16" else torch.float32
+    c32 = torch.empty(M, N, device=DEV)
+    c16 = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    O.gemm(A.to(dt), B.to(dt), M, N, K, K, 0, K, 0, alpha=0.5, add=add, act=6, c32=c32, c16=c16,
+           engine=O.SIMT if mode == "simt" else O.AUTO)
+    torch.cuda.synchronize()
+    pre = 0.5 * (A.double() @ B.double().t()) + add.double()
+    ref = 0.5 * pre * (1 + torch.erf(pre / 1.41421356))
+    assert relerr(c32.cpu(), ref.cpu()) < 1e-5
+    assert relerr(c16.float().cpu(), ref.cpu()) < 5e-3
+
+
+def test_gemm_simt_matches_reference_order_exactly():
+    """fp32 SIMT GEMM accumulates each output with fmaf in increasing k, as
+    the reference's scalar loop compiles; compare to the C oracle."""
+    rng = np.random.default_rng(0)
+    A = rng.uniform(-1, 1, (67, 45)).astype(np.float32)
+    B = rng.uniform(-1, 1, (45, 39)).astype(np.float32)
+    ref = R.matmul(A, B)
+    Ad = torch.from_numpy(A).to(DEV)
+    Bt = torch.from_numpy(B).to(DEV)  # B[K,N] row-major is MN-major for the (n,k) operand
+    C = torch.empty(67, 39, device=DEV)
+    O.gemm(Ad, Bt, 67, 39, 45, 45, 0, 39, 1, c32=C, engine=O.SIMT)
+    torch.cuda.synchronize()
+    got = C.cpu().numpy()
+    assert relerr(got, ref) < 1e-6
+    assert np.mean(got == ref) > 0.9  # nearly all bit-identical
+
+
+def test_layernorm_fwd_bwd():
+    for M, D in ((1000, 512), (37, 48), (64, 1024)):
+        rng = np.random.default_rng(M)
+        x = rng.normal(0.3, 2.0, (M, D)).astype(np.float32)
+        dy = rng.normal(0, 1, (M, D)).astype(np.float32)
+        add = rng.normal(0, 1, (M, D)).astype(np.float32)
+        xd, dyd, addd = (torch.from_numpy(a).to(DEV) for a in (x, dy, add))
+        y = torch.empty_like(xd)
+        y16 = torch.empty(M, D, device=DEV, dtype=torch.bfloat16)
+        O.layernorm_fwd(xd, y, y16)
+        dx = torch.empty_like(xd)
+        O.layernorm_bwd(dyd, xd, addd, dx)
+        torch.cuda.synchronize()
+        assert relerr(y.cpu(), R.layernorm(x)) < 2e-6
+        assert relerr(y16.float().cpu(), R.layernorm(x)) < 5e-3
+        assert relerr(dx.cpu(), R.layernorm_grad(dy, x) + add) < 2e-6
+
+
+def test_embedding_fwd_bwd_deterministic_and_exact():
+    V, D, M = 1000, 512, 16384
+    rng = np.random.default_rng(1)
+    W = rng.normal(0, 1, (V, D)).astype(np.float32)
+    ids = rng.integers(0, V, M).astype(np.float32)
+    ids[:5] = [-1, V, 3.7, -0.5, 2.2]          # out of range and fractional
+    ids[100:160] = 7                           # one bucket larger than a warp
+    dout = rng.normal(0, 1, (M, D)).astype(np.float32)
+    Wd, idd, dd = (torch.from_numpy(a).to(DEV) for a in (W, ids, dout))
+    out = torch.empty(M, D, device=DEV)
+    O.embedding_fwd(Wd, idd, out32=out)
+    dW1 = torch.empty(V, D, device=DEV)
+    dW2 = torch.empty(V, D, device=DEV)
+    O.embedding_bwd(dd, idd, V, dW1)
+    O.embedding_bwd(dd, idd, V, dW2)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), R.embedding(W, ids))
+    ref = R.embedding_grad_w(dout, ids, V)
+    assert np.array_equal(dW1.cpu().numpy(), ref)  # same row order, same additions
+    assert torch.equal(dW1, dW2)
+
+
+def attn_reference(qkv, B, S, H, D, dctx=None):
+    dh = D // H
+    q = qkv[:, :D].reshape(B, S, H, dh).transpose(0, 2, 1, 3)
+    k = qkv[:, D:2 * D].reshape(B, S, H, dh).transpose(0, 2, 1, 3)
+    v = qkv[:, 2 * D:].reshape(B, S, H, dh).transpose(0, 2, 1, 3)
+    sc = (q @ k.transpose(0, 1, 3, 2)) * (1.0 / np.sqrt(dh))
+    sc = sc - sc.max(-1, keepdims=True)
+    p = np.exp(sc)
+    p /= p.sum(-1, keepdims=True)
+    o = p @ v
+    ctx = o.transpose(0, 2, 1, 3).reshape(B * S, D)
+    if dctx is None:
+        return ctx, None
+    g = dctx.reshape(B, S, H, dh).transpose(0, 2, 1, 3)
+    dv = p.transpose(0, 1, 3, 2) @ g
+    dp = g @ v.transpose(0, 1, 3, 2)
+    ds = p * (dp - (dp * p).sum(-1, keepdims=True))
+    dq = ds @ k / np.sqrt(dh)
+    dk = ds.transpose(0, 1, 3, 2) @ q / np.sqrt(dh)
+    flat = lambda t: t.transpose(0, 2, 1, 3).reshape(B * S, D)
+    return ctx, np.concatenate([flat(dq), flat(dk), flat(dv)], axis=1)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("B,S,H,D", [(2, 64, 2, 64), (3, 8, 4, 16), (4, 256, 8, 512), (2, 100, 2, 6), (1, 70, 1, 128)])
+def test_attention(dtype, B, S, H, D):
+    rng = np.random.default_rng(S + D)
+    qkv = rng.normal(0, 1, (B * S, 3 * D)).astype(np.float32)
+    dctx = rng.normal(0, 1, (B * S, D)).astype(np.float32)
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    if dtype == "bf16":
+        qkv = torch.from_numpy(qkv).bfloat16().float().numpy()
+        dctx = torch.from_numpy(dctx).bfloat16().float().numpy()
+    ref_ctx, ref_d = attn_reference(qkv.astype(np.float64), B, S, H, D, dctx.astype(np.float64))
+    qd = torch.from_numpy(qkv).to(DEV).to(tdt)
+    ctx = torch.empty(B * S, D, device=DEV, dtype=tdt)
+    lse = torch.empty(B * H * S, device=DEV)
+    O.attention_fwd(B, S, H, D, qd, ctx, lse)
+    gd = torch.from_numpy(dctx).to(DEV).to(tdt)
+    dq = torch.empty(B * S, 3 * D, device=DEV, dtype=tdt)
+    dvec = torch.empty(B * H * S, device=DEV)
+    O.attention_bwd(B, S, H, D, qd, ctx, lse, gd, dq, dvec)
+    torch.cuda.synchronize()
+    tol = 1e-5 if dtype == "f32" else 8e-3
+    assert relerr(ctx.float().cpu(), ref_ctx) < tol
+    assert relerr(dq.float().cpu(), ref_d) < (1e-5 if dtype == "f32" else 2e-2)
+
+
+def test_attention_core_matches_oracle_attention():
+    """Through projections: oracle ns_attention_fwd/bwd restatement vs
+    projections in fp64 + the kernel."""
+    B, S, H, D = 2, 64, 2, 64
+    rng = np.random.default_rng(9)
+    x = rng.normal(0, 1, (B * S, D)).astype(np.float32)
+    Ws = [rng.normal(0, 0.25, (D, D)).astype(np.float32) for _ in range(4)]
+    ref = R.attention_fwd(x, *Ws, H, S)
+    qkv = np.concatenate([x.astype(np.float64) @ W for W in Ws[:3]], axis=1).astype(np.float32)
+    qd = torch.from_numpy(qkv).to(DEV)
+    ctx = torch.empty(B * S, D, device=DEV)
+    lse = torch.empty(B * H * S, device=DEV)
+    O.attention_fwd(B, S, H, D, qd, ctx, lse)
+    torch.cuda.synchronize()
+    out = ctx.cpu().numpy().astype(np.float64) @ Ws[3]
+    assert relerr(out, ref) < 1e-5
+
+
+def test_cross_entropy():
+    M, Cc = 300, 8192
+    rng = np.random.default_rng(3)
+    logits = rng.normal(0, 2, (M, Cc)).astype(np.float32)
+    t = rng.integers(0, Cc, M)
+    y = np.zeros((M, Cc), np.float32)
+    y[np.arange(M), t] = 1
+    ld, yd = torch.from_numpy(logits).to(DEV), torch.from_numpy(y).to(DEV)
+    rl = torch.empty(M, device=DEV)
+    d = torch.empty(M, Cc, device=DEV)
+    O.cross_entropy(ld, labels=yd, row_loss=rl, d32=d)
+    rl2 = torch.empty(M, device=DEV)
+    d2 = torch.empty(M, Cc, device=DEV)
+    O.cross_entropy(ld, targets=torch.from_numpy(t.astype(np.int32)).to(DEV), row_loss=rl2, d32=d2)
+    tot = torch.empty(1, device=DEV)
+    O.reduce_sum(rl, 1.0 / M, tot)
+    torch.cuda.synchronize()
+    assert relerr(d.cpu(), R.loss_grad(logits, y)) < 1e-6
+    assert relerr(rl.cpu(), R.cross_entropy_rows(logits, y)) < 1e-6
+    assert torch.equal(d, d2) and torch.equal(rl, rl2)
+    assert abs(tot.item() - R.cross_entropy(logits, y)) < 1e-5 * abs(R.cross_entropy(logits, y))
+
+
+def test_adamw_matches_oracle():
+    n = 100003
+    rng = np.random.default_rng(4)
+    w, g = rng.normal(0, 1, n).astype(np.float32), rng.normal(0, 1, n).astype(np.float32)
+    m, v = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    wd, gd, md, vd = (torch.from_numpy(a.copy()).to(DEV) for a in (w, g, m, v))
+    for t in (1, 2, 3):
+        O.adamw(wd, gd, md, vd, t, 1e-3, 0.9, 0.95, 0.1, 0.05, 1e-8, 0.1)
+        R.lib.orc_adamw_step(w, g, m, v, n, t, 1e-3, 0.9, 0.95, 0.1, 0.05, 1e-8, 0.1)
+    torch.cuda.synchronize()
+    assert relerr(wd.cpu(), w) < 1e-6 and relerr(md.cpu(), m) < 1e-6 and relerr(vd.cpu(), v) < 1e-6
+
+
+@pytest.mark.parametrize("r,c", [(12, 9), (5, 11), (64, 32)])
+def test_mgs(r, c):
+    G = np.random.default_rng(r * c).normal(0, 1, (r, c)).astype(np.float32)
+    Gd = torch.from_numpy(G.copy()).to(DEV)
+    O.mgs(Gd)
+    torch.cuda.synchronize()
+    assert relerr(Gd.cpu(), R.orthonom(G)) < 1e-5
+
+
+def test_activations():
+    x = np.linspace(-6, 6, 4001).astype(np.float32)
+    dy = np.random.default_rng(0).normal(0, 1, x.size).astype(np.float32)
+    xd, dyd = torch.from_numpy(x).to(DEV), torch.from_numpy(dy).to(DEV)
+    for code in range(7):
+        y = torch.empty_like(xd)
+        O.act_fwd(xd, code, y)
+        d = torch.empty_like(xd)
+        O.act_bwd(dyd, xd, code, d)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(y.cpu().numpy(), R.act(x, code), rtol=2e-6, atol=1e-6)
+        np.testing.assert_allclose(d.cpu().numpy(), R.act_grad(dy, x, code), rtol=2e-6, atol=1e-6)
