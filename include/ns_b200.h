@@ -70,12 +70,19 @@ int nsb_get_precision(const ns_model* m);
 int nsb_runtime_train_step_idx(ns_model* m, const float* input, const int* targets, size_t input_numel,
                                float* loss_out, float lr);
 
-/* Device-resident variants: pointers are device memory, `stream` a
- * cudaStream_t (NULL = the model's stream); no host synchronisation except
- * for *loss_out (may be NULL to skip it). */
+/* Device-resident variants: pointers are device memory, `stream` the
+ * caller's cudaStream_t (NULL = the legacy default stream). The work is
+ * ordered after prior work on `stream`, and later work on `stream` sees the
+ * outputs. eval returns without host synchronisation; the train step
+ * synchronises (it reports device errors and, if loss_out is not NULL, the
+ * loss). */
 int nsb_eval_infer_device(ns_model* m, const float* d_input, float* d_output, size_t input_numel, void* stream);
 int nsb_train_step_device(ns_model* m, const float* d_input, const float* d_labels, const int* d_targets,
                           size_t input_numel, float* loss_out, float lr, void* stream);
+
+/* Gradient blob of the last train step (same layout as the weights; summed
+ * over ranks when data-parallel), copied to host `out` of n floats. */
+int nsb_model_get_gradients(const ns_model* m, float* out, size_t n);
 
 /* Number of kernel launches issued by the last public call on this model. */
 long long nsb_last_launch_count(const ns_model* m);

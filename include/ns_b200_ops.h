@@ -94,6 +94,15 @@ int nsb_op_adamw(float* w, const float* g, float* m, float* v, long long n, long
  * ns_orthonom (codegen.cpp:1617-1633). */
 int nsb_op_mgs(float* G, int r, int c, void* stream);
 
+/* Top-1 MoE router: logits x.Wg accumulated with fmaf in increasing k (the
+ * reference's scalar order, so the logits are bit-identical to its CPU emit),
+ * softmax over live experts (active[e] != 0; NULL = all live), best = first
+ * maximum of the exp'd logits (-1 if none live), pb = its probability, probs
+ * [M,E] (may be NULL) the live softmax. Replaces the routing of ns_moe_kernel
+ * (cuda_backend.cpp:371-407) and ns_moe_fwd (codegen.cpp:1915-1931). */
+int nsb_op_moe_route(const float* x, const float* Wg, const unsigned char* active, int M, int D, int E, int* best,
+                     float* pb, float* probs, void* stream);
+
 /* Activation forward / derivative product. Replaces ns_act_kernel /
  * ns_act_grad_kernel (cuda_backend.cpp:80-84, 468-472). */
 int nsb_op_act_fwd(const float* x, size_t n, int act, float* out32, void* out16, void* stream);

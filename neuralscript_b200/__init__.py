@@ -78,6 +78,7 @@ def lib() -> C.CDLL:
         "nsb_train_step_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, _f32p,
                                             C.c_float, C.c_void_p]),
         "nsb_last_launch_count": (C.c_longlong, [C.c_void_p]),
+        "nsb_model_get_gradients": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
         "nsb_dist_unique_id": (C.c_int, [C.c_void_p]),
         "nsb_dist_init": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
         "nsb_last_error": (C.c_char_p, []),
@@ -193,6 +194,12 @@ class Model:
         _check(lib().nsb_model_get_weights(self._h, _ptr(out), out.size), "ns_model_get_weights")
         return out
 
+    def get_gradients(self) -> np.ndarray:
+        """Gradients of the last train step, in weight-blob layout."""
+        out = np.empty(self.weight_count(), np.float32)
+        _check(lib().nsb_model_get_gradients(self._h, _ptr(out), out.size), "get_gradients")
+        return out
+
     def layout(self):
         return spec_layout(self.spec_text)
 
@@ -281,8 +288,3 @@ class RuntimeLib:
     def __getattr__(self, item):
         return getattr(self.L, item)
 
-
-def ops():
-    """Kernel-level bindings (include/ns_b200_ops.h)."""
-    from . import ops as _ops
-    return _ops

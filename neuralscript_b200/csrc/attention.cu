@@ -310,6 +310,7 @@ static int bwd_launch(const AttnArgs& a, cudaStream_t s) {
 int attention_fwd(const AttnArgs& a, cudaStream_t s) {
     if (a.B <= 0 || a.S <= 0) return 0;
     if (a.dh > 128) return -1;
+    if (attention_tc_supported(a)) return attention_tc_fwd(a, s, a.err);
     const bool bf = a.dtype == kBF16;
     if (a.dh <= 32) return bf ? fwd_launch<__nv_bfloat16, 32>(a, s) : fwd_launch<float, 32>(a, s);
     if (a.dh <= 64) return bf ? fwd_launch<__nv_bfloat16, 64>(a, s) : fwd_launch<float, 64>(a, s);

@@ -18,9 +18,13 @@ struct AttnArgs {
     void* dqkv = nullptr;   // [M, ld] dQ | dK | dV
     long long ld_dqkv = 0;
     float* dvec = nullptr;  // [B*H*S] scratch: dO_i . O_i
+    int* err = nullptr;     // device error word for bounded waits (tensor-core path)
 };
 
 int attention_fwd(const AttnArgs& a, cudaStream_t s);
+// tcgen05 forward (attention_tc.cu): bf16, head dim 64, S <= 256
+bool attention_tc_supported(const AttnArgs& a);
+int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err);
 int attention_bwd(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace nsb

@@ -22,7 +22,10 @@ enum DevErr : int {
 enum DType : int { kF32 = 0, kBF16 = 1 };
 
 // Activation codes (reference ns_act2, src/codegen/codegen.cpp:1244-1255).
-enum Act : int { kIdentity = 0, kRelu = 1, kLeaky = 2, kSigmoid = 3, kTanh = 4, kSilu = 5, kGelu = 6 };
+enum Act : int { kIdentity = 0, kRelu = 1, kLeaky = 2, kSigmoid = 3, kTanh = 4, kSilu = 5, kGelu = 6, kGeluMoe = 7 };
+// kGeluMoe is the exact-erf GELU as written in the reference's MoE helpers
+// (src/codegen/codegen.cpp:1938, 1430-1431): multiplies by 0.7071067811865476f
+// where ns_act2 divides by 1.41421356f.
 
 __host__ __device__ __forceinline__ float act_fwd(float x, int code) {
     switch (code) {
@@ -32,6 +35,7 @@ __host__ __device__ __forceinline__ float act_fwd(float x, int code) {
         case kTanh: return tanhf(x);
         case kSilu: return x / (1.f + expf(-x));
         case kGelu: return 0.5f * x * (1.f + erff(x / 1.41421356f));
+        case kGeluMoe: return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
         default: return x;
     }
 }
@@ -58,6 +62,8 @@ __host__ __device__ __forceinline__ float act_deriv(float x, int code) {
             float p = 0.5f * (1.f + erff(u));
             return p + x * expf(-u * u) / 2.50662827f;
         }
+        case kGeluMoe:
+            return 0.5f * (1.f + erff(x * 0.7071067811865476f)) + x * expf(-x * x * 0.5f) * 0.3989422804014327f;
         default: return 1.f;
     }
 }

@@ -370,6 +370,7 @@ static int plan(ns_model* m, int M, bool train) {
         if (v.need_h16) v.h16 = PA(__nv_bfloat16, R * v.cols);
     }
     m->vals[0].f32 = m->d_in;
+    if (m->vals[0].need_h16) m->vals[0].h16 = PA(__nv_bfloat16, R * s.in_cols);
     for (size_t vi = 1; vi < m->vals.size(); vi++) {
         Val& v = m->vals[vi];
         if (v.alias_of >= 0) {
@@ -463,6 +464,10 @@ static const void* as_operand(ns_model* m, const Val& v) { return m->wdt == kBF1
 // ---------------------------------------------------------------------------
 static int forward(ns_model* m, int M, bool train) {
     const Spec& s = m->spec;
+    if (m->vals[0].h16) {  // the raw input feeds a bf16 GEMM
+        launch_counter() += 1;
+        if (f32_to_bf16(m->d_in, (size_t)M * s.in_cols, m->vals[0].h16, m->stream)) return fail("input cast failed");
+    }
     for (size_t oi = 0; oi < m->ops.size(); oi++) {
         Op& op = m->ops[oi];
         if (op.skip) continue;
@@ -536,6 +541,7 @@ static int forward(ns_model* m, int M, bool train) {
                 a.ctx = op.ctx;
                 a.ld_ctx = D;
                 a.lse = op.lse;
+                a.err = m->d_err;
                 launch_counter() += 1;
                 if ((rc = attention_fwd(a, m->stream))) {
                     rc = fail("attention launch failed");
@@ -1191,6 +1197,12 @@ int nsb_get_precision(const ns_model* m) { return m ? m->precision : -1; }
 
 long long nsb_last_launch_count(const ns_model* m) { return m ? m->launches : 0; }
 
+int nsb_model_get_gradients(const ns_model* m, float* out, size_t n) {
+    if (!m || !out || n != m->spec.total) return -1;
+    cudaStreamSynchronize(m->stream);
+    return cudaMemcpy(out, m->d_g, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+
 static int rows_of(const ns_model* m, size_t input_numel) {
     return (int)(input_numel / (size_t)m->spec.in_cols);
 }
@@ -1202,7 +1214,9 @@ int nsb_eval_infer_device(ns_model* m, const float* d_input, float* d_output, si
     const int M = rows_of(m, input_numel);
     if (M <= 0) return 0;
     if (plan(m, M, false)) return -1;
-    cudaStream_t us = stream ? (cudaStream_t)stream : m->stream;
+    // the caller's stream (NULL = the legacy default stream); the engine runs
+    // on its own stream, ordered after and before the caller's by events
+    cudaStream_t us = stream ? (cudaStream_t)stream : cudaStreamLegacy;
     cudaEvent_t ev;
     if (us != m->stream) {
         cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
@@ -1284,8 +1298,8 @@ static int train_entry(ns_model* m, const float* input, const float* labels, con
     if (!input || (!labels && !targets)) return fail("null input/labels");
     if (plan(m, M, true)) return -1;
     cudaMemcpyKind k = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    cudaStream_t us = stream ? (cudaStream_t)stream : m->stream;
-    if (device_ptrs && us != m->stream) cudaStreamSynchronize(us);
+    cudaStream_t us = stream ? (cudaStream_t)stream : cudaStreamLegacy;
+    if (device_ptrs) cudaStreamSynchronize(us);  // inputs produced on the caller's stream
     cudaMemcpyAsync(m->d_in, input, sizeof(float) * (size_t)M * m->spec.in_cols, k, m->stream);
     const float* dl = nullptr;
     const int* dt = nullptr;

@@ -80,6 +80,7 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
         for (int j = 0; j < 32; j++) v[j] *= s;
     }
     if (ep.dz) {
+        float z[32];
         if (ep.dz_dtype == kBF16) {
             const uint4* a = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ep.dz) +
                                                             (size_t)row * ep.ld_dz + col0);
@@ -88,7 +89,7 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
                 uint4 t = a[j];
                 const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&t);
 #pragma unroll
-                for (int q = 0; q < 8; q++) v[8 * j + q] *= act_deriv(bf2f(h[q]), ep.dz_act);
+                for (int q = 0; q < 8; q++) z[8 * j + q] = bf2f(h[q]);
             }
         } else {
             const float4* a = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ep.dz) +
@@ -96,11 +97,24 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 float4 t = a[j];
-                v[4 * j] *= act_deriv(t.x, ep.dz_act);
-                v[4 * j + 1] *= act_deriv(t.y, ep.dz_act);
-                v[4 * j + 2] *= act_deriv(t.z, ep.dz_act);
-                v[4 * j + 3] *= act_deriv(t.w, ep.dz_act);
+                z[4 * j] = t.x;
+                z[4 * j + 1] = t.y;
+                z[4 * j + 2] = t.z;
+                z[4 * j + 3] = t.w;
             }
+        }
+        switch (ep.dz_act) {
+            case kRelu:
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], kRelu);
+                break;
+            case kGelu:
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], kGelu);
+                break;
+            default:
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], ep.dz_act);
         }
     }
     if (ep.z) {
@@ -120,9 +134,24 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
             for (int j = 0; j < 8; j++) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
     }
-    if (ep.act) {
+    switch (ep.act) {
+        case kIdentity:
+            break;
+        case kRelu:
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], ep.act);
+            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], kRelu);
+            break;
+        case kGelu:
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], kGelu);
+            break;
+        case kGeluMoe:
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], kGeluMoe);
+            break;
+        default:
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], ep.act);
     }
     int orow = ep.out_rows ? ep.out_rows[row] : row;
     if (ep.c32) {
@@ -157,6 +186,7 @@ struct TcParams {
     // grouped: group g owns rows [seg[g], seg[g+1]); B rows offset g * N
     int groups;
     const int* seg;
+    const int* seg_end;
     int max_m_tiles_per_group;
 };
 
@@ -172,6 +202,11 @@ struct TcCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = (BN == 256) ? 4 : 6;
     static constexpr int TMEM_COLS = 2 * BN;
+    // MN-major operands: 128-byte chunks along M/N, BK k-rows each. bf16 uses
+    // the 16-byte-granule 128B swizzle (8-row atoms, SBO 1024); tf32 needs the
+    // 32-byte-granule variant (4-row atoms, SBO 512).
+    static constexpr uint32_t MN_LAYOUT = TF32 ? 1 : 2;
+    static constexpr uint32_t MN_SBO = TF32 ? 512 : 1024;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -189,7 +224,7 @@ __device__ __forceinline__ bool tc_decode(const TcParams& p, int u, int BN, int&
         int t = tile % per_group;
         m_blk = t / p.n_tiles;
         n_blk = t % p.n_tiles;
-        int s0 = p.seg[g], s1 = p.seg[g + 1];
+        int s0 = p.seg[g], s1 = p.seg_end ? p.seg_end[g] : p.seg[g + 1];
         m0 = s0 + m_blk * 128;
         if (m0 >= s1) return false;
         row_end = s1;
@@ -206,8 +241,11 @@ __device__ __forceinline__ bool tc_decode(const TcParams& p, int u, int BN, int&
     return true;
 }
 
+constexpr int kEpiWarps = 8;                    // two per TMEM lane quarter
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + epilogue
+
 template <int BN, bool TF32, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const TcParams p) {
     using C = TcCfg<BN, TF32>;
     constexpr uint32_t IDESC = ptx::instr_desc(TF32 ? 2 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0, C::BM, BN);
@@ -227,7 +265,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int a = 0; a < 2; a++) {
             ptx::mbar_init(&acc_full[a], 1);
-            ptx::mbar_init(&acc_empty[a], 128);
+            ptx::mbar_init(&acc_empty[a], 32 * kEpiWarps);
         }
         ptx::fence_mbar_init();
     }
@@ -311,10 +349,12 @@ __global__ void __launch_bounds__(192, 1)
                     const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
-                        uint64_t ad = A_MN ? ptx::smem_desc_sw128(sa + k * C::KSTEP * 128, C::BK * 128, 1024)
-                                           : ptx::smem_desc_sw128(sa + k * 32, 16, 1024);
-                        uint64_t bd = B_MN ? ptx::smem_desc_sw128(sb + k * C::KSTEP * 128, C::BK * 128, 1024)
-                                           : ptx::smem_desc_sw128(sb + k * 32, 16, 1024);
+                        uint64_t ad =
+                            A_MN ? ptx::smem_desc(sa + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
+                                 : ptx::smem_desc(sa + k * 32, 16, 1024, 2);
+                        uint64_t bd =
+                            B_MN ? ptx::smem_desc(sb + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
+                                 : ptx::smem_desc(sb + k * 32, 16, 1024, 2);
                         uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
                         if (TF32) ptx::mma_tf32(d, ad, bd, IDESC, accum);
                         else ptx::mma_bf16(d, ad, bd, IDESC, accum);
@@ -332,9 +372,13 @@ __global__ void __launch_bounds__(192, 1)
         mma_done:;
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int lane_grp = warp & 3;  // TMEM lanes [32*lane_grp, +32)
+        // ---------------- epilogue (warps 2..9) ----------------
+        // warp w reads TMEM lanes [32*(w%4), +32) (its hardware lane quarter)
+        // and half (w-2)/4 of the tile's columns
+        const int lane_grp = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int r_in_tile = lane_grp * 32 + lane;
+        constexpr int HALF_COLS = BN / 2;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
@@ -345,7 +389,7 @@ __global__ void __launch_bounds__(192, 1)
             const int row = m0 + r_in_tile;
             const bool row_ok = row < row_end;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = half * HALF_COLS; c < (half + 1) * HALF_COLS; c += 32) {
                 uint32_t r[32];
                 ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + acc * BN + c, r);
                 ptx::tmem_ld_wait();
@@ -354,19 +398,24 @@ __global__ void __launch_bounds__(192, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                const bool full = p.vec_ok && col0 + 32 <= p.N;
                 if (p.splits > 1) {
                     float* w = p.workspace + ((size_t)split * p.M + row) * p.N + col0;
-                    if (p.vec_ok && col0 + 32 <= p.N) {
+                    if (full) {
 #pragma unroll
                         for (int j = 0; j < 8; j++)
                             reinterpret_cast<float4*>(w)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                     } else {
-                        for (int j = 0; j < 32 && col0 + j < p.N; j++) w[j] = v[j];
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N) w[j] = v[j];
                     }
-                } else if (p.vec_ok && col0 + 32 <= p.N) {
+                } else if (full) {
                     epi_apply32_vec(p.ep, row, col0, v);
                 } else {
-                    for (int j = 0; j < 32 && col0 + j < p.N; j++) epi_apply(p.ep, row, col0 + j, v[j]);
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (col0 + j < p.N) epi_apply(p.ep, row, col0 + j, v[j]);
                 }
             }
             ptx::tc_fence_before();
@@ -405,7 +454,10 @@ struct SimtParams {
     Epilogue ep;
     int groups;
     const int* seg;
+    const int* seg_end;
     long long b_group_stride;
+    bool group_k;
+    long long c_group_stride;
 };
 
 __device__ __forceinline__ float ld_op(const GemmOperand& o, long long i, long long k) {
@@ -420,29 +472,39 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
     const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
     int g = 0, row_end = p.M;
     GemmOperand b = p.b;
-    if (p.groups > 1) {
-        // blockIdx.z = group; rows [seg[g], seg[g+1])
+    Epilogue ep = p.ep;
+    int kbeg = 0, kend = p.K;
+    int mbase = m0;
+    if (p.groups > 1 && !p.group_k) {
+        // blockIdx.z = group; rows [seg[g], seg_end[g])
         g = blockIdx.z;
-        int s0 = p.seg[g], s1 = p.seg[g + 1];
+        int s0 = p.seg[g], s1 = p.seg_end ? p.seg_end[g] : p.seg[g + 1];
         if (s0 + m0 >= s1) return;
         row_end = s1;
+        mbase = s0 + m0;
         b.ptr = (const char*)b.ptr + (size_t)g * p.b_group_stride * (b.dtype == kBF16 ? 2 : 4);
+    } else if (p.group_k) {
+        // blockIdx.z = group; reduce k in [seg[g], seg_end[g]); C block g
+        g = blockIdx.z;
+        kbeg = p.seg[g];
+        kend = p.seg_end ? p.seg_end[g] : p.seg[g + 1];
+        if (ep.c32) ep.c32 += (size_t)g * p.c_group_stride;
+        if (ep.c16) ep.c16 += (size_t)g * p.c_group_stride;
     }
-    const int mbase = (p.groups > 1 ? p.seg[g] : 0) + m0;
     float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
-    for (int k0 = 0; k0 < p.K; k0 += 16) {
+    for (int k0 = kbeg; k0 < kend; k0 += 16) {
         for (int e = threadIdx.x; e < 16 * 64; e += 256) {
             int kk = e / 64, ii = e % 64;
             int gm = mbase + ii, gk = k0 + kk, gn = n0 + ii;
-            As[kk][ii] = (gm < row_end && gk < p.K) ? ld_op(p.a, gm, gk) : 0.f;
-            Bs[kk][ii] = (gn < p.N && gk < p.K) ? ld_op(b, gn, gk) : 0.f;
+            As[kk][ii] = (gm < row_end && gk < kend) ? ld_op(p.a, gm, gk) : 0.f;
+            Bs[kk][ii] = (gn < p.N && gk < kend) ? ld_op(b, gn, gk) : 0.f;
         }
         __syncthreads();
-        const int kmax = min(16, p.K - k0);
+        const int kmax = min(16, kend - k0);
         for (int kk = 0; kk < kmax; kk++) {
             float av[4], bv[4];
 #pragma unroll
@@ -463,7 +525,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             int col = n0 + tx + 16 * j;
-            if (col < p.N) epi_apply(p.ep, row, col, acc[i][j]);
+            if (col < p.N) epi_apply(ep, row, col, acc[i][j]);
         }
     }
 }
@@ -489,9 +551,10 @@ static EncodeTiledFn get_encode() {
 }
 
 // 2D map over a row-major [outer, inner] array with leading dimension ld
-// (elements); box {box_inner, box_outer}; 128-byte swizzle.
+// (elements); box {box_inner, box_outer}; 128-byte swizzle (32-byte granules
+// when atom32: MN-major tf32 operands).
 static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner, long long outer, long long ld,
-                     int box_inner, int box_outer) {
+                     int box_inner, int box_outer, bool atom32 = false) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
     const int es = dtype == kBF16 ? 2 : 4;
@@ -501,7 +564,8 @@ static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                      const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -519,6 +583,9 @@ bool gemm_uses_tensor_cores(const GemmDesc& d) {
     if (d.M <= 0 || d.N <= 0 || d.K <= 0) return false;
     // very narrow outputs waste a 128-wide tile; the SIMT kernel is cheaper
     if (d.N < 32) return false;
+    // grouped: only row groups with a K-major B (one 2D tensor map)
+    if (d.group_k) return false;
+    if (d.groups > 1 && (d.b.mn_major || d.b_group_stride != (long long)d.N * d.b.ld)) return false;
     return true;
 }
 
@@ -560,7 +627,7 @@ static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const
     }
     int grid = min(p.total_units, num_sms());
     if (grid <= 0) return cudaSuccess;
-    k<<<grid, 192, C::SMEM, s>>>(ta, tb, p);
+    k<<<grid, kTcThreads, C::SMEM, s>>>(ta, tb, p);
     return cudaGetLastError();
 }
 
@@ -595,11 +662,11 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     // A: M x K. K-major -> array [M][ld] (inner K); MN-major -> [K][ld] (inner M)
     bool ok;
     if (!d.a.mn_major) ok = make_map(&ta, d.a.ptr, d.a.dtype, d.K, d.M, d.a.ld, bk, 128);
-    else ok = make_map(&ta, d.a.ptr, d.a.dtype, d.M, d.K, d.a.ld, chunk, bk);
+    else ok = make_map(&ta, d.a.ptr, d.a.dtype, d.M, d.K, d.a.ld, chunk, bk, tf32);
     if (!ok) return -2;
     const long long brows = (long long)d.N * d.groups;
     if (!d.b.mn_major) ok = make_map(&tb, d.b.ptr, d.b.dtype, d.K, brows, d.b.ld, bk, bn);
-    else ok = make_map(&tb, d.b.ptr, d.b.dtype, brows, d.K, d.b.ld, chunk, bk);
+    else ok = make_map(&tb, d.b.ptr, d.b.dtype, brows, d.K, d.b.ld, chunk, bk, tf32);
     if (!ok) return -2;
 
     TcParams p;
@@ -614,6 +681,7 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     p.err = dev_err;
     p.groups = d.groups;
     p.seg = d.seg;
+    p.seg_end = d.seg_end;
     p.max_m_tiles_per_group = p.m_tiles;
     p.workspace = nullptr;
     if (p.splits > 1) {
@@ -656,7 +724,10 @@ static int gemm_simt(const GemmDesc& d, cudaStream_t s) {
     p.ep = d.ep;
     p.groups = d.groups;
     p.seg = d.seg;
+    p.seg_end = d.seg_end;
     p.b_group_stride = d.b_group_stride;
+    p.group_k = d.group_k;
+    p.c_group_stride = d.c_group_stride;
     dim3 grid((d.N + 63) / 64, (d.M + 63) / 64, d.groups);
     if (grid.x == 0 || grid.y == 0) return 0;
     gemm_simt_kernel<<<grid, 256, 0, s>>>(p);
@@ -666,6 +737,8 @@ static int gemm_simt(const GemmDesc& d, cudaStream_t s) {
 int gemm(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     if (d.M < 0 || d.N < 0 || d.K < 0) return -1;
     if (d.M == 0 || d.N == 0) return 0;
+    if (!d.a.ptr || !d.b.ptr || d.a.ld <= 0 || d.b.ld <= 0) return -1;
+    if (!d.ep.c32 && !d.ep.c16 && !d.ep.z) return -1;
     if (d.engine == kEngineTensor && !gemm_uses_tensor_cores(d)) return -1;
     if (gemm_uses_tensor_cores(d)) return gemm_tc(d, s, dev_err);
     return gemm_simt(d, s);

@@ -40,7 +40,12 @@ struct GemmDesc {
     // the B matrix at b.ptr + g * b_group_stride elements.
     int groups = 1;
     const int* seg = nullptr;
+    const int* seg_end = nullptr;  // optional: rows [seg[g], seg_end[g]) are real (the rest padding)
     long long b_group_stride = 0;
+    // Grouped over K instead (per-expert weight gradients): group g reduces
+    // k in [seg[g], seg_end[g]) and writes C at ep.c32 + g * c_group_stride.
+    bool group_k = false;
+    long long c_group_stride = 0;
     // Split-K workspace (fp32, >= splits * M * N floats); splits chosen by
     // the dispatcher when 0.
     float* workspace = nullptr;

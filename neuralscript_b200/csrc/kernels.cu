@@ -165,13 +165,16 @@ __global__ void emb_fill_kernel(const float* __restrict__ ids, int M, int V, con
 }
 
 // One warp per vocabulary row: gather the rows that hit it, order them by
-// row index, and sum their gradients in that order.
+// row index, and sum their gradients in that order. The sorted row ids are
+// staged in shared memory so the column loops (where only some lanes may be
+// active for narrow rows) never shuffle across inactive lanes.
 __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, const int* __restrict__ count,
                                   const int* __restrict__ offset, const int* __restrict__ rows,
                                   float* __restrict__ dW, int vec) {
+    __shared__ int sorted[8][32];  // blockDim.x == 256
     const int warps = blockDim.x >> 5;
-    const int lane = threadIdx.x & 31;
-    for (int v = blockIdx.x * warps + (threadIdx.x >> 5); v < V; v += gridDim.x * warps) {
+    const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+    for (int v = blockIdx.x * warps + wi; v < V; v += gridDim.x * warps) {
         const int n = count[v];
         const int* rv = rows + offset[v];
         float* dst = dW + (size_t)v * D;
@@ -181,7 +184,7 @@ __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, 
         }
         if (n <= 32) {
             int key = lane < n ? rv[lane] : 0x7fffffff;
-            // warp bitonic sort, ascending
+            // warp bitonic sort, ascending (all 32 lanes participate)
 #pragma unroll
             for (int k = 2; k <= 32; k <<= 1) {
 #pragma unroll
@@ -193,27 +196,25 @@ __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, 
                     key = (lower == up) ? mn : mx;
                 }
             }
+            sorted[wi][lane] = key;
+            __syncwarp();
             if (vec) {
                 for (int c = lane * 4; c < D; c += 128) {
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (int q = 0; q < n; q++) {
-                        int r = __shfl_sync(kFull, key, q);
-                        float4 t = *reinterpret_cast<const float4*>(dout + (size_t)r * D + c);
+                        float4 t = *reinterpret_cast<const float4*>(dout + (size_t)sorted[wi][q] * D + c);
                         acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
                     }
                     *reinterpret_cast<float4*>(dst + c) = acc;
                 }
             } else {
-                for (int c0 = 0; c0 < D; c0 += 32) {
-                    int c = c0 + lane;
+                for (int c = lane; c < D; c += 32) {
                     float acc = 0.f;
-                    for (int q = 0; q < n; q++) {
-                        int r = __shfl_sync(kFull, key, q);
-                        if (c < D) acc += dout[(size_t)r * D + c];
-                    }
-                    if (c < D) dst[c] = acc;
+                    for (int q = 0; q < n; q++) acc += dout[(size_t)sorted[wi][q] * D + c];
+                    dst[c] = acc;
                 }
             }
+            __syncwarp();
         } else {
             // large bucket: repeatedly take the next-smallest row index
             for (int c = lane; c < D; c += 32) dst[c] = 0.f;
@@ -229,6 +230,7 @@ __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, 
                 for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(kFull, cand, o));
                 last = cand;
                 for (int c = lane; c < D; c += 32) dst[c] += dout[(size_t)cand * D + c];
+                __syncwarp();
             }
         }
     }

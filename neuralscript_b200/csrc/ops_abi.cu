@@ -8,6 +8,7 @@
 #include "engine.h"
 #include "gemm.h"
 #include "kernels.h"
+#include "moe.h"
 
 using namespace nsb;
 
@@ -154,6 +155,12 @@ int nsb_op_adamw(float* w, const float* g, float* m, float* v, long long n, long
 }
 
 int nsb_op_mgs(float* G, int r, int c, void* stream) { return mgs_orthonormalize(G, r, c, (cudaStream_t)stream); }
+
+int nsb_op_moe_route(const float* x, const float* Wg, const unsigned char* active, int M, int D, int E, int* best,
+                     float* pb, float* probs, void* stream) {
+    if (E <= 0 || E > 64 || D <= 0) return -1;
+    return moe_route(x, Wg, active, M, D, E, best, pb, probs, (cudaStream_t)stream);
+}
 
 int nsb_op_act_fwd(const float* x, size_t n, int act, float* out32, void* out16, void* stream) {
     return act_fwd_f32(x, n, act, out32, reinterpret_cast<__nv_bfloat16*>(out16), (cudaStream_t)stream);

@@ -138,15 +138,17 @@ __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2),
-// version 1 (sm_100), base offset 0 (tiles are 1024-byte aligned).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor, version 1 (sm_100), base offset 0 (tiles
+// are 1024-byte aligned). layout: 2 = 128-byte swizzle (16-byte granules,
+// 8-row atoms); 1 = 128-byte swizzle with 32-byte granules (4-row atoms),
+// the only layout MN-major tf32 operands accept.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
     d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
     d |= 1ull << 46;
-    d |= 2ull << 61;
+    d |= (uint64_t)(layout & 7) << 61;
     return d;
 }
 

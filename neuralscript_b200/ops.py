@@ -38,6 +38,8 @@ _sigs = {
                                C.c_float, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
                                C.c_void_p]),
     "nsb_op_mgs": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "nsb_op_moe_route": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                   C.c_void_p, C.c_void_p, C.c_void_p]),
     "nsb_op_act_fwd": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     "nsb_op_act_bwd": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_size_t, C.c_void_p, C.c_void_p]),
 }
@@ -153,3 +155,9 @@ def act_fwd(x, act, out32):
 
 def act_bwd(dy, z, act, out32):
     _check(L().nsb_op_act_bwd(p(dy), p(z), act, dy.numel(), p(out32), _stream()), "act_bwd")
+
+
+def moe_route(x, Wg, active, best, pb, probs=None):
+    M, D = x.shape
+    E = Wg.shape[1]
+    _check(L().nsb_op_moe_route(p(x), p(Wg), p(active), M, D, E, p(best), p(pb), p(probs), _stream()), "moe_route")

@@ -269,3 +269,13 @@ def c5(layers: int = 8, dim: int = 4096) -> str:
 C5 = c5()
 
 CONFIGS = {"c1": C1, "c2": C2, "c3": C3, "c4": C4, "c5": C5}
+
+# Config 3 as BASELINE.json words it: each expert a single [D, D] matrix scaled
+# by its routing weight (no counterpart in the reference's code, whose
+# experts are D -> ffn -> D FFNs; C3 above is that reference-expressible form).
+C3_LINEAR = """network C3L
+input 1024
+layer moe moe dim=1024 experts=8 expert=linear
+y = moe(x)
+output y
+"""

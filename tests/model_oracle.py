@@ -165,7 +165,11 @@ class OracleModel:
             elif l.kind == "moe":
                 d = l.i("dim")
                 if l.p.get("expert", "ffn") == "linear":
-                    raise NotImplementedError("linear-expert backward is checked kernel by kernel")
+                    dx, dwg, dwe = linear_moe_grads(dv, u, self.W(f"{l.name}_g_w"), self.W(f"{l.name}_e1_w"),
+                                                    self.active)
+                    grads.update({f"{l.name}_g_w": dwg, f"{l.name}_e1_w": dwe})
+                    add(op.args[0], dx)
+                    continue
                 dx, dwg, dwe1, dwe2 = O.moe_grads(dv, u, self.W(f"{l.name}_g_w"), self.W(f"{l.name}_e1_w"),
                                                   self.W(f"{l.name}_e2_w"), l.i("ffn", 4 * d), self.active)
                 grads.update({f"{l.name}_g_w": dwg, f"{l.name}_e1_w": dwe1, f"{l.name}_e2_w": dwe2})
@@ -259,3 +263,31 @@ def make_weights(spec_text: str, seed: int, sds: Optional[list] = None, default_
         sd = sds[l_idx] if sds is not None else (default_sd if default_sd is not None else 1.0 / math.sqrt(r))
         parts.append(synth.normal(cnt, seed + l_idx, 0.0, sd))
     return np.concatenate(parts) if parts else np.zeros(0, np.float32)
+
+
+def linear_moe_grads(dy, x, Wg, We, active=None):
+    """Gradients of y_i = pb_i (x_i We[b_i]) with the reference router (no
+    reference counterpart: its experts are FFNs). Same gate rule as
+    codegen.cpp:1420-1428: dg_ie = p_ie ((e == b_i) dpb_i - dpb_i pb_i)."""
+    x = np.asarray(x, np.float64)
+    dy = np.asarray(dy, np.float64)
+    M, D = x.shape
+    E = Wg.shape[1]
+    best, pb, p = O.moe_route(np.asarray(x, np.float32), Wg, active)
+    we = np.asarray(We, np.float64).reshape(E, D, D)
+    dx = np.zeros_like(x)
+    dwe = np.zeros_like(we)
+    dpb = np.zeros(M)
+    for e in range(E):
+        idx = np.nonzero(best == e)[0]
+        if idx.size == 0:
+            continue
+        ys = x[idx] @ we[e]
+        dpb[idx] = (ys * dy[idx]).sum(axis=1)
+        sd = dy[idx] * pb[idx, None]
+        dwe[e] = x[idx].T @ sd
+        dx[idx] += sd @ we[e].T
+    dg = p.astype(np.float64) * ((np.arange(E)[None, :] == best[:, None]) * dpb[:, None] - (dpb * pb)[:, None])
+    dwg = x.T @ dg
+    dx += dg @ np.asarray(Wg, np.float64).T
+    return dx.astype(np.float32), dwg.astype(np.float32), dwe.reshape(E, D * D).astype(np.float32)
