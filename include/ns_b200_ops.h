@@ -57,6 +57,23 @@ size_t nsb_op_embedding_bwd_scratch_bytes(int M, int V);
 int nsb_op_embedding_bwd(const float* dout, const float* ids, int M, int V, int D, float* dW, void* scratch,
                          void* stream);
 
+/* Allocation-free variant of nsb_op_embedding_bwd (same result, bit for
+ * bit). No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory when they need this gradient - code running inside
+ * a memory-pool or allocator callback, hosts that have given all device
+ * memory to their own pool, runtimes that forbid cudaMalloc after start-up.
+ * Its sort scratch is a fixed array in the library's device memory, so it
+ * calls no cudaMalloc, cudaFree or allocating library routine.
+ * Limits: M <= 262144 rows and V <= 65536 vocabulary rows; larger sizes
+ * return -2 without launching anything. Every GPU that loads the library
+ * holds the 1.75 MB array until the process exits. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress, once per
+ * device, with that device current); make that first call before any CUDA
+ * stream capture. All calls share the one array: calls that overlap on the
+ * same GPU (for example on two streams) race on it, so serialise them on one
+ * stream. Counters are cleared by every call. */
+int nsb_op_embedding_bwd_noalloc(const float* dout, const float* ids, int M, int V, int D, float* dW, void* stream);
+
 /* LayerNorm, no affine, eps 1e-5. Replaces ns_layernorm_kernel /
  * ns_layernorm_grad_kernel (cuda_backend.cpp:420-431, 473-499),
  * ns_layernorm / ns_layernorm_grad (codegen.cpp:1280-1291, 1346-1371). */

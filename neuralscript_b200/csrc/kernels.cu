@@ -6,6 +6,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "gemm.h"
 #include "kernels.h"
@@ -250,6 +252,53 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     emb_reduce_kernel<<<grid_for((size_t)V, 8), 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
     return launch_ok();
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free embedding gradient
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory at the point they need the
+// embedding gradient: code running inside a custom allocator or memory-pool
+// callback, a host that has handed all device memory to its own pool, or a
+// runtime that forbids cudaMalloc after start-up. For them the sort scratch
+// (counts, offsets, cursors and the row list) lives in this fixed device
+// array instead of a caller buffer. Every GPU that loads the library holds
+// it (kNoAllocScratchBytes) until the process exits.
+constexpr int kNoAllocMaxRows = 262144;
+constexpr int kNoAllocMaxVocab = 65536;
+constexpr size_t kNoAllocScratchBytes = sizeof(int) * ((size_t)3 * kNoAllocMaxVocab + kNoAllocMaxRows);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device. In host code the symbol
+// itself is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+static void* noalloc_scratch_ptr() {
+    static std::mutex mu;
+    static void* ptrs[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> g(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+        ptrs[dev] = p;
+    }
+    return ptrs[dev];
+}
+
+}  // namespace nsb
+
+// The extern "C" entry point is declared in include/ns_b200_ops.h.
+extern "C" int nsb_op_embedding_bwd_noalloc(const float* dout, const float* ids, int M, int V, int D, float* dW,
+                                            void* stream) {
+    if (M < 0 || V <= 0 || D <= 0 || !dout || !ids || !dW) return -1;
+    if (M > nsb::kNoAllocMaxRows || V > nsb::kNoAllocMaxVocab) return -2;  // beyond the fixed scratch
+    void* scratch = nsb::noalloc_scratch_ptr();
+    if (!scratch) return -3;
+    // embedding_bwd zeroes the counters it needs at the start of every call
+    return nsb::embedding_bwd(dout, ids, M, V, D, dW, scratch, (cudaStream_t)stream);
+}
+
+namespace nsb {
 
 // ---------------------------------------------------------------------------
 // LayerNorm (no affine, eps 1e-5) — reference ns_layernorm / ns_layernorm_grad
