@@ -62,30 +62,58 @@ def c4_flops_per_token():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples while the timed region runs."""
+    """SM clock and throttle-reason samples (NVML, every few ms; nvidia-smi
+    when NVML is unavailable) while the measured phase runs."""
 
-    def __init__(self, index):
+    _REASONS = [("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                ("sw_power_cap", 0x4)]
+
+    def __init__(self, index, period_s=0.005):
         self.index = index
-        self.samples = []
+        self.period = period_s
+        self.samples = []  # (sm_mhz, max_mhz, reasons bitmask)
         self._stop = threading.Event()
         self._t = None
 
+    def _nvml_reader(self):
+        import pynvml as N
+        N.nvmlInit()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = int(vis.split(",")[self.index]) if vis and vis.split(",")[0].isdigit() else self.index
+        h = N.nvmlDeviceGetHandleByIndex(idx)
+        mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+        get_r = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            N.nvmlDeviceGetCurrentClocksThrottleReasons
+        return lambda: (N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM), mx, int(get_r(h)))
+
+    def _smi_reader(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+        def read():
+            out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                  "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                 timeout=5).stdout.strip().split(",")
+            bits = sum(b for (_, b), v in zip(self._REASONS, out[2:6]) if v.strip().lower() == "active")
+            return float(out[0]), float(out[1]), bits
+        return read
+
     def start(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+        try:
+            read = self._nvml_reader()
+            self.source = "nvml"
+        except Exception:
+            read = self._smi_reader()
+            self.source = "nvidia-smi"
+            self.period = 0.2
 
         def run():
             while not self._stop.is_set():
                 try:
-                    out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                         timeout=5).stdout.strip()
-                    if out:
-                        self.samples.append([s.strip() for s in out.split(",")])
+                    self.samples.append(read())
                 except Exception:
                     pass
-                self._stop.wait(0.2)
+                self._stop.wait(self.period)
 
         self._t = threading.Thread(target=run, daemon=True)
         self._t.start()
@@ -96,13 +124,10 @@ class ClockSampler:
             self._t.join(timeout=10)
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 3 + i and
-                          s[3 + i].lower() == "active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+        reasons = sorted({n for _, _, bits in self.samples for n, b in self._REASONS if bits & b})
+        return {"sm_mhz": float(np.median([s[0] for s in self.samples])),
+                "sm_max_mhz": float(max(s[1] for s in self.samples)), "reasons": reasons,
+                "samples": len(self.samples), "source": self.source}
 
 
 def dist_env():
@@ -115,9 +140,12 @@ def dist_env():
 # ---------------------------------------------------------------------------
 # reference CPU arm
 # ---------------------------------------------------------------------------
-def _ref_worker(args):
+_REF = {}
+
+
+def _ref_init(lib_path):
+    """Worker initialiser: load the reference library and build one model."""
     import ctypes as C
-    lib_path, seqs, seed = args
     L = C.CDLL(lib_path)
     L.ns_runtime_init.restype = C.c_void_p
     L.ns_runtime_init.argtypes = [C.c_void_p, C.c_size_t]
@@ -126,12 +154,15 @@ def _ref_worker(args):
     from neuralscript_b200.spec import C2, parse
     s = parse(C2)
     w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
-    m = L.ns_runtime_init(w.ctypes.data, w.size)
-    out = np.empty(256 * 512, np.float32)
+    _REF.update(L=L, m=L.ns_runtime_init(w.ctypes.data, w.size), w=w, out=np.empty(256 * 512, np.float32))
+
+
+def _ref_run(seed):
+    """One 256-token sequence through the reference ns_eval_infer."""
+    from neuralscript_b200 import synth
+    tok = synth.tokens(256, seed, 8192)
     t0 = time.perf_counter()
-    for q in range(seqs):
-        tok = synth.tokens(256, seed + q, 8192)
-        L.ns_eval_infer(m, tok.ctypes.data, out.ctypes.data, 256)
+    _REF["L"].ns_eval_infer(_REF["m"], tok.ctypes.data, _REF["out"].ctypes.data, 256)
     return time.perf_counter() - t0
 
 
@@ -140,22 +171,39 @@ def ref_lib_path():
     return p if os.path.exists(p) else None
 
 
-def cpu_reference_throughput(seqs_per_worker, workers):
-    """tokens/s of the reference's emitted CPU code for config 2, one call
-    per 256-token sequence (the reference attends over the whole call)."""
-    path = ref_lib_path()
-    if path is None:
-        return None
-    if workers == 1:
-        dt = _ref_worker((path, seqs_per_worker, 9001))
-        return 256 * seqs_per_worker / dt
-    import multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    with ctx.Pool(workers) as pool:
+class RefPool:
+    """Reference CPU emit for config 2 on `workers` processes (the emitted
+    code is single-threaded and keeps file-scope buffers, so parallelism is
+    one process per core, each on whole 256-token sequences: the reference
+    attends over one call, so one call per sequence is the per-sequence
+    semantics)."""
+
+    def __init__(self, workers):
+        import multiprocessing as mp
+        self.workers = workers
+        path = ref_lib_path()
+        if workers == 1:
+            _ref_init(path)
+            self.pool = None
+        else:
+            self.pool = mp.get_context("spawn").Pool(workers, initializer=_ref_init, initargs=(path,))
+            self.pool.map(_ref_run, range(workers))  # warm every worker
+
+    def step(self, seqs_per_worker=1, seed=9001):
+        n = self.workers * seqs_per_worker
         t0 = time.perf_counter()
-        pool.map(_ref_worker, [(path, seqs_per_worker, 9001 + 100 * i) for i in range(workers)])
+        if self.pool is None:
+            for q in range(n):
+                _ref_run(seed + q)
+        else:
+            self.pool.map(_ref_run, range(seed, seed + n))
         dt = time.perf_counter() - t0
-    return 256 * seqs_per_worker * workers / dt
+        return 256 * n / dt, dt
+
+    def close(self):
+        if self.pool is not None:
+            self.pool.close()
+            self.pool.join()
 
 
 def run_reference(args):
@@ -163,26 +211,26 @@ def run_reference(args):
     if rank != 0:
         return 0
     metric, unit = "tokens_per_s_ns_eval_infer_c2", "tokens/s"
-    path = ref_lib_path()
-    if path is None:
+    if ref_lib_path() is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
         return 0
     cores = os.cpu_count() or 1
-    # one step = one 256-token sequence per core (a bounded sample of the batch)
-    for _ in range(max(args.warmup, 0) and 1):
-        cpu_reference_throughput(1, 1)
-    vals = []
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(cpu_reference_throughput(1, cores))
-    dt = time.perf_counter() - t0
+    pool = RefPool(cores)
+    for w in range(min(args.warmup, 1)):
+        pool.step(1, 5000 + w)
+    vals, tot = [], 0.0
+    for i in range(args.steps):
+        v, dt = pool.step(1, 9001 + i * cores)
+        vals.append(v)
+        tot += dt
+    pool.close()
     v = float(np.median(vals))
     line = {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * dt / max(args.steps, 1), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * tot / max(args.steps, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config 2 transformer block forward, reference CPU emit (nsc --cpp --runtime), "
-                                   "one ns_eval_infer call per 256-token sequence", "seq_len": 256,
-                       "tokens_per_step": 256 * cores},
+            "config": {"workload": "config 2 transformer block forward, reference CPU emit (nsc --cpp --runtime, "
+                                   "g++ -O3 -march=x86-64-v3), one ns_eval_infer call per 256-token sequence",
+                       "seq_len": 256, "tokens_per_step": 256 * cores},
             "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": "reference",
                              "sample": f"{cores} sequences of 256 tokens per step, one process per core"},
             "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -193,22 +241,37 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
-def time_gemm(O, torch, M, N, K, act, steps, stream_ptr):
-    """Average device time of one GEMM launch with the engine's operand
-    layouts (A K-major bf16, W [K,N] as MN-major B)."""
-    A = torch.randn(M, K, device="cuda").bfloat16()
-    B = torch.randn(K, N, device="cuda").bfloat16()
-    C16 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    for _ in range(3):
-        O.gemm(A, B, M, N, K, K, 0, N, 1, act=act, c16=C16)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(steps):
-        O.gemm(A, B, M, N, K, K, 0, N, 1, act=act, c16=C16)
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / steps / 1e3
+def region_work(spec, label, M, train):
+    """Algorithmic work of one engine region: ("flops"|"bytes", amount)."""
+    from neuralscript_b200.spec import parse
+    s = parse(spec)
+    phase, name = label.split(":", 1) if ":" in label else ("", label)
+    lname, _, part = name.partition(".")
+    try:
+        l = s.layer(lname)
+    except KeyError:
+        if label == "loss":
+            return "bytes", M * 8192 * (4 + (4 if train else 0))
+        if label == "optimizer":
+            return "bytes", s.weight_count * 4 * 7
+        return None, 0
+    k = l.kind
+    bwd = phase == "bwd"
+    if k == "dense":
+        f = 2.0 * M * l.i("in") * l.i("out")
+        return "flops", 2 * f if bwd else f
+    if k == "attention":
+        D, S = l.i("dim"), l.i("seq", 0) or M
+        if bwd:
+            return "flops", 2 * (2.0 * M * 3 * D * D + 2.0 * M * D * D) + 2.5 * 4.0 * M * S * D
+        return "flops", {"qkv": 2.0 * M * 3 * D * D, "core": 4.0 * M * S * D, "out": 2.0 * M * D * D}.get(part, 0)
+    if k == "layernorm":
+        D = 512
+        return "bytes", M * D * ((4 + 4 + 4 + 4) if bwd else (4 + 4 + 2))
+    if k == "embedding":
+        D = l.i("dim")
+        return "bytes", M * D * ((4 + 4) if bwd else (4 + 4 + 2)) + M * 4
+    return None, 0
 
 
 def run_b200(args):
@@ -216,7 +279,6 @@ def run_b200(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     import neuralscript_b200 as nsb
-    from neuralscript_b200 import ops as O
     from neuralscript_b200 import synth
     from neuralscript_b200.spec import CONFIGS, parse
 
@@ -285,19 +347,21 @@ def run_b200(args):
     value = tokens_step / (ms_step / 1e3)
 
     # end to end through the reference-facing ABI with host buffers
-    tok_h = tok.cpu().numpy()
+    # host buffers are page-locked, as a serving caller would hold them
+    tok_h = tok.cpu().pin_memory().numpy()
     if train:
-        tgt_h = tgt.cpu().numpy()
+        tgt_h = tgt.cpu().pin_memory().numpy()
         y1h = None
         if args.e2e_one_hot:
-            y1h = np.zeros((M, 8192), np.float32)
+            y1h = torch.zeros(M, 8192).pin_memory().numpy()
             y1h[np.arange(M), tgt_h] = 1.0
         e2e_fn = (lambda: model.train_step(tok_h, y1h, 3e-4)) if y1h is not None else \
             (lambda: model.train_step_idx(tok_h, tgt_h, 3e-4))
         h2d = tok_h.nbytes + (y1h.nbytes if y1h is not None else tgt_h.nbytes)
         d2h = 4
     else:
-        e2e_fn = lambda: model.infer(tok_h)
+        out_h = torch.empty(M * 512, dtype=torch.float32).pin_memory().numpy()
+        e2e_fn = lambda: model.infer(tok_h, out_h)
         h2d = tok_h.nbytes
         d2h = M * 512 * 4
     for _ in range(2):
@@ -316,23 +380,47 @@ def run_b200(args):
     e2e = {"value": tokens_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h)}
 
-    # roofline of the dominant GEMM (ff1: 16384 x 2048 x 512, GELU epilogue)
+    # per-region device time inside the engine (CUDA events on the engine
+    # stream) over the same number of steps; the dominant region's kernel is
+    # the roofline line
     pk, pk_kind = peaks()
-    t_ff1 = time_gemm(O, torch, M, 2048, 512, 6, 20, sp)
-    flops_ff1 = 2.0 * M * 2048 * 512
-    ach = flops_ff1 / t_ff1 / 1e12
-    roof = {"kernel": "gemm_tc_kernel bf16 ff1 16384x2048x512 (+GELU)", "bound": "tensor",
-            "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
-            "peak_kind": f"{pk_kind} bf16 burst", "traffic": None}
+    model.region_timing(True)
+    for i in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    regs = model.regions()
+    model.region_timing(False)
+    kernels = []
+    for label, (tot_ms, n) in regs.items():
+        kind, work = region_work(spec, label, M, train)
+        if not kind or n == 0:
+            continue
+        t = tot_ms / n / 1e3
+        if kind == "flops":
+            ach, peak, unit, bound = work / t / 1e12, pk["bf16_tflops"], "TFLOP/s", "tensor"
+        else:
+            ach, peak, unit, bound = work / t / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
+        kernels.append({"region": label, "us": t * 1e6, "bound": bound, "achieved": ach, "peak": peak,
+                        "unit": unit, "frac": ach / peak, "work": work})
+    kernels.sort(key=lambda k: -k["us"])
+    roof = None
+    if kernels:
+        top = kernels[0]
+        roof = {"kernel": top["region"], "bound": top["bound"], "achieved": top["achieved"], "peak": top["peak"],
+                "unit": top["unit"], "frac": top["frac"], "traffic": None,
+                "peak_kind": f"{pk_kind} ({'bf16 burst' if top['bound'] == 'tensor' else 'HBM copy'})",
+                "us_per_launch": top["us"]}
 
     result = None
     if rank == 0:
         cpu = None
-        if args.cpu_baseline and not train:
-            v = cpu_reference_throughput(2, 1)
+        if args.cpu_baseline and not train and ref_lib_path():
+            pool = RefPool(1)
+            v, _ = pool.step(8, 9001)
             if v is not None:
                 cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
-                       "sample": "2 sequences x 256 tokens through the reference CPU emit (libref_c2.so)"}
+                       "sample": "8 sequences x 256 tokens through the reference CPU emit (libref_c2.so), 1 core"}
         fl = c4_flops_per_token() if train else c2_flops_per_token()
         result = {
             "metric": "tokens_per_s_ns_runtime_train_step_c4" if train else "tokens_per_s_ns_eval_infer_c2",
@@ -346,7 +434,9 @@ def run_b200(args):
                        "l2": "flushed between steps (512 MB write outside timing)"},
             "model_tflops": fl * value / 1e12,
             "step_frac_of_bf16_peak": fl * value / world / 1e12 / pk["bf16_tflops"],
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "roofline": roof,
+            "kernels": [{k: (round(v, 4) if isinstance(v, float) else v) for k, v in kk.items()} for kk in kernels],
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": int(launches) * args.steps,
         }
         print(json.dumps(result))
@@ -360,7 +450,7 @@ def run_b200(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="c2", choices=["c2", "c4"])

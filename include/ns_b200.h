@@ -84,6 +84,16 @@ int nsb_train_step_device(ns_model* m, const float* d_input, const float* d_labe
  * over ranks when data-parallel), copied to host `out` of n floats. */
 int nsb_model_get_gradients(const ns_model* m, float* out, size_t n);
 
+/* Per-region timing: CUDA events recorded on the model's stream around every
+ * forward op (attention split into qkv / core / out), every backward op,
+ * the loss, the all-reduce and the optimizer. enable != 0 switches it on and
+ * resets the totals (also on at init when NS_B200_REGION_TIMING is set).
+ * nsb_region_count synchronises and folds pending events into the totals;
+ * nsb_region_get returns region i's label, total milliseconds and count. */
+int nsb_region_timing(ns_model* m, int enable);
+int nsb_region_count(ns_model* m);
+int nsb_region_get(const ns_model* m, int i, const char** label, double* total_ms, long long* count);
+
 /* Number of kernel launches issued by the last public call on this model. */
 long long nsb_last_launch_count(const ns_model* m);
 

@@ -79,6 +79,10 @@ def lib() -> C.CDLL:
                                             C.c_float, C.c_void_p]),
         "nsb_last_launch_count": (C.c_longlong, [C.c_void_p]),
         "nsb_model_get_gradients": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+        "nsb_region_timing": (C.c_int, [C.c_void_p, C.c_int]),
+        "nsb_region_count": (C.c_int, [C.c_void_p]),
+        "nsb_region_get": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
+                                     C.POINTER(C.c_longlong)]),
         "nsb_dist_unique_id": (C.c_int, [C.c_void_p]),
         "nsb_dist_init": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
         "nsb_last_error": (C.c_char_p, []),
@@ -156,11 +160,17 @@ class Model:
     def weight_count(self) -> int:
         return lib().nsb_model_weight_count(self._h)
 
-    def infer(self, x: np.ndarray) -> np.ndarray:
+    def infer(self, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """ns_eval_infer with host buffers; `out` (float32, contiguous) may be
+        a caller-owned buffer, e.g. page-locked memory."""
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
-        out = np.empty(self.output_numel(x.size), np.float32)
+        n = self.output_numel(x.size)
+        if out is None:
+            out = np.empty(n, np.float32)
+        if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < n:
+            raise ValueError("infer: out must be a contiguous float32 array of at least %d elements" % n)
         _check(lib().nsb_eval_infer(self._h, _ptr(x), _ptr(out), x.size), "ns_eval_infer")
-        return out.reshape(-1, self.spec_out_cols)
+        return out.reshape(-1)[:n].reshape(-1, self.spec_out_cols)
 
     @property
     def spec_out_cols(self) -> int:
@@ -235,6 +245,18 @@ class Model:
                                            C.byref(loss) if want_loss else None, lr, C.c_void_p(stream)),
                "train_step_device")
         return loss.value
+
+    def region_timing(self, enable: bool = True) -> None:
+        _check(lib().nsb_region_timing(self._h, 1 if enable else 0), "region_timing")
+
+    def regions(self):
+        """{label: (total_ms, count)} of the regions timed since enabling."""
+        out = {}
+        for i in range(lib().nsb_region_count(self._h)):
+            lab, ms, n = C.c_char_p(), C.c_double(), C.c_longlong()
+            lib().nsb_region_get(self._h, i, C.byref(lab), C.byref(ms), C.byref(n))
+            out[lab.value.decode()] = (ms.value, n.value)
+        return out
 
     def last_launch_count(self) -> int:
         return lib().nsb_last_launch_count(self._h)

@@ -460,6 +460,52 @@ static GemmOperand opnd(const void* p, int dt, long long ld, bool mn) {
 static const void* as_operand(ns_model* m, const Val& v) { return m->wdt == kBF16 ? (const void*)v.h16 : (const void*)v.f32; }
 
 // ---------------------------------------------------------------------------
+// region timing (events on the engine stream; read back after a sync)
+// ---------------------------------------------------------------------------
+static int region_begin(ns_model* m, const std::string& label) {
+    if (!m->timing) return -1;
+    int idx = -1;
+    for (size_t i = 0; i < m->regions.size(); i++)
+        if (m->regions[i].label == label) idx = (int)i;
+    if (idx < 0) {
+        m->regions.push_back(ns_model::Region());
+        m->regions.back().label = label;
+        idx = (int)m->regions.size() - 1;
+    }
+    ns_model::Region& r = m->regions[idx];
+    std::pair<cudaEvent_t, cudaEvent_t> ev;
+    if (!r.pool.empty()) {
+        ev = r.pool.back();
+        r.pool.pop_back();
+    } else {
+        cudaEventCreate(&ev.first);
+        cudaEventCreate(&ev.second);
+    }
+    cudaEventRecord(ev.first, m->stream);
+    r.pending.push_back(ev);
+    return idx;
+}
+
+static void region_end(ns_model* m, int idx) {
+    if (idx < 0) return;
+    cudaEventRecord(m->regions[idx].pending.back().second, m->stream);
+}
+
+static void regions_collect(ns_model* m) {
+    for (auto& r : m->regions) {
+        for (auto& ev : r.pending) {
+            float ms = 0.f;
+            if (cudaEventSynchronize(ev.second) == cudaSuccess && cudaEventElapsedTime(&ms, ev.first, ev.second) == cudaSuccess) {
+                r.ms += ms;
+                r.count++;
+            }
+            r.pool.push_back(ev);
+        }
+        r.pending.clear();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
 static int forward(ns_model* m, int M, bool train) {
@@ -474,6 +520,8 @@ static int forward(ns_model* m, int M, bool train) {
         Val& in = m->vals[op.in];
         Val& out = m->vals[op.out];
         int rc = 0;
+        const std::string& lname = op.layer >= 0 ? s.layers[op.layer].name : s.ops[oi].out;
+        int reg = op.kind == OP_ATTN ? -1 : region_begin(m, std::string("fwd:") + lname);
         switch (op.kind) {
             case OP_DENSE: {
                 const WeightInfo& w = s.weights[op.widx];
@@ -527,7 +575,10 @@ static int forward(ns_model* m, int M, bool train) {
                     d.ep.c32 = reinterpret_cast<float*>(op.qkv);
                     d.ep.ld_c32 = 3 * D;
                 }
-                if ((rc = run_gemm(m, d))) break;
+                int r1 = region_begin(m, "fwd:" + lname + ".qkv");
+                rc = run_gemm(m, d);
+                region_end(m, r1);
+                if (rc) break;
                 AttnArgs a;
                 a.B = M / S;
                 a.S = S;
@@ -543,7 +594,10 @@ static int forward(ns_model* m, int M, bool train) {
                 a.lse = op.lse;
                 a.err = m->d_err;
                 launch_counter() += 1;
-                if ((rc = attention_fwd(a, m->stream))) {
+                int r2 = region_begin(m, "fwd:" + lname + ".core");
+                rc = attention_fwd(a, m->stream);
+                region_end(m, r2);
+                if (rc) {
                     rc = fail("attention launch failed");
                     break;
                 }
@@ -561,7 +615,9 @@ static int forward(ns_model* m, int M, bool train) {
                 o.ep.ld_c32 = D;
                 o.ep.c16 = out.h16;
                 o.ep.ld_c16 = D;
+                int r3 = region_begin(m, "fwd:" + lname + ".out");
                 rc = run_gemm(m, o);
+                region_end(m, r3);
                 break;
             }
             case OP_LN:
@@ -588,6 +644,7 @@ static int forward(ns_model* m, int M, bool train) {
             default:
                 return fail("operation not supported by this backend: " + s.ops[oi].fn);
         }
+        region_end(m, reg);
         if (rc) return rc < 0 && !g_err.empty() ? -1 : fail("kernel launch failed in " + s.ops[oi].out);
     }
     return 0;
@@ -627,6 +684,7 @@ static int backward(ns_model* m, int M) {
         const float* dv = out.gcur;
         Val& in = m->vals[op.in];
         int rc = 0;
+        const int reg = region_begin(m, std::string("bwd:") + (op.layer >= 0 ? s.layers[op.layer].name : s.ops[oi].out));
         switch (op.kind) {
             case OP_DENSE: {
                 const WeightInfo& w = s.weights[op.widx];
@@ -794,6 +852,7 @@ static int backward(ns_model* m, int M) {
             default:
                 return fail("backward not supported for " + s.ops[oi].fn);
         }
+        region_end(m, reg);
         if (rc) return -1;
     }
     return 0;
@@ -902,6 +961,10 @@ static int optimizer_step(ns_model* m, float lr) {
         if ((int)at.size() > m->adam_cap) {
             if (m->d_adam) cudaFree(m->d_adam);
             if (m->h_adam) cudaFreeHost(m->h_adam);
+    for (auto& r : m->regions) {
+        for (auto& ev : r.pending) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
+        for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
+    }
             m->adam_cap = (int)at.size();
             if (cudaMalloc(&m->d_adam, sizeof(AdamTensor) * at.size()) != cudaSuccess) return fail("alloc failed");
             if (cudaMallocHost(&m->h_adam, sizeof(AdamTensor) * at.size()) != cudaSuccess) return fail("alloc failed");
@@ -1110,6 +1173,7 @@ ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_fl
         return nullptr;
     }
     m->precision = env_precision(m->spec.precision);
+    m->timing = getenv("NS_B200_REGION_TIMING") != nullptr;
     m->wdt = m->precision == 2 ? kBF16 : kF32;
     cudaGetDevice(&m->device);
     bool ok = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
@@ -1162,6 +1226,10 @@ void nsb_free(ns_model* m) {
                     (void*)m->d_ns, (void*)m->d_active, m->d_adam})
         if (p) cudaFree(p);
     if (m->h_adam) cudaFreeHost(m->h_adam);
+    for (auto& r : m->regions) {
+        for (auto& ev : r.pending) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
+        for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
+    }
     if (m->h_loss) cudaFreeHost(m->h_loss);
     if (m->comm) nccl().CommDestroy(m->comm);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -1196,6 +1264,33 @@ int nsb_set_precision(ns_model* m, int mode) {
 int nsb_get_precision(const ns_model* m) { return m ? m->precision : -1; }
 
 long long nsb_last_launch_count(const ns_model* m) { return m ? m->launches : 0; }
+
+int nsb_region_timing(ns_model* m, int enable) {
+    if (!m) return -1;
+    cudaStreamSynchronize(m->stream);
+    regions_collect(m);
+    for (auto& r : m->regions) {
+        r.ms = 0;
+        r.count = 0;
+    }
+    m->timing = enable != 0;
+    return 0;
+}
+
+int nsb_region_count(ns_model* m) {
+    if (!m) return 0;
+    cudaStreamSynchronize(m->stream);
+    regions_collect(m);
+    return (int)m->regions.size();
+}
+
+int nsb_region_get(const ns_model* m, int i, const char** label, double* total_ms, long long* count) {
+    if (!m || i < 0 || i >= (int)m->regions.size()) return -1;
+    if (label) *label = m->regions[i].label.c_str();
+    if (total_ms) *total_ms = m->regions[i].ms;
+    if (count) *count = m->regions[i].count;
+    return 0;
+}
 
 int nsb_model_get_gradients(const ns_model* m, float* out, size_t n) {
     if (!m || !out || n != m->spec.total) return -1;
@@ -1260,7 +1355,9 @@ int nsb_eval_infer(ns_model* m, const float* input, float* output, size_t input_
 static int train_core(ns_model* m, int M, const float* d_labels, const int* d_targets, float* loss_out, float lr,
                       bool train) {
     if (forward(m, M, train)) return -1;
+    int rl = region_begin(m, "loss");
     if (loss_and_seed(m, M, d_labels, d_targets, train)) return -1;
+    region_end(m, rl);
     launch_counter() += 1;
     const float scale = 1.0f / ((float)M * (m->spec.loss == "mse" ? (float)m->spec.out_cols : 1.f));
     if (train) {
@@ -1270,12 +1367,16 @@ static int train_core(ns_model* m, int M, const float* d_labels, const int* d_ta
         if (backward(m, M)) return -1;
         // the loss sum rides at the end of the gradient blob
         reduce_sum(m->d_rowloss, M, 1.0f, m->d_g + m->spec.total, m->stream);
+        int ra = region_begin(m, "allreduce");
         if (m->comm && m->world > 1) {
             launch_counter() += 1;
             ncclResult_t r = nccl().AllReduce(m->d_g, m->d_g, m->spec.total + 1, ncclFloat, ncclSum, m->comm, m->stream);
             if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("allreduce: ") + nccl().GetErrorString(r));
         }
+        region_end(m, ra);
+        int ro = region_begin(m, "optimizer");
         if (optimizer_step(m, lr)) return -1;
+        region_end(m, ro);
         m->host_dirty = true;
         const float gscale = 1.0f / ((float)M * (float)m->world *
                                      (m->spec.loss == "mse" ? (float)m->spec.out_cols : 1.f));

@@ -119,4 +119,14 @@ struct ns_model {
     int rank = 0, world = 1;
     int timeout_ms = 60000;
     long long launches = 0;
+    // per-region CUDA-event timing on the engine stream (opt-in)
+    bool timing = false;
+    struct Region {
+        std::string label;
+        std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+        std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pool;
+        double ms = 0;
+        long long count = 0;
+    };
+    std::vector<Region> regions;
 };

@@ -1,0 +1,116 @@
+"""Kernel micro-benchmarks: time one hot-path kernel family through the
+kernel-level C-ABI (include/ns_b200_ops.h) on synthetic operands, with CUDA
+events on the launching stream after warm-up.
+
+    python -m neuralscript_b200.kbench gemm --M 16384 --N 2048 --K 512 --act gelu
+    python -m neuralscript_b200.kbench attention --B 64 --S 256 --H 8 --D 512
+    python -m neuralscript_b200.kbench layernorm --M 16384 --D 512
+
+Prints one JSON line per run: average launch time, achieved TFLOP/s or GB/s
+and the fraction of the measured peak (MEASURED_PEAKS.json).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+ACTS = {"none": 0, "relu": 1, "gelu": 6}
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def _time(fn, iters, warmup=3):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters / 1e3
+
+
+def gemm_case(M, N, K, act="none", dtype="bf16", iters=20):
+    """The engine's forward layout: A [M,K] K-major, W [K,N] row-major (MN-major B)."""
+    import torch
+    from . import ops as O
+    dt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    A = torch.randn(M, K, device="cuda").to(dt)
+    B = torch.randn(K, N, device="cuda").to(dt)
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    t = _time(lambda: O.gemm(A, B, M, N, K, K, 0, N, 1, act=ACTS[act], c16=C), iters)
+    pk, kind = _peaks()
+    tf = 2.0 * M * N * K / t / 1e12
+    return {"kernel": "gemm", "M": M, "N": N, "K": K, "act": act, "dtype": dtype, "us": t * 1e6,
+            "tflops": tf, "frac_of_bf16_peak": tf / pk["bf16_tflops"], "peak_kind": kind,
+            "tensor_cores": O.uses_tensor_cores(A, B, M, N, K, K, 0, N, 1)}
+
+
+def attention_case(B, S, H, D, iters=20, backward=False):
+    import torch
+    from . import ops as O
+    qkv = torch.randn(B * S, 3 * D, device="cuda").bfloat16()
+    ctx = torch.empty(B * S, D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B * H * S, device="cuda")
+    t = _time(lambda: O.attention_fwd(B, S, H, D, qkv, ctx, lse), iters)
+    fl = 4.0 * B * H * S * S * (D // H)
+    res = {"kernel": "attention_fwd", "B": B, "S": S, "H": H, "D": D, "us": t * 1e6, "tflops": fl / t / 1e12}
+    if backward:
+        g = torch.randn(B * S, D, device="cuda").bfloat16()
+        dq = torch.empty(B * S, 3 * D, device="cuda", dtype=torch.bfloat16)
+        dv = torch.empty(B * H * S, device="cuda")
+        tb = _time(lambda: O.attention_bwd(B, S, H, D, qkv, ctx, lse, g, dq, dv), iters)
+        res.update({"bwd_us": tb * 1e6, "bwd_tflops": 2.5 * fl / tb / 1e12})
+    return res
+
+
+def layernorm_case(M, D, iters=50):
+    import torch
+    from . import ops as O
+    x = torch.randn(M, D, device="cuda")
+    y = torch.empty_like(x)
+    y16 = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    t = _time(lambda: O.layernorm_fwd(x, y, y16), iters)
+    pk, kind = _peaks()
+    gbs = (M * D * (4 + 4 + 2)) / t / 1e9
+    return {"kernel": "layernorm_fwd", "M": M, "D": D, "us": t * 1e6, "gbs": gbs,
+            "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_kind": kind}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["gemm", "attention", "layernorm"])
+    ap.add_argument("--M", type=int, default=16384)
+    ap.add_argument("--N", type=int, default=2048)
+    ap.add_argument("--K", type=int, default=512)
+    ap.add_argument("--act", default="none", choices=sorted(ACTS))
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "tf32"])
+    ap.add_argument("--B", type=int, default=64)
+    ap.add_argument("--S", type=int, default=256)
+    ap.add_argument("--H", type=int, default=8)
+    ap.add_argument("--D", type=int, default=512)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--backward", action="store_true")
+    a = ap.parse_args()
+    if a.kernel == "gemm":
+        r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters)
+    elif a.kernel == "attention":
+        r = attention_case(a.B, a.S, a.H, a.D, a.iters, a.backward)
+    else:
+        r = layernorm_case(a.M, a.D, a.iters)
+    print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()
