@@ -317,9 +317,12 @@ int attention_fwd(const AttnArgs& a, cudaStream_t s) {
     return bf ? fwd_launch<__nv_bfloat16, 128>(a, s) : fwd_launch<float, 128>(a, s);
 }
 
+int attention_bwd_launches(const AttnArgs& a) { return attention_tc_bwd_supported(a) ? 1 : 2; }
+
 int attention_bwd(const AttnArgs& a, cudaStream_t s) {
     if (a.B <= 0 || a.S <= 0) return 0;
     if (a.dh > 128) return -1;
+    if (attention_tc_bwd_supported(a)) return attention_tc_bwd(a, s, a.err);
     const bool bf = a.dtype == kBF16;
     if (a.dh <= 32) return bf ? bwd_launch<__nv_bfloat16, 32>(a, s) : bwd_launch<float, 32>(a, s);
     if (a.dh <= 64) return bf ? bwd_launch<__nv_bfloat16, 64>(a, s) : bwd_launch<float, 64>(a, s);

@@ -25,6 +25,11 @@ int attention_fwd(const AttnArgs& a, cudaStream_t s);
 // tcgen05 forward (attention_tc.cu): bf16, head dim 64, S <= 256
 bool attention_tc_supported(const AttnArgs& a);
 int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err);
+// tcgen05 backward: bf16, head dim 64, S <= 256, lse from the forward
+bool attention_tc_bwd_supported(const AttnArgs& a);
+int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err);
+// Number of kernel launches attention_bwd issues for `a`.
+int attention_bwd_launches(const AttnArgs& a);
 int attention_bwd(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace nsb

@@ -183,18 +183,262 @@ __global__ void __launch_bounds__(128, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core attention backward (bf16, head dim 64, S <= 256), the flash
+// recomputation form of the reference's ns_attention_grad_kernel
+// (src/codegen/cuda_backend.cpp:231-366, CPU ns_attention_bwd
+// src/codegen/codegen.cpp:1785-1907): with P = exp(scale*QK^T - lse),
+//   dV = P^T dO,  dP = dO V^T,  dS = P o (dP - rowdot(dO, O)),
+//   dQ = scale * dS K,  dK = scale * dS^T Q.
+// One CTA (8 warps) per (sequence b, head h) holds the whole sequence's
+// Q, K, V, dO in shared memory (TMA, 128-byte swizzle) and walks the
+// (key tile j, query tile i) pairs of 128 x 128:
+//   MMA1  S^T = K_j Q_i^T, dP^T = V_j dO_i^T          -> TMEM cols [0,256)
+//   elementwise: warp w owns key rows 32*(w%4).., query half w/4; P^T and
+//         dS^T are rounded to bf16 into shared memory (K-major swizzled)
+//   MMA2  dV_j += P^T dO_i, dK_j += dS^T Q_i          -> cols [256,384)
+//         dQ_i += dS K_j (dS^T read as an MN-major A) -> cols [384,512)
+// dK_j / dV_j are written when key tile j is done, dQ at the end, so every
+// sum over keys or queries stays inside the CTA (no atomics). All waits are
+// bounded and report through the error word.
+namespace {
+constexpr int kBT = 128;                 // key / query tile
+constexpr int kTile = kBT * 128;         // 128 rows x 64 bf16 = 16 KB
+constexpr int kBwdThreads = 256;
+constexpr int kBwdSmem = 12 * kTile + 2 * 256 * 4 + 64 + 1024;
+constexpr uint32_t kIdescT = ptx::instr_desc(1, 0, 0, kBT, kBT);   // S^T, dP^T
+constexpr uint32_t kIdescKV = ptx::instr_desc(1, 0, 1, kBT, kDh);  // dV, dK
+constexpr uint32_t kIdescQ = ptx::instr_desc(1, 1, 1, kBT, kDh);   // dQ
+}  // namespace
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t* v, float mul) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        uint4 pk;
+        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+            h2[t] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * t]) * mul,
+                                          __uint_as_float(v[8 * g + 2 * t + 1]) * mul);
+        d[g] = pk;
+    }
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_tc_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo, int S,
+                       int H, int D, float scale, const __nv_bfloat16* __restrict__ ctx, long long ld_ctx,
+                       const __nv_bfloat16* __restrict__ dctx, long long ld_dctx, const float* __restrict__ lse,
+                       __nv_bfloat16* __restrict__ dqkv, long long ld_dqkv, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + 2 * kTile;
+    uint8_t* sV = sK + 2 * kTile;
+    uint8_t* sO = sV + 2 * kTile;  // dO
+    uint8_t* sP = sO + 2 * kTile;  // P^T  [128 keys][128 queries] as two 64-query chunks
+    uint8_t* sD = sP + 2 * kTile;  // dS^T, same layout
+    float* lse_s = reinterpret_cast<float*>(sD + 2 * kTile);
+    float* dv_s = lse_s + 256;
+    uint64_t* ld_bar = reinterpret_cast<uint64_t*>(dv_s + 256);
+    uint64_t* mma_bar = ld_bar + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int t = threadIdx.x, warp = t >> 5;
+    const int lg = warp & 3, half = warp >> 2;
+    const int r = lg * 32 + (t & 31);  // TMEM lane = tile row this thread reads
+    const int row0 = b * S;
+    const int nt = (S + kBT - 1) / kBT;
+
+    if (t == 0) {
+        ptx::mbar_init(ld_bar, 1);
+        ptx::mbar_init(mma_bar, 1);
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&tqkv);
+        ptx::prefetch_tmap(&tdo);
+    }
+    if (warp == 0) {
+        ptx::tmem_alloc(tmem_slot, 512);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + ((uint32_t)(lg * 32) << 16);
+
+    if (t == 0) {
+        ptx::mbar_arrive_expect_tx(ld_bar, nt * 4 * kTile);
+        for (int x = 0; x < nt; x++) {
+            const int y = row0 + x * kBT;
+            ptx::tma_load_2d(sQ + x * kTile, &tqkv, ld_bar, h * kDh, y);
+            ptx::tma_load_2d(sK + x * kTile, &tqkv, ld_bar, D + h * kDh, y);
+            ptx::tma_load_2d(sV + x * kTile, &tqkv, ld_bar, 2 * D + h * kDh, y);
+            ptx::tma_load_2d(sO + x * kTile, &tdo, ld_bar, h * kDh, y);
+        }
+    }
+    // lse and rowdot(dO, O) of every query, while the tiles load
+    {
+        const int q = t;
+        float L = 0.f, dd = 0.f;
+        if (q < S) {
+            L = lse[((size_t)b * H + h) * S + q];
+            const uint4* go = reinterpret_cast<const uint4*>(dctx + (size_t)(row0 + q) * ld_dctx + h * kDh);
+            const uint4* oo = reinterpret_cast<const uint4*>(ctx + (size_t)(row0 + q) * ld_ctx + h * kDh);
+#pragma unroll
+            for (int g = 0; g < kDh / 8; g++) {
+                uint4 a = go[g], c = oo[g];
+                const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+                const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float2 fa = __bfloat1622float2(a2[e]), fc = __bfloat1622float2(c2[e]);
+                    dd = fmaf(fa.x, fc.x, dd);
+                    dd = fmaf(fa.y, fc.y, dd);
+                }
+            }
+        }
+        if (q < 256) {
+            lse_s[q] = L;
+            dv_s[q] = dd;
+        }
+    }
+    __syncthreads();
+
+    const uint32_t aQ = ptx::smem_u32(sQ), aK = ptx::smem_u32(sK), aV = ptx::smem_u32(sV), aO = ptx::smem_u32(sO);
+    const uint32_t aP = ptx::smem_u32(sP), aD = ptx::smem_u32(sD);
+    bool ok = true;
+    auto mma1 = [&](int j, int i) {
+#pragma unroll
+        for (int s = 0; s < kDh / 16; s++)
+            ptx::mma_bf16(tmem, ptx::smem_desc(aK + j * kTile + s * 32, 16, 1024, 2),
+                          ptx::smem_desc(aQ + i * kTile + s * 32, 16, 1024, 2), kIdescT, s > 0);
+#pragma unroll
+        for (int s = 0; s < kDh / 16; s++)
+            ptx::mma_bf16(tmem + kBT, ptx::smem_desc(aV + j * kTile + s * 32, 16, 1024, 2),
+                          ptx::smem_desc(aO + i * kTile + s * 32, 16, 1024, 2), kIdescT, s > 0);
+    };
+    auto mma2 = [&](int j, int i) {
+#pragma unroll
+        for (int s = 0; s < kBT / 16; s++) {
+            const uint64_t pa = ptx::smem_desc(aP + (s >> 2) * kTile + (s & 3) * 32, 16, 1024, 2);
+            const uint64_t ob = ptx::smem_desc(aO + i * kTile + s * 2048, kTile, 1024, 2);
+            ptx::mma_bf16(tmem + 256, pa, ob, kIdescKV, (i > 0) || (s > 0));
+        }
+#pragma unroll
+        for (int s = 0; s < kBT / 16; s++) {
+            const uint64_t da = ptx::smem_desc(aD + (s >> 2) * kTile + (s & 3) * 32, 16, 1024, 2);
+            const uint64_t qb = ptx::smem_desc(aQ + i * kTile + s * 2048, kTile, 1024, 2);
+            ptx::mma_bf16(tmem + 320, da, qb, kIdescKV, (i > 0) || (s > 0));
+        }
+#pragma unroll
+        for (int s = 0; s < kBT / 16; s++) {
+            const uint64_t da = ptx::smem_desc(aD + s * 2048, kTile, 1024, 2);
+            const uint64_t kb = ptx::smem_desc(aK + j * kTile + s * 2048, kTile, 1024, 2);
+            ptx::mma_bf16(tmem + 384 + 64 * i, da, kb, kIdescQ, (j > 0) || (s > 0));
+        }
+    };
+    // dK_j / dV_j: warps of the first half write dV, the second half dK
+    auto write_kv = [&](int j) {
+        uint32_t v[32];
+        const int kg = j * kBT + r;
+        const int col = (half == 0 ? 2 * D : D) + h * kDh;
+        const float mul = half == 0 ? 1.f : scale;
+#pragma unroll 1
+        for (int c = 0; c < kDh; c += 32) {
+            ptx::tmem_ld32(lane_base + 256 + half * 64 + c, v);
+            ptx::tmem_ld_wait();
+            if (ok && kg < S) store_bf16x32(dqkv + (size_t)(row0 + kg) * ld_dqkv + col + c, v, mul);
+        }
+    };
+
+    if (t == 0) {
+        ok = ptx::mbar_wait(ld_bar, 0, err, kErrTimeoutAttn);
+        ptx::tc_fence_after();
+        if (ok) mma1(0, 0);
+        ptx::mma_commit(mma_bar);
+    }
+    uint32_t mph = 0;
+    const int steps = nt * nt;
+#pragma unroll 1
+    for (int st = 0; st < steps; st++) {
+        const int j = st / nt, i = st % nt;
+        ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
+        mph ^= 1;
+        ptx::tc_fence_after();
+        if (st > 0 && i == 0) write_kv(j - 1);  // MMA2 of key tile j-1 has completed
+        const int kg = j * kBT + r;
+        const bool kval = kg < S;
+        uint8_t* prow = sP + half * kTile + r * 128;
+        uint8_t* drow = sD + half * kTile + r * 128;
+#pragma unroll 1
+        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+            uint32_t sv[32], pv[32];
+            ptx::tmem_ld32(lane_base + c0, sv);
+            ptx::tmem_ld32(lane_base + kBT + c0, pv);
+            ptx::tmem_ld_wait();
+            float p[32], ds[32];
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                const int qg = i * kBT + c0 + e;
+                const bool v = kval && qg < S;
+                const float pe = v ? expf(__uint_as_float(sv[e]) * scale - lse_s[qg]) : 0.f;
+                p[e] = pe;
+                ds[e] = v ? pe * (__uint_as_float(pv[e]) - dv_s[qg]) : 0.f;
+            }
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                const int gi = ((c0 & 63) >> 3) + g;
+                uint4 pk, dk;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+                __nv_bfloat162* d2 = reinterpret_cast<__nv_bfloat162*>(&dk);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    p2[e] = __floats2bfloat162_rn(p[8 * g + 2 * e], p[8 * g + 2 * e + 1]);
+                    d2[e] = __floats2bfloat162_rn(ds[8 * g + 2 * e], ds[8 * g + 2 * e + 1]);
+                }
+                *reinterpret_cast<uint4*>(prow + ((gi ^ (r & 7)) << 4)) = pk;
+                *reinterpret_cast<uint4*>(drow + ((gi ^ (r & 7)) << 4)) = dk;
+            }
+        }
+        ptx::fence_proxy_async();  // generic-proxy P/dS writes -> tensor-core reads
+        ptx::tc_fence_before();
+        __syncthreads();
+        if (t == 0) {
+            ptx::tc_fence_after();
+            if (ok) {
+                mma2(j, i);
+                if (st + 1 < steps) mma1((st + 1) / nt, (st + 1) % nt);
+            }
+            ptx::mma_commit(mma_bar);
+        }
+    }
+    ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
+    ptx::tc_fence_after();
+    write_kv(nt - 1);
+    // dQ_i: warps of the first half write columns [0,32), the second [32,64)
+#pragma unroll 1
+    for (int i = 0; i < nt; i++) {
+        uint32_t v[32];
+        ptx::tmem_ld32(lane_base + 384 + 64 * i + half * 32, v);
+        ptx::tmem_ld_wait();
+        const int qg = i * kBT + r;
+        if (ok && qg < S) store_bf16x32(dqkv + (size_t)(row0 + qg) * ld_dqkv + h * kDh + half * 32, v, scale);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, 512);
+    }
+}
+
 typedef CUresult (*EncodeTiledFn2)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-bool attention_tc_supported(const AttnArgs& a) {
-    if (a.dtype != kBF16 || a.dh != 64 || a.S > kKeys || a.S <= 0) return false;
-    if ((reinterpret_cast<uintptr_t>(a.qkv) & 15) || (a.ld_qkv * 2) % 16) return false;
-    if ((reinterpret_cast<uintptr_t>(a.ctx) & 15) || (a.ld_ctx * 2) % 16) return false;
-    return true;
-}
-
-int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
+static EncodeTiledFn2 tmap_encoder() {
     static EncodeTiledFn2 enc = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -204,17 +448,37 @@ int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
             q == cudaDriverEntryPointSuccess)
             enc = reinterpret_cast<EncodeTiledFn2>(f);
     });
-    if (!enc) return -2;
-    CUtensorMap m;
-    const long long rows = (long long)a.B * a.S;
-    cuuint64_t dims[2] = {(cuuint64_t)(3LL * a.D), (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(a.ld_qkv * 2)};
+    return enc;
+}
+
+// 2D bf16 map over a row-major [rows, cols] matrix with row stride ld
+// elements, 64 x 128 boxes, 128-byte swizzle.
+static bool bf16_tmap(CUtensorMap* m, const void* base, long long cols, long long rows, long long ld) {
+    EncodeTiledFn2 enc = tmap_encoder();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
     cuuint32_t box[2] = {64, 128};
     cuuint32_t estr[2] = {1, 1};
-    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a.qkv), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return -2;
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool aligned16(const void* p, long long ld) {
+    return !(reinterpret_cast<uintptr_t>(p) & 15) && (ld * 2) % 16 == 0;
+}
+
+bool attention_tc_supported(const AttnArgs& a) {
+    if (a.dtype != kBF16 || a.dh != 64 || a.S > kKeys || a.S <= 0) return false;
+    if ((reinterpret_cast<uintptr_t>(a.qkv) & 15) || (a.ld_qkv * 2) % 16) return false;
+    if ((reinterpret_cast<uintptr_t>(a.ctx) & 15) || (a.ld_ctx * 2) % 16) return false;
+    return true;
+}
+
+int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
+    CUtensorMap m;
+    if (!bf16_tmap(&m, a.qkv, 3LL * a.D, (long long)a.B * a.S, a.ld_qkv)) return -2;
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(attn_tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
@@ -223,6 +487,30 @@ int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
     dim3 grid((a.S + kQ - 1) / kQ, a.H, a.B);
     attn_tc_fwd_kernel<<<grid, 128, kSmem, s>>>(m, a.S, a.H, a.D, a.scale, reinterpret_cast<__nv_bfloat16*>(a.ctx),
                                                  a.ld_ctx, a.lse, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+bool attention_tc_bwd_supported(const AttnArgs& a) {
+    if (a.dtype != kBF16 || a.dh != 64 || a.S > 2 * kBT || a.S <= 0 || !a.lse) return false;
+    return aligned16(a.qkv, a.ld_qkv) && aligned16(a.ctx, a.ld_ctx) && aligned16(a.dctx, a.ld_dctx) &&
+           aligned16(a.dqkv, a.ld_dqkv);
+}
+
+int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err) {
+    CUtensorMap mq, mo;
+    const long long rows = (long long)a.B * a.S;
+    if (!bf16_tmap(&mq, a.qkv, 3LL * a.D, rows, a.ld_qkv) || !bf16_tmap(&mo, a.dctx, a.D, rows, a.ld_dctx))
+        return -2;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(attn_tc_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+        attr = true;
+    }
+    dim3 grid(a.H, a.B);
+    attn_tc_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(
+        mq, mo, a.S, a.H, a.D, a.scale, reinterpret_cast<const __nv_bfloat16*>(a.ctx), a.ld_ctx,
+        reinterpret_cast<const __nv_bfloat16*>(a.dctx), a.ld_dctx, a.lse, reinterpret_cast<__nv_bfloat16*>(a.dqkv),
+        a.ld_dqkv, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

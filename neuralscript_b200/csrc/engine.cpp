@@ -789,7 +789,8 @@ static int backward(ns_model* m, int M) {
                 a.dqkv = op.dqkv;
                 a.ld_dqkv = 3LL * D;
                 a.dvec = op.dvec;
-                launch_counter() += 2;
+                a.err = m->d_err;
+                launch_counter() += attention_bwd_launches(a);
                 if ((rc = attention_bwd(a, m->stream))) {
                     rc = fail("attention backward launch failed");
                     break;
