@@ -68,6 +68,35 @@ __host__ __device__ __forceinline__ float act_deriv(float x, int code) {
     }
 }
 
+// GELU for the bf16 tensor-core path, from the rational approximation of
+// erf in Abramowitz & Stegun, Handbook of Mathematical Functions, 7.1.26
+// (|error| <= 1.5e-7):  for a >= 0,
+//   erfc(a) ~= t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2),  t = 1 / (1 + p a),
+// with p = 0.3275911, a1..a5 = 0.254829592, -0.284496736, 1.421413741,
+// -1.453152027, 1.061405429. With a = |x| / sqrt(2), Phi(x) = 1 - erfc(a)/2
+// for x >= 0 and erfc(a)/2 for x < 0; GELU(x) = x Phi(x) and
+// GELU'(x) = Phi(x) + x exp(-x^2/2) / sqrt(2 pi). exp and the reciprocal use
+// the hardware approximations. Its error (~1e-7 absolute in Phi) is far below
+// bf16 resolution; the fp32 and TF32 modes keep the exact erff form.
+__device__ __forceinline__ float as_phi(float x, float& g) {
+    const float a = fabsf(x) * 0.70710678f;
+    const float t = __fdividef(1.f, fmaf(0.3275911f, a, 1.f));
+    g = __expf(-a * a);  // exp(-x^2 / 2)
+    const float poly =
+        t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f), -0.284496736f), 0.254829592f);
+    const float q = 0.5f * poly * g;
+    return x >= 0.f ? 1.f - q : q;
+}
+__device__ __forceinline__ float gelu_fast(float x) {
+    float g;
+    return x * as_phi(x, g);
+}
+__device__ __forceinline__ float gelu_fast_deriv(float x) {
+    float g;
+    const float phi = as_phi(x, g);
+    return fmaf(x * g, 0.39894228f, phi);
+}
+
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 

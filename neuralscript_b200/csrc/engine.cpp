@@ -283,39 +283,52 @@ static int alloc_working(ns_model* m) {
     return 0;
 }
 
-// Refresh the working copies from the fp32 master blob.
-static int refresh_working(ns_model* m) {
+// Where weight wi's working copy lives (dst == nullptr: the GEMMs read the
+// fp32 master directly): a [rows, cols] view written at dst[r * ld + off + c].
+struct WkTarget {
+    void* dst = nullptr;
+    long long ld = 0;
+    int off = 0;
+    int rows = 1, cols = 0;
+};
+
+static WkTarget working_target(const ns_model* m, int wi) {
     const Spec& s = m->spec;
-    const int dt = m->wdt;
-    for (size_t li = 0; li < s.layers.size(); li++) {
-        const LayerSpec& l = s.layers[li];
-        int w0 = -1;
-        for (size_t wi = 0; wi < s.weights.size(); wi++)
-            if (s.weights[wi].layer == (int)li) {
-                w0 = (int)wi;
-                break;
-            }
-        if (w0 < 0) continue;
-        auto copy = [&](int wi) -> int {
-            if (!m->wk_owned[wi]) return 0;
-            const WeightInfo& w = s.weights[wi];
-            launch_counter() += 1;
-            return pack_weight(m->d_w + w.off, 1, (int)w.count, m->wk[wi], dt, (long long)w.count, 0, m->stream);
-        };
-        if (l.kind == "dense") {
-            if (copy(w0)) return -1;
-        } else if (l.kind == "attention") {
-            int d = (int)l.geti("dim", 0);
-            for (int g = 0; g < 3; g++) {
-                launch_counter() += 1;
-                if (pack_weight(m->d_w + s.weights[w0 + g].off, d, d, m->wk[w0], dt, 3LL * d, g * d, m->stream))
-                    return -1;
-            }
-            if (copy(w0 + 3)) return -1;
-        } else if (l.kind == "moe") {
-            if (copy(w0 + 1)) return -1;
-            if (l.gets("expert", "ffn") != "linear" && copy(w0 + 2)) return -1;
-        }
+    const WeightInfo& w = s.weights[wi];
+    WkTarget t;
+    if (w.layer < 0) return t;
+    const LayerSpec& l = s.layers[w.layer];
+    int w0 = wi;
+    while (w0 > 0 && s.weights[w0 - 1].layer == w.layer) w0--;
+    if (l.kind == "attention" && wi - w0 < 3) {
+        const int d = (int)l.geti("dim", 0);
+        t.dst = m->wk[w0];
+        t.ld = 3LL * d;
+        t.off = (wi - w0) * d;
+        t.rows = d;
+        t.cols = d;
+        return t;
+    }
+    if (l.kind != "dense" && l.kind != "attention" && l.kind != "moe") return t;
+    if (l.kind == "moe" && (wi == w0 || (wi == w0 + 2 && l.gets("expert", "ffn") == "linear"))) return t;
+    if (!m->wk_owned[wi]) return t;
+    t.dst = m->wk[wi];
+    t.ld = (long long)w.count;
+    t.rows = 1;
+    t.cols = (int)w.count;
+    return t;
+}
+
+// Refresh the working copies from the fp32 master blob (all of them, or
+// those not marked in `done`).
+static int refresh_working(ns_model* m, const std::vector<char>* done = nullptr) {
+    const Spec& s = m->spec;
+    for (size_t wi = 0; wi < s.weights.size(); wi++) {
+        if (done && (*done)[wi]) continue;
+        const WkTarget t = working_target(m, (int)wi);
+        if (!t.dst) continue;
+        launch_counter() += 1;
+        if (pack_weight(m->d_w + s.weights[wi].off, t.rows, t.cols, t.dst, m->wdt, t.ld, t.off, m->stream)) return -1;
     }
     return 0;
 }
@@ -690,7 +703,11 @@ static int backward(ns_model* m, int M) {
                 const WeightInfo& w = s.weights[op.widx];
                 const size_t n = (size_t)M * w.cols;
                 const void* dz;
-                if (op.act) {
+                if (op.act && op.dz_ready) {
+                    // the consumer's input-gradient GEMM already applied act'
+                    dz = m->wdt == kBF16 ? op.dz : (const void*)op.dz32;
+                    op.dz_ready = false;
+                } else if (op.act) {
                     launch_counter() += 1;
                     if (m->wdt == kBF16) {
                         rc = act_bwd(dv, op.z, kBF16, op.act, nullptr, n, nullptr,
@@ -701,6 +718,8 @@ static int backward(ns_model* m, int M) {
                         dz = op.dz32;
                     }
                     if (rc) break;
+                } else if (m->seed16 && oi == m->vals[m->out_val].producer) {
+                    dz = op.dz;  // the loss kernel wrote the bf16 seed here
                 } else {
                     dz = grad_operand(m, dv, op.dz, n);
                 }
@@ -721,6 +740,29 @@ static int backward(ns_model* m, int M) {
                     gx.K = w.cols;
                     gx.a = opnd(dz, m->wdt, w.cols, false);
                     gx.b = opnd(m->wk[op.widx], m->wdt, w.cols, false);
+                    // The input is a Dense layer's activation output consumed only
+                    // here: apply that layer's act' in this epilogue and write its
+                    // pre-activation gradient straight into its GEMM operand buffer.
+                    Op* P = in.producer >= 0 ? &m->ops[in.producer] : nullptr;
+                    if (P && !in.gcur && P->kind == OP_DENSE && P->act && !P->skip && P->self_out == op.in &&
+                        P->fused_res < 0 && in.consumers.size() == 1 && P->z &&
+                        (m->wdt == kBF16 ? P->dz != nullptr : P->dz32 != nullptr)) {
+                        gx.ep.dz = P->z;
+                        gx.ep.dz_dtype = m->wdt;
+                        gx.ep.ld_dz = w.rows;
+                        gx.ep.dz_act = P->act;
+                        if (m->wdt == kBF16) {
+                            gx.ep.c16 = reinterpret_cast<__nv_bfloat16*>(P->dz);
+                            gx.ep.ld_c16 = w.rows;
+                        } else {
+                            gx.ep.c32 = P->dz32;
+                            gx.ep.ld_c32 = w.rows;
+                        }
+                        if ((rc = run_gemm(m, gx))) break;
+                        P->dz_ready = true;
+                        in.gcur = in.gbuf;  // marks the gradient present; P reads its dz
+                        break;
+                    }
                     if (in.gcur) {
                         gx.ep.add = in.gcur;
                         gx.ep.ld_add = w.rows;
@@ -879,15 +921,22 @@ static int loss_and_seed(ns_model* m, int M, const float* labels, const int* tar
     Val& o = m->vals[m->out_val];
     const int C = o.cols;
     const float denom = (float)M * (float)m->world;
-    float* d32 = want_grad ? o.gbuf : nullptr;
+    // When the output comes straight from a Dense layer without activation
+    // or fused residual, its backward only needs the seed as a bf16 GEMM
+    // operand: the loss kernel writes it there and skips the fp32 copy.
+    const Op* prod = o.producer >= 0 ? &m->ops[o.producer] : nullptr;
+    m->seed16 = want_grad && m->wdt == kBF16 && prod && prod->kind == OP_DENSE && prod->act == 0 &&
+                prod->fused_res < 0 && prod->dz;
+    float* d32 = want_grad && !m->seed16 ? o.gbuf : nullptr;
+    __nv_bfloat16* d16 = m->seed16 ? reinterpret_cast<__nv_bfloat16*>(prod->dz) : nullptr;
     launch_counter() += 1;
     int rc;
     if (m->spec.loss == "mse") {
         if (!labels) return fail("mse loss needs dense targets");
-        rc = mse_fwd_bwd(o.f32, labels, M, C, want_grad ? (float)M * C * m->world : 1.f, m->d_rowloss, d32, nullptr,
+        rc = mse_fwd_bwd(o.f32, labels, M, C, want_grad ? (float)M * C * m->world : 1.f, m->d_rowloss, d32, d16,
                          m->stream);
     } else {
-        rc = cross_entropy_fwd_bwd(o.f32, labels, targets, M, C, denom, m->d_rowloss, d32, nullptr, m->stream);
+        rc = cross_entropy_fwd_bwd(o.f32, labels, targets, M, C, denom, m->d_rowloss, d32, d16, m->stream);
     }
     if (rc) return fail("loss kernel launch failed");
     if (want_grad) o.gcur = o.gbuf;
@@ -921,7 +970,7 @@ static int optimizer_step(ns_model* m, float lr) {
         omb2 = (float)(1.0 - B2);
     }
     std::vector<AdamTensor> at;
-    long long maxn = 0;
+    std::vector<char> fresh(s.weights.size(), 0);  // working copy written by the AdamW pass
     for (size_t wi = 0; wi < s.weights.size(); wi++) {
         const WeightInfo& w = s.weights[wi];
         const bool matrix = w.rows > 1 && w.cols > 1;
@@ -954,31 +1003,24 @@ static int optimizer_step(ns_model* m, float lr) {
             a.n = (long long)w.count;
             a.b1t = 1.f - powf(b1, (float)t);
             a.b2t = 1.f - powf(b2, (float)t);
+            const WkTarget wt = working_target(m, (int)wi);
+            if (wt.dst) {
+                a.wk = wt.dst;
+                a.wk_ld = wt.ld;
+                a.wk_cols = wt.cols;
+                a.wk_off = wt.off;
+                a.wk_bf16 = m->wdt == kBF16;
+                fresh[wi] = 1;
+            }
             at.push_back(a);
-            if (a.n > maxn) maxn = a.n;
         }
     }
     if (!at.empty()) {
-        if ((int)at.size() > m->adam_cap) {
-            if (m->d_adam) cudaFree(m->d_adam);
-            if (m->h_adam) cudaFreeHost(m->h_adam);
-    for (auto& r : m->regions) {
-        for (auto& ev : r.pending) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
-        for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
-    }
-            m->adam_cap = (int)at.size();
-            if (cudaMalloc(&m->d_adam, sizeof(AdamTensor) * at.size()) != cudaSuccess) return fail("alloc failed");
-            if (cudaMallocHost(&m->h_adam, sizeof(AdamTensor) * at.size()) != cudaSuccess) return fail("alloc failed");
-        }
-        cudaStreamSynchronize(m->stream);  // the pinned staging may still feed the previous copy
-        memcpy(m->h_adam, at.data(), sizeof(AdamTensor) * at.size());
-        cudaMemcpyAsync(m->d_adam, m->h_adam, sizeof(AdamTensor) * at.size(), cudaMemcpyHostToDevice, m->stream);
         AdamHyper h{lr, b1, b2, omb1, omb2, eps, dec};
-        launch_counter() += 1;
-        if (adamw_multi(reinterpret_cast<AdamTensor*>(m->d_adam), (int)at.size(), maxn, h, m->stream))
-            return fail("adamw launch failed");
+        launch_counter() += (at.size() + kAdamBatch - 1) / kAdamBatch;
+        if (adamw_multi(at.data(), (int)at.size(), h, m->stream)) return fail("adamw launch failed");
     }
-    return refresh_working(m);
+    return refresh_working(m, &fresh);
 }
 
 // X (r x c, fp32) -> out = NS5(X / ||X||). Uses m->d_ns as scratch.
@@ -1224,9 +1266,8 @@ void nsb_free(ns_model* m) {
     free_plan(m);
     free_working(m);
     for (void* p : {(void*)m->d_err, (void*)m->d_w, (void*)m->d_g, (void*)m->d_m, (void*)m->d_v, (void*)m->d_o,
-                    (void*)m->d_ns, (void*)m->d_active, m->d_adam})
+                    (void*)m->d_ns, (void*)m->d_active})
         if (p) cudaFree(p);
-    if (m->h_adam) cudaFreeHost(m->h_adam);
     for (auto& r : m->regions) {
         for (auto& ev : r.pending) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
         for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }

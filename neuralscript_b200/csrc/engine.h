@@ -61,6 +61,7 @@ struct Op {
     float* lse = nullptr;
     float* dvec = nullptr;
     MoeScratch* moe = nullptr;
+    bool dz_ready = false;  // backward: dz already holds act'(z) * dout (written by the consumer's GEMM)
 };
 
 }  // namespace nsb
@@ -83,9 +84,6 @@ struct ns_model {
     std::vector<void*> wk;   // working copy per weight index (nullptr when unused)
     std::vector<bool> wk_owned;
     std::vector<long long> adam_t;
-    void* d_adam = nullptr;  // device array of AdamTensor
-    int adam_cap = 0;
-    void* h_adam = nullptr;  // pinned staging for it
     // host mirror of the master blob
     mutable std::vector<float> h_w;
     mutable bool host_dirty = false;
@@ -96,6 +94,7 @@ struct ns_model {
     uint8_t* d_active = nullptr;
     std::mt19937 rng{0x9E3779B9u};
     long long lr_step = 0;
+    bool seed16 = false;  // last loss seed went to the output Dense layer's bf16 dz
     // graph
     std::vector<nsb::Val> vals;
     std::vector<nsb::Op> ops;

@@ -20,6 +20,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -58,30 +59,41 @@ __device__ __forceinline__ void epi_apply(const Epilogue& ep, int row, int col, 
     if (ep.c16) ep.c16[(size_t)orow * ep.ld_c16 + col] = f2bf(v);
 }
 
-// 32 consecutive columns of one row, 16-byte vectorised (all leading
-// dimensions multiples of 8 elements, col0 a multiple of 32, col0+32 <= N).
-__device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int col0, float* v) {
+// Epilogue of 32 consecutive columns of one row held in registers, split in
+// the order the outputs need it: pre() = alpha, residual, row scale and
+// activation derivative (the value stored as z), act() = the activation.
+// ncols < 32 marks a ragged last chunk (scalar, guarded loads); full chunks
+// use 16-byte loads (leading dimensions multiples of 8 elements, col0 a
+// multiple of 32).
+template <bool FAST>
+__device__ __forceinline__ void epi_pre32(const Epilogue& ep, int row, int col0, float* v, int ncols) {
 #pragma unroll
     for (int j = 0; j < 32; j++) v[j] *= ep.alpha;
     if (ep.add) {
-        const float4* a = reinterpret_cast<const float4*>(ep.add + (size_t)row * ep.ld_add + col0);
+        const float* a = ep.add + (size_t)row * ep.ld_add + col0;
+        if (ncols == 32) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            float4 t = a[j];
-            v[4 * j] += ep.add_scale * t.x;
-            v[4 * j + 1] += ep.add_scale * t.y;
-            v[4 * j + 2] += ep.add_scale * t.z;
-            v[4 * j + 3] += ep.add_scale * t.w;
+            for (int j = 0; j < 8; j++) {
+                float4 t = reinterpret_cast<const float4*>(a)[j];
+                v[4 * j] += ep.add_scale * t.x;
+                v[4 * j + 1] += ep.add_scale * t.y;
+                v[4 * j + 2] += ep.add_scale * t.z;
+                v[4 * j + 3] += ep.add_scale * t.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (j < ncols) v[j] += ep.add_scale * a[j];
         }
     }
     if (ep.row_scale) {
-        float s = ep.row_scale[row];
+        float sc = ep.row_scale[row];
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] *= s;
+        for (int j = 0; j < 32; j++) v[j] *= sc;
     }
     if (ep.dz) {
         float z[32];
-        if (ep.dz_dtype == kBF16) {
+        if (ncols == 32 && ep.dz_dtype == kBF16) {
             const uint4* a = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ep.dz) +
                                                             (size_t)row * ep.ld_dz + col0);
 #pragma unroll
@@ -91,7 +103,7 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
 #pragma unroll
                 for (int q = 0; q < 8; q++) z[8 * j + q] = bf2f(h[q]);
             }
-        } else {
+        } else if (ncols == 32) {
             const float4* a = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ep.dz) +
                                                               (size_t)row * ep.ld_dz + col0);
 #pragma unroll
@@ -102,6 +114,10 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
                 z[4 * j + 2] = t.z;
                 z[4 * j + 3] = t.w;
             }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                z[j] = j < ncols ? ld_any(ep.dz, ep.dz_dtype, (size_t)row * ep.ld_dz + col0 + j) : 0.f;
         }
         switch (ep.dz_act) {
             case kRelu:
@@ -110,31 +126,18 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
                 break;
             case kGelu:
 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], kGelu);
+                for (int j = 0; j < 32; j++) v[j] *= FAST ? gelu_fast_deriv(z[j]) : act_deriv(z[j], kGelu);
                 break;
             default:
 #pragma unroll
                 for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], ep.dz_act);
         }
     }
-    if (ep.z) {
-        if (ep.z_dtype == kBF16) {
-            uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ep.z) + (size_t)row * ep.ld_z + col0);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                uint4 t;
-                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&t);
-#pragma unroll
-                for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
-                o[j] = t;
-            }
-        } else {
-            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.z) + (size_t)row * ep.ld_z + col0);
-#pragma unroll
-            for (int j = 0; j < 8; j++) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
-    }
-    switch (ep.act) {
+}
+
+template <bool FAST>
+__device__ __forceinline__ void epi_act32(int act, float* v) {
+    switch (act) {
         case kIdentity:
             break;
         case kRelu:
@@ -143,7 +146,7 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
             break;
         case kGelu:
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], kGelu);
+            for (int j = 0; j < 32; j++) v[j] = FAST ? gelu_fast(v[j]) : act_fwd(v[j], kGelu);
             break;
         case kGeluMoe:
 #pragma unroll
@@ -151,25 +154,40 @@ __device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int
             break;
         default:
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], ep.act);
+            for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], act);
     }
+}
+
+__device__ __forceinline__ void store32_f32(float* dst, const float* v) {
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+__device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float* v) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        uint4 t;
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&t);
+#pragma unroll
+        for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
+        reinterpret_cast<uint4*>(dst)[j] = t;
+    }
+}
+
+// Full 32-column chunk with direct (per-row) stores.
+template <bool FAST>
+__device__ __forceinline__ void epi_apply32_vec(const Epilogue& ep, int row, int col0, float* v) {
+    epi_pre32<FAST>(ep, row, col0, v, 32);
+    if (ep.z) {
+        if (ep.z_dtype == kBF16)
+            store32_bf16(reinterpret_cast<__nv_bfloat16*>(ep.z) + (size_t)row * ep.ld_z + col0, v);
+        else
+            store32_f32(reinterpret_cast<float*>(ep.z) + (size_t)row * ep.ld_z + col0, v);
+    }
+    epi_act32<FAST>(ep.act, v);
     int orow = ep.out_rows ? ep.out_rows[row] : row;
-    if (ep.c32) {
-        float4* o = reinterpret_cast<float4*>(ep.c32 + (size_t)orow * ep.ld_c32 + col0);
-#pragma unroll
-        for (int j = 0; j < 8; j++) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    }
-    if (ep.c16) {
-        uint4* o = reinterpret_cast<uint4*>(ep.c16 + (size_t)orow * ep.ld_c16 + col0);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            uint4 t;
-            __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&t);
-#pragma unroll
-            for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
-            o[j] = t;
-        }
-    }
+    if (ep.c32) store32_f32(ep.c32 + (size_t)orow * ep.ld_c32 + col0, v);
+    if (ep.c16) store32_bf16(ep.c16 + (size_t)orow * ep.ld_c16 + col0, v);
 }
 
 // ---------------------------------------------------------------------------
@@ -188,6 +206,7 @@ struct TcParams {
     const int* seg;
     const int* seg_end;
     int max_m_tiles_per_group;
+    int tma_out;  // outputs leave through the TMA-store epilogue (tz / tc32 / tc16)
 };
 
 template <int BN, bool TF32>
@@ -207,7 +226,9 @@ struct TcCfg {
     // 32-byte-granule variant (4-row atoms, SBO 512).
     static constexpr uint32_t MN_LAYOUT = TF32 ? 1 : 2;
     static constexpr uint32_t MN_SBO = TF32 ? 512 : 1024;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    // epilogue staging: per epilogue warp two 2 KB buffers (32 rows x 64 B)
+    static constexpr int STAGING = 8 * 2 * 2048;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 // Decode a work unit into (m0, n0, kb0, kb1, split, group); returns false
@@ -246,12 +267,16 @@ constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + e
 
 template <int BN, bool TF32, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const TcParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                   const __grid_constant__ CUtensorMap tz, const __grid_constant__ CUtensorMap tc32,
+                   const __grid_constant__ CUtensorMap tc16, const TcParams p) {
     using C = TcCfg<BN, TF32>;
+    static_assert(kEpiWarps == 8, "staging is sized for 8 epilogue warps");
     constexpr uint32_t IDESC = ptx::instr_desc(TF32 ? 2 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0, C::BM, BN);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+    uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING);
     uint64_t* empty = full + C::STAGES;
     uint64_t* acc_full = empty + C::STAGES;
     uint64_t* acc_empty = acc_full + 2;
@@ -272,6 +297,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0 && lane == 0) {
         ptx::prefetch_tmap(&ta);
         ptx::prefetch_tmap(&tb);
+        if (p.tma_out) {
+            if (p.ep.z) ptx::prefetch_tmap(&tz);
+            if (p.ep.c32) ptx::prefetch_tmap(&tc32);
+            if (p.ep.c16) ptx::prefetch_tmap(&tc16);
+        }
     }
     if (warp == 1) {
         ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -379,6 +409,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int half = (warp - 2) >> 2;
         const int r_in_tile = lane_grp * 32 + lane;
         constexpr int HALF_COLS = BN / 2;
+        constexpr bool FAST = !TF32;
+        // TMA-store staging: two 2 KB buffers of 32 rows x 64 bytes, 64-byte
+        // swizzle (16-byte granule j of row r at j ^ ((r >> 1) & 3)), which is
+        // also conflict-free for the row-per-thread writes
+        uint8_t* stg = staging + (warp - 2) * 4096;
+        int sbuf = 0;
+        auto stage_store = [&](const CUtensorMap* map, const uint4* g4, int x, int y) {
+            uint8_t* buf = stg + sbuf * 2048;
+            if (lane == 0) ptx::bulk_wait_read1();
+            __syncwarp();
+            uint8_t* rowp = buf + lane * 64;
+#pragma unroll
+            for (int j = 0; j < 4; j++) *reinterpret_cast<uint4*>(rowp + ((j ^ ((lane >> 1) & 3)) << 4)) = g4[j];
+            ptx::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                ptx::tma_store_2d(map, buf, x, y);
+                ptx::bulk_commit();
+            }
+            sbuf ^= 1;
+        };
+        // boxes that start at or beyond N are not issued (the first one of a
+        // chunk always starts inside: col0 < N)
+        auto out_f32 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
+            stage_store(map, reinterpret_cast<const uint4*>(v), col0, y);
+            if (col0 + 16 < p.N) stage_store(map, reinterpret_cast<const uint4*>(v + 16), col0 + 16, y);
+        };
+        auto out_bf16 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
+            uint4 g4[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&g4[j]);
+#pragma unroll
+                for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
+            }
+            stage_store(map, g4, col0, y);
+        };
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
@@ -394,24 +461,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + acc * BN + c, r);
                 ptx::tmem_ld_wait();
                 const int col0 = n0 + c;
-                if (!row_ok || col0 >= p.N) continue;
+                if (col0 >= p.N) continue;  // uniform across the warp
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+                if (p.tma_out) {
+                    // rows >= M and columns >= N of a box are clipped by the
+                    // store; a 32-row slab entirely past M issues nothing
+                    const int y = m0 + lane_grp * 32;
+                    if (y >= p.M) continue;
+                    const int nc = col0 + 32 <= p.N ? 32 : p.N - col0;
+                    if (row_ok) epi_pre32<FAST>(p.ep, row, col0, v, nc);
+                    if (p.ep.z) {
+                        if (p.ep.z_dtype == kBF16) out_bf16(&tz, v, col0, y);
+                        else out_f32(&tz, v, col0, y);
+                    }
+                    epi_act32<FAST>(p.ep.act, v);
+                    if (p.ep.c32) out_f32(&tc32, v, col0, y);
+                    if (p.ep.c16) out_bf16(&tc16, v, col0, y);
+                    continue;
+                }
+                if (!row_ok) continue;
                 const bool full = p.vec_ok && col0 + 32 <= p.N;
                 if (p.splits > 1) {
                     float* w = p.workspace + ((size_t)split * p.M + row) * p.N + col0;
                     if (full) {
-#pragma unroll
-                        for (int j = 0; j < 8; j++)
-                            reinterpret_cast<float4*>(w)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        store32_f32(w, v);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; j++)
                             if (col0 + j < p.N) w[j] = v[j];
                     }
                 } else if (full) {
-                    epi_apply32_vec(p.ep, row, col0, v);
+                    epi_apply32_vec<FAST>(p.ep, row, col0, v);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; j++)
@@ -423,6 +505,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1;
         }
+        if (p.tma_out && lane == 0) ptx::bulk_wait_all();
     }
 
     ptx::tc_fence_before();
@@ -569,6 +652,22 @@ static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner
     return r == CUDA_SUCCESS;
 }
 
+// Output map for the TMA-store epilogue: row-major [rows, cols] with leading
+// dimension ld; 32-row boxes of 64 bytes (16 fp32 or 32 bf16), 64-byte swizzle.
+static bool make_out_map(CUtensorMap* m, const void* ptr, int dtype, long long cols, long long rows, long long ld) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return false;
+    const int es = dtype == kBF16 ? 2 : 4;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+    cuuint32_t box[2] = {(cuuint32_t)(64 / es), 32};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+               const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static bool operand_tc_ok(const GemmOperand& o) {
     const int es = o.dtype == kBF16 ? 2 : 4;
     if ((reinterpret_cast<uintptr_t>(o.ptr) & 15) != 0) return false;
@@ -616,8 +715,13 @@ size_t gemm_workspace_floats(const GemmDesc& d) {
     return splits > 1 ? (size_t)splits * d.M * d.N : 0;
 }
 
+struct OutMaps {
+    CUtensorMap z, c32, c16;
+};
+
 template <int BN, bool TF32, bool A_MN, bool B_MN>
-static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t s) {
+static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om, const TcParams& p,
+                             cudaStream_t s) {
     using C = TcCfg<BN, TF32>;
     auto k = gemm_tc_kernel<BN, TF32, A_MN, B_MN>;
     static bool attr = false;
@@ -627,17 +731,17 @@ static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const
     }
     int grid = min(p.total_units, num_sms());
     if (grid <= 0) return cudaSuccess;
-    k<<<grid, kTcThreads, C::SMEM, s>>>(ta, tb, p);
+    k<<<grid, kTcThreads, C::SMEM, s>>>(ta, tb, om.z, om.c32, om.c16, p);
     return cudaGetLastError();
 }
 
 template <int BN, bool TF32>
-static cudaError_t launch_tc_majors(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, bool amn,
-                                    bool bmn, cudaStream_t s) {
-    if (!amn && !bmn) return launch_tc<BN, TF32, false, false>(ta, tb, p, s);
-    if (!amn && bmn) return launch_tc<BN, TF32, false, true>(ta, tb, p, s);
-    if (amn && !bmn) return launch_tc<BN, TF32, true, false>(ta, tb, p, s);
-    return launch_tc<BN, TF32, true, true>(ta, tb, p, s);
+static cudaError_t launch_tc_majors(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps& om,
+                                    const TcParams& p, bool amn, bool bmn, cudaStream_t s) {
+    if (!amn && !bmn) return launch_tc<BN, TF32, false, false>(ta, tb, om, p, s);
+    if (!amn && bmn) return launch_tc<BN, TF32, false, true>(ta, tb, om, p, s);
+    if (amn && !bmn) return launch_tc<BN, TF32, true, false>(ta, tb, om, p, s);
+    return launch_tc<BN, TF32, true, true>(ta, tb, om, p, s);
 }
 
 static bool ep_vec_ok(const GemmDesc& d) {
@@ -697,13 +801,25 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     } else {
         p.total_units = p.m_tiles * p.n_tiles * p.splits;
     }
+    // TMA-store epilogue: plain row-major outputs of a single (non-split,
+    // non-grouped, non-scattered) GEMM; the store clips rows >= M, cols >= N
+    OutMaps om;
+    memset(&om, 0, sizeof(om));
+    p.tma_out = 0;
+    if (p.vec_ok && d.groups == 1 && p.splits == 1 && !d.ep.out_rows && (d.ep.z || d.ep.c32 || d.ep.c16)) {
+        bool okm = true;
+        if (d.ep.z) okm = okm && make_out_map(&om.z, d.ep.z, d.ep.z_dtype, d.N, d.M, d.ep.ld_z);
+        if (d.ep.c32) okm = okm && make_out_map(&om.c32, d.ep.c32, kF32, d.N, d.M, d.ep.ld_c32);
+        if (d.ep.c16) okm = okm && make_out_map(&om.c16, d.ep.c16, kBF16, d.N, d.M, d.ep.ld_c16);
+        p.tma_out = okm ? 1 : 0;
+    }
     cudaError_t e;
     if (bn == 256) {
-        e = tf32 ? launch_tc_majors<256, true>(ta, tb, p, d.a.mn_major, d.b.mn_major, s)
-                 : launch_tc_majors<256, false>(ta, tb, p, d.a.mn_major, d.b.mn_major, s);
+        e = tf32 ? launch_tc_majors<256, true>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s)
+                 : launch_tc_majors<256, false>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s);
     } else {
-        e = tf32 ? launch_tc_majors<128, true>(ta, tb, p, d.a.mn_major, d.b.mn_major, s)
-                 : launch_tc_majors<128, false>(ta, tb, p, d.a.mn_major, d.b.mn_major, s);
+        e = tf32 ? launch_tc_majors<128, true>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s)
+                 : launch_tc_majors<128, false>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s);
     }
     if (e != cudaSuccess) return -5;
     if (p.splits > 1) {

@@ -526,11 +526,101 @@ __global__ void __launch_bounds__(256) ce_kernel(const float* __restrict__ logit
     }
 }
 
+// Single-pass form for rows of C = 1024*NV classes: 256 threads hold the
+// row in registers (NV float4 each), so the logits are read once and the
+// gradient written once.
+template <int NV>
+__global__ void __launch_bounds__(256) ce_rows_vec_kernel(const float* __restrict__ logits,
+                                                          const float* __restrict__ labels,
+                                                          const int* __restrict__ targets, int M, float denom,
+                                                          float* __restrict__ row_loss, float* __restrict__ d32,
+                                                          __nv_bfloat16* __restrict__ d16) {
+    constexpr int C = 1024 * NV;
+    __shared__ float sh[33];
+    for (int r = blockIdx.x; r < M; r += gridDim.x) {
+        const float4* x4 = reinterpret_cast<const float4*>(logits + (size_t)r * C);
+        float4 e[NV];
+#pragma unroll
+        for (int v = 0; v < NV; v++) e[v] = __ldcs(x4 + v * 256 + threadIdx.x);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int v = 0; v < NV; v++) mx = fmaxf(fmaxf(mx, fmaxf(e[v].x, e[v].y)), fmaxf(e[v].z, e[v].w));
+        mx = block_max(mx, sh);
+        // exp of arguments in [-inf, 0] through the hardware exp2 path
+        // (__expf: a few ulp here, far inside the tolerances) and one
+        // reciprocal per row: this kernel moves 3/4 of a GB per step, and
+        // with the accurate expf and two divisions per element it is bound
+        // by instruction issue rather than by HBM.
+        float se = 0.f;
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            e[v].x = __expf(e[v].x - mx);
+            e[v].y = __expf(e[v].y - mx);
+            e[v].z = __expf(e[v].z - mx);
+            e[v].w = __expf(e[v].w - mx);
+            se += (e[v].x + e[v].y) + (e[v].z + e[v].w);
+        }
+        se = block_sum(se, sh);
+        const float inv_se = 1.f / se, inv_denom = 1.f / denom;
+        const int t = targets ? targets[r] : -1;
+        float loss = 0.f;
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            const int j0 = 4 * (v * 256 + threadIdx.x);
+            float4 y;
+            if (labels) {
+                y = __ldcs(reinterpret_cast<const float4*>(labels + (size_t)r * C) + v * 256 + threadIdx.x);
+            } else {
+                y.x = j0 == t ? 1.f : 0.f;
+                y.y = j0 + 1 == t ? 1.f : 0.f;
+                y.z = j0 + 2 == t ? 1.f : 0.f;
+                y.w = j0 + 3 == t ? 1.f : 0.f;
+            }
+            float4 p;
+            p.x = e[v].x * inv_se;
+            p.y = e[v].y * inv_se;
+            p.z = e[v].z * inv_se;
+            p.w = e[v].w * inv_se;
+            if (y.x > 0.f) loss -= logf(p.x);
+            if (y.y > 0.f) loss -= logf(p.y);
+            if (y.z > 0.f) loss -= logf(p.z);
+            if (y.w > 0.f) loss -= logf(p.w);
+            float4 d;
+            d.x = (p.x - y.x) * inv_denom;
+            d.y = (p.y - y.y) * inv_denom;
+            d.z = (p.z - y.z) * inv_denom;
+            d.w = (p.w - y.w) * inv_denom;
+            if (d32) __stcs(reinterpret_cast<float4*>(d32 + (size_t)r * C) + v * 256 + threadIdx.x, d);
+            if (d16) {
+                __nv_bfloat162 a = __floats2bfloat162_rn(d.x, d.y), b = __floats2bfloat162_rn(d.z, d.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&a);
+                u.y = *reinterpret_cast<uint32_t*>(&b);
+                __stcs(reinterpret_cast<uint2*>(d16 + (size_t)r * C) + v * 256 + threadIdx.x, u);
+            }
+        }
+        loss = block_sum(loss, sh);
+        if (threadIdx.x == 0) row_loss[r] = loss;
+    }
+}
+
 int cross_entropy_fwd_bwd(const float* logits, const float* labels, const int* targets, int M, int C, float denom,
                           float* row_loss, float* d32, __nv_bfloat16* d16, cudaStream_t s) {
     if (M <= 0) return 0;
+    const bool vec = C % 1024 == 0 && C <= 16384 && aligned16(logits) && (!labels || aligned16(labels)) &&
+                     (!d32 || aligned16(d32)) && (!d16 || (reinterpret_cast<uintptr_t>(d16) & 7) == 0);
     unsigned g = (unsigned)min(M, num_sms() * 8);
-    ce_kernel<<<g, 256, 0, s>>>(logits, labels, targets, M, C, denom, row_loss, d32, d16);
+    if (vec) {
+        switch (C / 1024) {
+#define NSB_CE(NV) \
+    case NV: ce_rows_vec_kernel<NV><<<g, 256, 0, s>>>(logits, labels, targets, M, denom, row_loss, d32, d16); break;
+            NSB_CE(1) NSB_CE(2) NSB_CE(3) NSB_CE(4) NSB_CE(5) NSB_CE(6) NSB_CE(7) NSB_CE(8)
+            NSB_CE(9) NSB_CE(10) NSB_CE(11) NSB_CE(12) NSB_CE(13) NSB_CE(14) NSB_CE(15) NSB_CE(16)
+#undef NSB_CE
+        }
+    } else {
+        ce_kernel<<<g, 256, 0, s>>>(logits, labels, targets, M, C, denom, row_loss, d32, d16);
+    }
     return launch_ok();
 }
 
@@ -677,37 +767,111 @@ int pack_weight(const float* src, int rows, int cols, void* dst, int dst_dtype, 
 // Optimizers
 // ---------------------------------------------------------------------------
 // codegen.cpp:3108-3120 per element.
+__device__ __forceinline__ float adamw_elem(float w, float gg, float& m, float& v, float b1t, float b2t,
+                                            const AdamHyper& h) {
+    m = h.beta1 * m + h.one_minus_beta1 * gg;
+    v = h.beta2 * v + h.one_minus_beta2 * gg * gg;
+    const float mh = m / b1t, vh = v / b2t;
+    return w - ((h.lr * mh / (sqrtf(vh) + h.eps)) + (h.decay * h.lr) * w);
+}
+
+__device__ __forceinline__ long long wk_index(const AdamTensor& t, long long i) {
+    const long long r = i / t.wk_cols, c = i - r * t.wk_cols;
+    return r * t.wk_ld + t.wk_off + c;
+}
+
 __device__ __forceinline__ void adamw_body(const AdamTensor& t, const AdamHyper& h) {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < t.n; i += (long long)gridDim.x * blockDim.x) {
-        const float gg = t.g[i];
-        const float m = h.beta1 * t.m[i] + h.one_minus_beta1 * gg;
-        const float v = h.beta2 * t.v[i] + h.one_minus_beta2 * gg * gg;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const long long first = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (t.vec4) {
+        const long long n4 = t.n >> 2;
+        for (long long i = first; i < n4; i += stride) {
+            const float4 g = __ldcs(reinterpret_cast<const float4*>(t.g) + i);
+            float4 m = __ldcs(reinterpret_cast<const float4*>(t.m) + i);
+            float4 v = __ldcs(reinterpret_cast<const float4*>(t.v) + i);
+            float4 w = __ldcs(reinterpret_cast<const float4*>(t.w) + i);
+            w.x = adamw_elem(w.x, g.x, m.x, v.x, t.b1t, t.b2t, h);
+            w.y = adamw_elem(w.y, g.y, m.y, v.y, t.b1t, t.b2t, h);
+            w.z = adamw_elem(w.z, g.z, m.z, v.z, t.b1t, t.b2t, h);
+            w.w = adamw_elem(w.w, g.w, m.w, v.w, t.b1t, t.b2t, h);
+            __stcs(reinterpret_cast<float4*>(t.m) + i, m);
+            __stcs(reinterpret_cast<float4*>(t.v) + i, v);
+            reinterpret_cast<float4*>(t.w)[i] = w;
+            if (t.wk) {
+                const long long o = wk_index(t, 4 * i);
+                if (t.wk_bf16) {
+                    __nv_bfloat162 a = __floats2bfloat162_rn(w.x, w.y), b = __floats2bfloat162_rn(w.z, w.w);
+                    uint2 u;
+                    u.x = *reinterpret_cast<uint32_t*>(&a);
+                    u.y = *reinterpret_cast<uint32_t*>(&b);
+                    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(t.wk) + o) = u;
+                } else {
+                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(t.wk) + o) = w;
+                }
+            }
+        }
+        return;
+    }
+    for (long long i = first; i < t.n; i += stride) {
+        float m = t.m[i], v = t.v[i];
+        const float w = adamw_elem(t.w[i], t.g[i], m, v, t.b1t, t.b2t, h);
         t.m[i] = m;
         t.v[i] = v;
-        const float mh = m / t.b1t, vh = v / t.b2t;
-        const float w = t.w[i];
-        t.w[i] = w - ((h.lr * mh / (sqrtf(vh) + h.eps)) + (h.decay * h.lr) * w);
+        t.w[i] = w;
+        if (t.wk) {
+            const long long o = wk_index(t, i);
+            if (t.wk_bf16) reinterpret_cast<__nv_bfloat16*>(t.wk)[o] = f2bf(w);
+            else reinterpret_cast<float*>(t.wk)[o] = w;
+        }
     }
 }
 
+struct AdamBatch {
+    AdamTensor t[kAdamBatch];
+};
+
 // blockIdx.y selects the tensor
-__global__ void adamw_kernel(const AdamTensor* __restrict__ ts, AdamHyper h) { adamw_body(ts[blockIdx.y], h); }
+__global__ void __launch_bounds__(256) adamw_batch_kernel(const __grid_constant__ AdamBatch b, AdamHyper h) {
+    adamw_body(b.t[blockIdx.y], h);
+}
 __global__ void adamw_single_kernel(AdamTensor t, AdamHyper h) { adamw_body(t, h); }
+
+void adamw_prepare(AdamTensor& t) {
+    const bool a16 = aligned16(t.w) && aligned16(t.g) && aligned16(t.m) && aligned16(t.v);
+    bool ok = a16 && t.n % 4 == 0;
+    if (ok && t.wk) {
+        const uintptr_t al = t.wk_bf16 ? 8 : 16;
+        ok = t.wk_cols % 4 == 0 && t.wk_ld % 4 == 0 && t.wk_off % 4 == 0 &&
+             (reinterpret_cast<uintptr_t>(t.wk) & (al - 1)) == 0;
+    }
+    t.vec4 = ok ? 1 : 0;
+}
 
 int adamw_single(AdamTensor t, AdamHyper h, cudaStream_t s) {
     if (t.n <= 0) return 0;
-    adamw_single_kernel<<<grid_for((size_t)t.n, 256), 256, 0, s>>>(t, h);
+    adamw_prepare(t);
+    adamw_single_kernel<<<grid_for((size_t)(t.vec4 ? t.n / 4 : t.n), 256), 256, 0, s>>>(t, h);
     return launch_ok();
 }
 
-int adamw_multi(const AdamTensor* dev_tensors, int count, long long max_n, AdamHyper h, cudaStream_t s) {
-    if (count <= 0) return 0;
-    long long blocks = (max_n + 255) / 256, cap = (long long)num_sms() * 4;
-    unsigned gx = (unsigned)(blocks < cap ? blocks : cap);
-    if (gx == 0) gx = 1;
-    dim3 grid(gx, count);
-    adamw_kernel<<<grid, 256, 0, s>>>(dev_tensors, h);
-    return launch_ok();
+int adamw_multi(const AdamTensor* ts, int count, AdamHyper h, cudaStream_t s) {
+    for (int b0 = 0; b0 < count; b0 += kAdamBatch) {
+        const int nb = count - b0 < kAdamBatch ? count - b0 : kAdamBatch;
+        AdamBatch batch;
+        long long maxw = 0;
+        for (int i = 0; i < nb; i++) {
+            batch.t[i] = ts[b0 + i];
+            adamw_prepare(batch.t[i]);
+            const long long wn = batch.t[i].vec4 ? batch.t[i].n / 4 : batch.t[i].n;
+            if (wn > maxw) maxw = wn;
+        }
+        if (maxw <= 0) continue;
+        long long blocks = (maxw + 255) / 256, cap = (long long)num_sms() * 4;
+        dim3 grid((unsigned)(blocks < cap ? blocks : cap), nb);
+        adamw_batch_kernel<<<grid, 256, 0, s>>>(batch, h);
+        if (launch_ok()) return -5;
+    }
+    return 0;
 }
 
 __global__ void muon_momentum_kernel(float* m, const float* g, long long n, float mu) {

@@ -65,14 +65,27 @@ struct AdamTensor {
     long long n;
     float b1t;  // 1 - beta1^t
     float b2t;  // 1 - beta2^t
+    // optional working copy refreshed from the updated weight in the same
+    // pass: element i = (r, c) of a [n / wk_cols, wk_cols] view goes to
+    // wk[r * wk_ld + wk_off + c] (bf16 when wk_bf16, else fp32)
+    void* wk = nullptr;
+    long long wk_ld = 0;
+    int wk_cols = 0;
+    int wk_off = 0;
+    int wk_bf16 = 0;
+    int vec4 = 0;  // all streams 16-byte aligned, n and the copy layout multiples of 4
 };
 struct AdamHyper {
     float lr, beta1, beta2, one_minus_beta1, one_minus_beta2, eps, decay;
 };
+// Sets t.vec4 from the pointers and layout.
+void adamw_prepare(AdamTensor& t);
 // One tensor, descriptor passed by value.
 int adamw_single(AdamTensor t, AdamHyper h, cudaStream_t s);
-// One launch over all tensors (device array of AdamTensor).
-int adamw_multi(const AdamTensor* dev_tensors, int count, long long max_n, AdamHyper h, cudaStream_t s);
+// All tensors in launches of up to kAdamBatch descriptors passed as kernel
+// parameters (no staging copy, no host synchronisation).
+constexpr int kAdamBatch = 40;
+int adamw_multi(const AdamTensor* host_tensors, int count, AdamHyper h, cudaStream_t s);
 
 // m = momentum * m + g
 int muon_momentum(float* m, const float* g, long long n, float momentum, cudaStream_t s);

@@ -3,6 +3,7 @@ kernel-level C-ABI (include/ns_b200_ops.h) on synthetic operands, with CUDA
 events on the launching stream after warm-up.
 
     python -m neuralscript_b200.kbench gemm --M 16384 --N 2048 --K 512 --act gelu
+    python -m neuralscript_b200.kbench gemm --M 16384 --N 8192 --K 512 --out f32
     python -m neuralscript_b200.kbench attention --B 64 --S 256 --H 8 --D 512
     python -m neuralscript_b200.kbench layernorm --M 16384 --D 512
 
@@ -41,20 +42,27 @@ def _time(fn, iters, warmup=3):
     return e0.elapsed_time(e1) / iters / 1e3
 
 
-def gemm_case(M, N, K, act="none", dtype="bf16", iters=20):
-    """The engine's forward layout: A [M,K] K-major, W [K,N] row-major (MN-major B)."""
+def gemm_case(M, N, K, act="none", dtype="bf16", iters=20, out="bf16", residual=False):
+    """The engine's forward layout: A [M,K] K-major, W [K,N] row-major (MN-major B);
+    output bf16 or fp32, optionally plus an fp32 residual [M,N]."""
     import torch
     from . import ops as O
     dt = torch.bfloat16 if dtype == "bf16" else torch.float32
     A = torch.randn(M, K, device="cuda").to(dt)
     B = torch.randn(K, N, device="cuda").to(dt)
-    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    t = _time(lambda: O.gemm(A, B, M, N, K, K, 0, N, 1, act=ACTS[act], c16=C), iters)
+    kw = {"act": ACTS[act]}
+    if out == "bf16":
+        kw["c16"] = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    else:
+        kw["c32"] = torch.empty(M, N, device="cuda")
+    if residual:
+        kw["add"] = torch.randn(M, N, device="cuda")
+    t = _time(lambda: O.gemm(A, B, M, N, K, K, 0, N, 1, **kw), iters)
     pk, kind = _peaks()
     tf = 2.0 * M * N * K / t / 1e12
-    return {"kernel": "gemm", "M": M, "N": N, "K": K, "act": act, "dtype": dtype, "us": t * 1e6,
-            "tflops": tf, "frac_of_bf16_peak": tf / pk["bf16_tflops"], "peak_kind": kind,
-            "tensor_cores": O.uses_tensor_cores(A, B, M, N, K, K, 0, N, 1)}
+    return {"kernel": "gemm", "M": M, "N": N, "K": K, "act": act, "dtype": dtype, "out": out,
+            "residual": residual, "us": t * 1e6, "tflops": tf, "frac_of_bf16_peak": tf / pk["bf16_tflops"],
+            "peak_kind": kind, "tensor_cores": O.uses_tensor_cores(A, B, M, N, K, K, 0, N, 1)}
 
 
 def attention_case(B, S, H, D, iters=20, backward=False):
@@ -102,9 +110,11 @@ def main():
     ap.add_argument("--D", type=int, default=512)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--backward", action="store_true")
+    ap.add_argument("--out", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--residual", action="store_true")
     a = ap.parse_args()
     if a.kernel == "gemm":
-        r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters)
+        r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters, a.out, a.residual)
     elif a.kernel == "attention":
         r = attention_case(a.B, a.S, a.H, a.D, a.iters, a.backward)
     else:
