@@ -251,7 +251,8 @@ def region_work(spec, label, M, train):
         l = s.layer(lname)
     except KeyError:
         if label == "loss":
-            return "bytes", M * 8192 * (4 + (4 if train else 0))
+            # fp32 logits read; training also writes the bf16 seed gradient
+            return "bytes", M * 8192 * (4 + (2 if train else 0))
         if label == "optimizer":
             return "bytes", s.weight_count * 4 * 7
         return None, 0
@@ -263,7 +264,9 @@ def region_work(spec, label, M, train):
     if k == "attention":
         D, S = l.i("dim"), l.i("seq", 0) or M
         if bwd:
-            return "flops", 2 * (2.0 * M * 3 * D * D + 2.0 * M * D * D) + 2.5 * 4.0 * M * S * D
+            # out: dWo + dctx; core: QK^T and dP recomputed, dV, dK, dQ; qkv: dWqkv + dx
+            return "flops", {"qkv": 2 * 2.0 * M * 3 * D * D, "core": 5 * 2.0 * M * S * D,
+                             "out": 2 * 2.0 * M * D * D}.get(part, 0)
         return "flops", {"qkv": 2.0 * M * 3 * D * D, "core": 4.0 * M * S * D, "out": 2.0 * M * D * D}.get(part, 0)
     if k == "layernorm":
         D = 512

@@ -2,13 +2,18 @@
 // head dim 64 and sequences of at most 256 positions (the configuration
 // shape; longer sequences use the SIMT path in attention.cu).
 //
-// One CTA (4 warps) per (sequence b, head h, 128-query tile):
+// Persistent: one CTA (8 warps) per SM walks the work items (sequence b,
+// head h, 128-query tile), Q/K/V double-buffered so the next item's TMA
+// loads overlap this item's softmax:
 //   TMA      Q [128 x 64], K [256 x 64], V [256 x 64] straight out of the
 //            fused qkv buffer (128-byte swizzle, no multicast)
 //   MMA      S = Q K^T            (M=128, N=256, K=64)  -> TMEM cols [0,256)
-//   softmax  thread r owns query row r: scale after the dot (as the
-//            reference), max, exp, sum read from TMEM; P rounded to bf16 and
-//            written to shared memory as a K-major swizzled operand
+//   softmax  warp w owns query rows 32*(w%4).. and key half w/4; the two
+//            halves of a row meet through shared memory for the max and the
+//            sum. Scores are scaled after the dot product (as the
+//            reference), exponentials use ex2 on log2e-prescaled values; P
+//            is rounded to bf16 into shared memory as a K-major swizzled
+//            operand
 //   MMA      O = P V              (M=128, N=64, K=256; V is the MN-major B
 //            operand in its natural row layout) -> TMEM cols [256,320)
 //   epilogue ctx = O / rowsum (bf16), lse = max + log(rowsum) for the backward
@@ -27,38 +32,48 @@
 namespace nsb {
 
 namespace {
-constexpr int kQ = 128;          // queries per CTA
+constexpr int kQ = 128;          // queries per item
 constexpr int kKeys = 256;       // key tile (= max sequence length here)
 constexpr int kDh = 64;          // head dim
 constexpr int kQBytes = kQ * 128;        // 16 KB
 constexpr int kKBytes = kKeys * 128;     // 32 KB
+constexpr int kBufBytes = kQBytes + 2 * kKBytes;  // Q | K | V of one item: 80 KB
 constexpr int kPChunk = kQ * 128;        // 64 keys x 128 rows, bf16 = 16 KB
 constexpr int kPBytes = 4 * kPChunk;     // 64 KB
-constexpr int kSmem = kQBytes + 2 * kKBytes + kPBytes + 1024 + 64;
+constexpr int kFwdThreads = 256;
+constexpr int kSmem = 2 * kBufBytes + kPBytes + 2 * kQ * 4 + 64 + 1024;
 constexpr uint32_t kIdescS = ptx::instr_desc(1, 0, 0, kQ, kKeys);
 constexpr uint32_t kIdescO = ptx::instr_desc(1, 0, 1, kQ, kDh);
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 }  // namespace
 
-__global__ void __launch_bounds__(128, 1)
-    attn_tc_fwd_kernel(const __grid_constant__ CUtensorMap tqkv, int S, int H, int D, float scale,
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_tc_fwd_kernel(const __grid_constant__ CUtensorMap tqkv, int B, int S, int H, int D, float scale,
                        __nv_bfloat16* __restrict__ ctx, long long ld_ctx, float* __restrict__ lse, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = sQ + kQBytes;
-    uint8_t* sV = sK + kKBytes;
-    uint8_t* sP = sV + kKBytes;
-    uint64_t* ld_bar = reinterpret_cast<uint64_t*>(sP + kPBytes);
-    uint64_t* mma_bar = ld_bar + 1;
+    uint8_t* sP = smem + 2 * kBufBytes;
+    float* xch = reinterpret_cast<float*>(sP + kPBytes);  // [2][kQ] half-row max / sum exchange
+    uint64_t* ld_bar = reinterpret_cast<uint64_t*>(xch + 2 * kQ);  // [2]
+    uint64_t* mma_bar = ld_bar + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
 
-    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int warp = threadIdx.x >> 5;
-    const int row0 = b * S;  // first row of this sequence in qkv
-    const int q0 = qt * kQ;
+    const int t = threadIdx.x, warp = t >> 5;
+    const int lg = warp & 3, half = warp >> 2;
+    const int r = lg * 32 + (t & 31);  // query row within the tile = TMEM lane
+    const int qtiles = (S + kQ - 1) / kQ;
+    const int items = B * H * qtiles;
 
-    if (threadIdx.x == 0) {
-        ptx::mbar_init(ld_bar, 1);
+    if (t == 0) {
+        ptx::mbar_init(&ld_bar[0], 1);
+        ptx::mbar_init(&ld_bar[1], 1);
         ptx::mbar_init(mma_bar, 1);
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tqkv);
@@ -71,110 +86,138 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    bool ok = true;
+    const uint32_t lane_base = tmem + ((uint32_t)(lg * 32) << 16);
 
-    if (threadIdx.x == 0) {
-        ptx::mbar_arrive_expect_tx(ld_bar, kQBytes + 2 * kKBytes);
-        ptx::tma_load_2d(sQ, &tqkv, ld_bar, h * kDh, row0 + q0);
-        ptx::tma_load_2d(sK, &tqkv, ld_bar, D + h * kDh, row0);
-        ptx::tma_load_2d(sK + kKBytes / 2, &tqkv, ld_bar, D + h * kDh, row0 + 128);
-        ptx::tma_load_2d(sV, &tqkv, ld_bar, 2 * D + h * kDh, row0);
-        ptx::tma_load_2d(sV + kKBytes / 2, &tqkv, ld_bar, 2 * D + h * kDh, row0 + 128);
-        ok = ptx::mbar_wait(ld_bar, 0, err, kErrTimeoutAttn);
-        if (ok) {
+    auto issue_load = [&](int it, int buf) {
+        const int qt = it % qtiles, h = (it / qtiles) % H, b = it / (qtiles * H);
+        const int row0 = b * S;
+        uint8_t* sQ = smem + buf * kBufBytes;
+        uint8_t* sK = sQ + kQBytes;
+        uint8_t* sV = sK + kKBytes;
+        ptx::mbar_arrive_expect_tx(&ld_bar[buf], kBufBytes);
+        ptx::tma_load_2d(sQ, &tqkv, &ld_bar[buf], h * kDh, row0 + qt * kQ);
+        ptx::tma_load_2d(sK, &tqkv, &ld_bar[buf], D + h * kDh, row0);
+        ptx::tma_load_2d(sK + kKBytes / 2, &tqkv, &ld_bar[buf], D + h * kDh, row0 + 128);
+        ptx::tma_load_2d(sV, &tqkv, &ld_bar[buf], 2 * D + h * kDh, row0);
+        ptx::tma_load_2d(sV + kKBytes / 2, &tqkv, &ld_bar[buf], 2 * D + h * kDh, row0 + 128);
+    };
+    if (t == 0) {
+        if ((int)blockIdx.x < items) issue_load(blockIdx.x, 0);
+        if ((int)(blockIdx.x + gridDim.x) < items) issue_load(blockIdx.x + gridDim.x, 1);
+    }
+
+    bool ok = true;
+    uint32_t mph = 0;
+    const float sl2 = scale * kLog2e;  // score -> log2 units
+    int li = 0;
+#pragma unroll 1
+    for (int it = blockIdx.x; it < items; it += gridDim.x, li++) {
+        const int buf = li & 1;
+        const int qt = it % qtiles, h = (it / qtiles) % H, b = it / (qtiles * H);
+        const int row0 = b * S, q0 = qt * kQ;
+        const uint32_t aQ = ptx::smem_u32(smem + buf * kBufBytes);
+        const uint32_t aK = aQ + kQBytes, aV = aK + kKBytes;
+        if (t == 0) {
+            ok = ptx::mbar_wait(&ld_bar[buf], (li >> 1) & 1, err, kErrTimeoutAttn) && ok;
             ptx::tc_fence_after();
-            const uint32_t q = ptx::smem_u32(sQ), k = ptx::smem_u32(sK);
+            if (ok) {
 #pragma unroll
-            for (int s = 0; s < kDh / 16; s++)
-                ptx::mma_bf16(tmem, ptx::smem_desc(q + s * 32, 16, 1024, 2), ptx::smem_desc(k + s * 32, 16, 1024, 2),
-                              kIdescS, s > 0);
+                for (int s = 0; s < kDh / 16; s++)
+                    ptx::mma_bf16(tmem, ptx::smem_desc(aQ + s * 32, 16, 1024, 2), ptx::smem_desc(aK + s * 32, 16, 1024, 2),
+                                  kIdescS, s > 0);
+            }
+            ptx::mma_commit(mma_bar);
         }
-        ptx::mma_commit(mma_bar);
-    }
-    // ---- softmax: thread r owns query row r (TMEM lane r) ----
-    ok = ptx::mbar_wait(mma_bar, 0, err, kErrTimeoutAttn) && ok;
-    ptx::tc_fence_after();
-    const int r = threadIdx.x;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int c = 0; c < kKeys; c += 32) {
-        uint32_t v[32];
-        ptx::tmem_ld32(lane_base + c, v);
-        ptx::tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-            float s = __uint_as_float(v[j]) * scale;
-            if (c + j < S) mx = fmaxf(mx, s);
-        }
-    }
-    float sum = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < kKeys; c += 32) {
-        uint32_t v[32];
-        ptx::tmem_ld32(lane_base + c, v);
-        ptx::tmem_ld_wait();
-        float p[32];
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-            float s = __uint_as_float(v[j]) * scale;
-            p[j] = (c + j < S) ? expf(s - mx) : 0.f;
-            sum += p[j];
-        }
-        // 32 keys = 4 granules of 16 bytes in 64-key chunk c/64, granule
-        // index (c%64)/8 + g, XOR-swizzled by row % 8 (128-byte swizzle)
-        uint8_t* chunk = sP + (c >> 6) * kPChunk + r * 128;
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            const int gi = ((c & 63) >> 3) + g;
-            uint4 pk;
-            __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-            for (int t = 0; t < 4; t++) h2[t] = __floats2bfloat162_rn(p[8 * g + 2 * t], p[8 * g + 2 * t + 1]);
-            *reinterpret_cast<uint4*>(chunk + ((gi ^ (r & 7)) << 4)) = pk;
-        }
-    }
-    ptx::fence_proxy_async();  // generic-proxy P writes -> tensor-core (async proxy) reads
-    ptx::tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x == 0) {
+        ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
+        mph ^= 1;
         ptx::tc_fence_after();
-        if (ok) {
-            const uint32_t pa = ptx::smem_u32(sP), vb = ptx::smem_u32(sV);
+        // ---- softmax over this thread's 128 keys of row r ----
+        const int c_lo = half * 128;
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = c_lo; c < c_lo + 128; c += 32) {
+            uint32_t v[32];
+            ptx::tmem_ld32(lane_base + c, v);
+            ptx::tmem_ld_wait();
 #pragma unroll
-            for (int s = 0; s < kKeys / 16; s++) {
-                const uint64_t ad = ptx::smem_desc(pa + (s >> 2) * kPChunk + (s & 3) * 32, 16, 1024, 2);
-                const uint64_t bd = ptx::smem_desc(vb + s * 16 * 128, kKBytes, 1024, 2);
-                ptx::mma_bf16(tmem + kKeys, ad, bd, kIdescO, s > 0);
+            for (int j = 0; j < 32; j++)
+                if (c + j < S) mx = fmaxf(mx, __uint_as_float(v[j]) * sl2);
+        }
+        xch[half * kQ + r] = mx;
+        __syncthreads();
+        mx = fmaxf(xch[r], xch[kQ + r]);
+        float sum = 0.f;
+#pragma unroll 1
+        for (int c = c_lo; c < c_lo + 128; c += 32) {
+            uint32_t v[32];
+            ptx::tmem_ld32(lane_base + c, v);
+            ptx::tmem_ld_wait();
+            float p[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                p[j] = (c + j < S) ? ex2_approx(fmaf(__uint_as_float(v[j]), sl2, -mx)) : 0.f;
+                sum += p[j];
+            }
+            // 32 keys = 4 granules of 16 bytes in 64-key chunk c/64, granule
+            // index (c%64)/8 + g, XOR-swizzled by row % 8 (128-byte swizzle)
+            uint8_t* chunk = sP + (c >> 6) * kPChunk + r * 128;
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                const int gi = ((c & 63) >> 3) + g;
+                uint4 pk;
+                __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; e++) h2[e] = __floats2bfloat162_rn(p[8 * g + 2 * e], p[8 * g + 2 * e + 1]);
+                *reinterpret_cast<uint4*>(chunk + ((gi ^ (r & 7)) << 4)) = pk;
             }
         }
-        ptx::mma_commit(mma_bar);
-    }
-    ok = ptx::mbar_wait(mma_bar, 1, err, kErrTimeoutAttn) && ok;
-    ptx::tc_fence_after();
-    // ---- epilogue ----
-    const int qi = q0 + r;
-    const float inv = 1.f / sum;
-#pragma unroll 1
-    for (int c = 0; c < kDh; c += 32) {
+        __syncthreads();  // everyone has read the max exchange
+        xch[half * kQ + r] = sum;
+        ptx::fence_proxy_async();  // generic-proxy P writes -> tensor-core (async proxy) reads
+        ptx::tc_fence_before();
+        __syncthreads();
+        sum = xch[r] + xch[kQ + r];
+        if (t == 0) {
+            ptx::tc_fence_after();
+            if (ok) {
+                const uint32_t pa = ptx::smem_u32(sP);
+#pragma unroll
+                for (int s = 0; s < kKeys / 16; s++) {
+                    const uint64_t ad = ptx::smem_desc(pa + (s >> 2) * kPChunk + (s & 3) * 32, 16, 1024, 2);
+                    const uint64_t bd = ptx::smem_desc(aV + s * 16 * 128, kKBytes, 1024, 2);
+                    ptx::mma_bf16(tmem + kKeys, ad, bd, kIdescO, s > 0);
+                }
+            }
+            ptx::mma_commit(mma_bar);
+        }
+        ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
+        mph ^= 1;
+        ptx::tc_fence_after();
+        // this item's Q/K/V buffer is free: load the item two steps ahead
+        if (t == 0 && it + 2 * (int)gridDim.x < items) issue_load(it + 2 * gridDim.x, buf);
+        // ---- epilogue: warp half h writes head columns [32*half, +32) ----
+        const int qi = q0 + r;
+        const float inv = 1.f / sum;
         uint32_t v[32];
-        ptx::tmem_ld32(lane_base + kKeys + c, v);
+        ptx::tmem_ld32(lane_base + kKeys + half * 32, v);
         ptx::tmem_ld_wait();
         if (ok && qi < S) {
-            uint4* dst = reinterpret_cast<uint4*>(ctx + (size_t)(row0 + qi) * ld_ctx + h * kDh + c);
+            uint4* dst = reinterpret_cast<uint4*>(ctx + (size_t)(row0 + qi) * ld_ctx + h * kDh + half * 32);
 #pragma unroll
             for (int g = 0; g < 4; g++) {
                 uint4 pk;
                 __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
-                for (int t = 0; t < 4; t++)
-                    h2[t] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * t]) * inv,
-                                                  __uint_as_float(v[8 * g + 2 * t + 1]) * inv);
+                for (int e = 0; e < 4; e++)
+                    h2[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * e]) * inv,
+                                                  __uint_as_float(v[8 * g + 2 * e + 1]) * inv);
                 dst[g] = pk;
             }
+            if (lse && half == 0) lse[((size_t)b * H + h) * S + qi] = mx * kLn2 + logf(sum);
         }
+        ptx::tc_fence_before();
+        __syncthreads();  // O and the exchange slots are read before the next item reuses them
     }
-    if (ok && lse && qi < S) lse[((size_t)b * H + h) * S + qi] = mx + logf(sum);
     ptx::tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -300,7 +343,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
         }
         if (q < 256) {
-            lse_s[q] = L;
+            lse_s[q] = L * kLog2e;  // log2 units: P = 2^(s * scale * log2e - lse2)
             dv_s[q] = dd;
         }
     }
@@ -360,6 +403,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ptx::mma_commit(mma_bar);
     }
     uint32_t mph = 0;
+    const float sl2 = scale * kLog2e;
     const int steps = nt * nt;
 #pragma unroll 1
     for (int st = 0; st < steps; st++) {
@@ -383,7 +427,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int e = 0; e < 32; e++) {
                 const int qg = i * kBT + c0 + e;
                 const bool v = kval && qg < S;
-                const float pe = v ? expf(__uint_as_float(sv[e]) * scale - lse_s[qg]) : 0.f;
+                const float pe = v ? ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -lse_s[qg])) : 0.f;
                 p[e] = pe;
                 ds[e] = v ? pe * (__uint_as_float(pv[e]) - dv_s[qg]) : 0.f;
             }
@@ -484,9 +528,10 @@ int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
         cudaFuncSetAttribute(attn_tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         attr = true;
     }
-    dim3 grid((a.S + kQ - 1) / kQ, a.H, a.B);
-    attn_tc_fwd_kernel<<<grid, 128, kSmem, s>>>(m, a.S, a.H, a.D, a.scale, reinterpret_cast<__nv_bfloat16*>(a.ctx),
-                                                 a.ld_ctx, a.lse, err);
+    const int items = a.B * a.H * ((a.S + kQ - 1) / kQ);
+    const int grid = items < num_sms() ? items : num_sms();
+    attn_tc_fwd_kernel<<<grid, kFwdThreads, kSmem, s>>>(m, a.B, a.S, a.H, a.D, a.scale,
+                                                        reinterpret_cast<__nv_bfloat16*>(a.ctx), a.ld_ctx, a.lse, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

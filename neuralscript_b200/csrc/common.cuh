@@ -131,6 +131,10 @@ struct Epilogue {
     __nv_bfloat16* c16 = nullptr;
     int ld_c16 = 0;
     const int* out_rows = nullptr;
+    // c32 split in column blocks: output column c goes to block c / col_block
+    // at c32 + block * col_block_stride, column c % col_block (0 = off)
+    int col_block = 0;
+    long long col_block_stride = 0;
 };
 
 __device__ __forceinline__ float ld_any(const void* p, int dtype, size_t idx) {

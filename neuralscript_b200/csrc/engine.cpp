@@ -697,7 +697,8 @@ static int backward(ns_model* m, int M) {
         const float* dv = out.gcur;
         Val& in = m->vals[op.in];
         int rc = 0;
-        const int reg = region_begin(m, std::string("bwd:") + (op.layer >= 0 ? s.layers[op.layer].name : s.ops[oi].out));
+        const std::string rname = std::string("bwd:") + (op.layer >= 0 ? s.layers[op.layer].name : s.ops[oi].out);
+        const int reg = op.kind == OP_ATTN ? -1 : region_begin(m, rname);
         switch (op.kind) {
             case OP_DENSE: {
                 const WeightInfo& w = s.weights[op.widx];
@@ -720,6 +721,9 @@ static int backward(ns_model* m, int M) {
                     if (rc) break;
                 } else if (m->seed16 && oi == m->vals[m->out_val].producer) {
                     dz = op.dz;  // the loss kernel wrote the bf16 seed here
+                } else if (op.g16_ready) {
+                    dz = op.dz;  // the consumer's LN backward wrote the bf16 copy
+                    op.g16_ready = false;
                 } else {
                     dz = grad_operand(m, dv, op.dz, n);
                 }
@@ -787,7 +791,9 @@ static int backward(ns_model* m, int M) {
                 const int D = (int)l.geti("dim", 0), H = (int)l.geti("heads", 1);
                 int S = (int)l.geti("seq", 0);
                 if (S <= 0) S = M;
-                const void* dout = grad_operand(m, dv, op.dout_w, (size_t)M * D);
+                int r1 = region_begin(m, rname + ".out");
+                const void* dout = op.g16_ready ? op.dout_w : grad_operand(m, dv, op.dout_w, (size_t)M * D);
+                op.g16_ready = false;
                 if (op.fused_res >= 0 && (rc = contribute_alias(m, m->vals[op.fused_res], dv, M))) break;
                 const WeightInfo& wo = s.weights[op.widx + 3];
                 GemmDesc go;  // dWo = ctx^T dout
@@ -813,6 +819,8 @@ static int backward(ns_model* m, int M) {
                     gc.ep.ld_c32 = D;
                 }
                 if ((rc = run_gemm(m, gc))) break;
+                region_end(m, r1);
+                int r2 = region_begin(m, rname + ".core");
                 AttnArgs a;
                 a.B = M / S;
                 a.S = S;
@@ -837,20 +845,23 @@ static int backward(ns_model* m, int M) {
                     rc = fail("attention backward launch failed");
                     break;
                 }
-                const size_t es = m->wdt == kBF16 ? 2 : 4;
-                for (int g = 0; g < 3; g++) {  // dWq, dWk, dWv = x^T dQ|dK|dV
-                    const WeightInfo& wq = s.weights[op.widx + g];
+                region_end(m, r2);
+                int r3 = region_begin(m, rname + ".qkv");
+                {  // [dWq | dWk | dWv] = x^T [dQ | dK | dV]: one GEMM, N = 3D, whose
+                   // column blocks land on the three consecutive blob tensors
+                    const WeightInfo& wq = s.weights[op.widx];
                     GemmDesc gq;
                     gq.M = D;
-                    gq.N = D;
+                    gq.N = 3 * D;
                     gq.K = M;
                     gq.a = opnd(as_operand(m, in), m->wdt, D, true);
-                    gq.b = opnd(reinterpret_cast<const char*>(op.dqkv) + (size_t)g * D * es, m->wdt, 3LL * D, true);
+                    gq.b = opnd(op.dqkv, m->wdt, 3LL * D, true);
                     gq.ep.c32 = m->d_g + wq.off;
                     gq.ep.ld_c32 = D;
+                    gq.ep.col_block = D;
+                    gq.ep.col_block_stride = (long long)D * D;
                     if ((rc = run_gemm(m, gq))) break;
                 }
-                if (rc) break;
                 if (in.gbuf) {
                     GemmDesc gx;  // dx = dQKV [Wq|Wk|Wv]^T (+ running total)
                     gx.M = M;
@@ -867,14 +878,26 @@ static int backward(ns_model* m, int M) {
                     if ((rc = run_gemm(m, gx))) break;
                     in.gcur = in.gbuf;
                 }
+                region_end(m, r3);
                 break;
             }
-            case OP_LN:
+            case OP_LN: {
                 if (!in.gbuf) break;
+                // When the LN input comes straight from a Dense (no activation)
+                // or Attention layer and LN is its only consumer, also write the
+                // gradient as that layer's bf16 GEMM operand (saves a cast pass).
+                __nv_bfloat16* dx16 = nullptr;
+                Op* P = in.producer >= 0 ? &m->ops[in.producer] : nullptr;
+                if (m->wdt == kBF16 && P && !P->skip && P->out == op.in && in.consumers.size() == 1) {
+                    if (P->kind == OP_DENSE && P->act == 0 && P->dz) dx16 = reinterpret_cast<__nv_bfloat16*>(P->dz);
+                    else if (P->kind == OP_ATTN && P->dout_w) dx16 = reinterpret_cast<__nv_bfloat16*>(P->dout_w);
+                }
                 launch_counter() += 1;
-                rc = layernorm_bwd(dv, in.f32, in.gcur, M, in.cols, in.gbuf, nullptr, m->stream);
+                rc = layernorm_bwd(dv, in.f32, in.gcur, M, in.cols, in.gbuf, dx16, m->stream);
                 in.gcur = in.gbuf;
+                if (dx16) P->g16_ready = true;
                 break;
+            }
             case OP_ADD:
                 if ((rc = contribute_alias(m, in, dv, M))) break;
                 rc = contribute_alias(m, m->vals[op.in2], dv, M);

@@ -62,6 +62,7 @@ struct Op {
     float* dvec = nullptr;
     MoeScratch* moe = nullptr;
     bool dz_ready = false;  // backward: dz already holds act'(z) * dout (written by the consumer's GEMM)
+    bool g16_ready = false;  // backward: dz / dout_w already holds the bf16 output gradient
 };
 
 }  // namespace nsb

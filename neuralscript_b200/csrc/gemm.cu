@@ -55,7 +55,14 @@ __device__ __forceinline__ void epi_apply(const Epilogue& ep, int row, int col, 
     }
     if (ep.act) v = act_fwd(v, ep.act);
     int orow = ep.out_rows ? ep.out_rows[row] : row;
-    if (ep.c32) ep.c32[(size_t)orow * ep.ld_c32 + col] = v;
+    if (ep.c32) {
+        if (ep.col_block) {
+            const int b = col / ep.col_block;
+            ep.c32[b * ep.col_block_stride + (size_t)orow * ep.ld_c32 + (col - b * ep.col_block)] = v;
+        } else {
+            ep.c32[(size_t)orow * ep.ld_c32 + col] = v;
+        }
+    }
     if (ep.c16) ep.c16[(size_t)orow * ep.ld_c16 + col] = f2bf(v);
 }
 
@@ -492,7 +499,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         for (int j = 0; j < 32; j++)
                             if (col0 + j < p.N) w[j] = v[j];
                     }
-                } else if (full) {
+                } else if (full && !p.ep.col_block) {
                     epi_apply32_vec<FAST>(p.ep, row, col0, v);
                 } else {
 #pragma unroll
@@ -806,7 +813,8 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     OutMaps om;
     memset(&om, 0, sizeof(om));
     p.tma_out = 0;
-    if (p.vec_ok && d.groups == 1 && p.splits == 1 && !d.ep.out_rows && (d.ep.z || d.ep.c32 || d.ep.c16)) {
+    if (p.vec_ok && d.groups == 1 && p.splits == 1 && !d.ep.out_rows && !d.ep.col_block &&
+        (d.ep.z || d.ep.c32 || d.ep.c16)) {
         bool okm = true;
         if (d.ep.z) okm = okm && make_out_map(&om.z, d.ep.z, d.ep.z_dtype, d.N, d.M, d.ep.ld_z);
         if (d.ep.c32) okm = okm && make_out_map(&om.c32, d.ep.c32, kF32, d.N, d.M, d.ep.ld_c32);

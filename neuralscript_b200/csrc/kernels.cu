@@ -131,27 +131,41 @@ __global__ void emb_count_kernel(const float* __restrict__ ids, int M, int V, in
     }
 }
 
-// Exclusive scan of n ints, one CTA of 1024 threads, chunked.
-__global__ void scan_kernel(const int* __restrict__ in, int* __restrict__ out, int n) {
-    __shared__ int sh[1024];
-    __shared__ int carry;
-    if (threadIdx.x == 0) carry = 0;
+// Exclusive prefix sum of n ints, one block of 1024 threads: each thread
+// owns a contiguous run, runs are combined by warp-shuffle scans.
+__global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ in, int* __restrict__ out, int n) {
+    __shared__ int warp_tot[32];
+    const int per = (n + 1023) / 1024;
+    const int b0 = threadIdx.x * per;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int local = 0;
+    for (int i = 0; i < per; i++)
+        if (b0 + i < n) local += in[b0 + i];
+    int x = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[w] = x;
     __syncthreads();
-    for (int base = 0; base < n; base += 1024) {
-        int i = base + threadIdx.x;
-        int v = i < n ? in[i] : 0;
-        sh[threadIdx.x] = v;
-        __syncthreads();
-        for (int off = 1; off < 1024; off <<= 1) {
-            int t = threadIdx.x >= off ? sh[threadIdx.x - off] : 0;
-            __syncthreads();
-            sh[threadIdx.x] += t;
-            __syncthreads();
+    if (w == 0) {
+        int t = warp_tot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, t, o);
+            if (lane >= o) t += y;
         }
-        if (i < n) out[i] = carry + sh[threadIdx.x] - v;
-        __syncthreads();
-        if (threadIdx.x == 1023) carry += sh[1023];
-        __syncthreads();
+        warp_tot[lane] = t;
+    }
+    __syncthreads();
+    int excl = x - local + (w > 0 ? warp_tot[w - 1] : 0);
+    for (int i = 0; i < per; i++) {
+        const int k = b0 + i;
+        if (k < n) {
+            out[k] = excl;
+            excl += in[k];
+        }
     }
 }
 
@@ -649,10 +663,22 @@ int mse_fwd_bwd(const float* p, const float* y, int M, int C, float denom, float
     return launch_ok();
 }
 
-__global__ void reduce_sum_kernel(const float* __restrict__ x, int n, float scale, float* out) {
+// Sum of n floats in a fixed order (one block; float4 loads when aligned).
+__global__ void __launch_bounds__(1024) reduce_sum_kernel(const float* __restrict__ x, int n, float scale, float* out) {
     __shared__ float sh[33];
     float acc = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) acc += x[i];
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int n4 = n >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 v = x4[i];
+            acc += (v.x + v.y) + (v.z + v.w);
+        }
+        for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) acc += x[i];
+    } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) acc += x[i];
+    }
     acc = block_sum(acc, sh);
     if (threadIdx.x == 0) *out = acc * scale;
 }
