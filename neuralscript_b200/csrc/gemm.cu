@@ -269,6 +269,22 @@ __device__ __forceinline__ bool tc_decode(const TcParams& p, int u, int BN, int&
     return true;
 }
 
+// One unit of work for a CTA: a tile (or split-K slice) and its k-block range.
+struct Work {
+    int m0, n0, kb0, kb1, split, g, row_end;
+};
+
+// Next work unit of this CTA (units blockIdx.x, +gridDim.x, ...), skipping
+// empty grouped tiles.
+__device__ __forceinline__ bool work_next(const TcParams& p, int BN, int& u, Work& o) {
+    while (u < p.total_units) {
+        const int cur = u;
+        u += gridDim.x;
+        if (tc_decode(p, cur, BN, o.m0, o.n0, o.kb0, o.kb1, o.split, o.g, o.row_end)) return true;
+    }
+    return false;
+}
+
 constexpr int kEpiWarps = 8;                    // two per TMEM lane quarter
 constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + epilogue
 
@@ -324,11 +340,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // ---------------- TMA producer ----------------
             int stage = 0;
             uint32_t phase = 0;
-            for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
-                int m0, n0, kb0, kb1, split, g, row_end;
-                if (!tc_decode(p, u, BN, m0, n0, kb0, kb1, split, g, row_end)) continue;
-                const int nb = g * p.N + n0;  // B row (grouped: groups stacked along N)
-                for (int kb = kb0; kb < kb1; kb++) {
+            int wu = blockIdx.x;
+            Work w;
+            while (work_next(p, BN, wu, w)) {
+                const int m0 = w.m0;
+                const int nb = w.g * p.N + w.n0;  // B row (grouped: groups stacked along N)
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) goto producer_done;
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     uint8_t* sb = sa + C::A_BYTES;
@@ -373,13 +390,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
-                int m0, n0, kb0, kb1, split, g, row_end;
-                if (!tc_decode(p, u, BN, m0, n0, kb0, kb1, split, g, row_end)) continue;
+            int wu = blockIdx.x;
+            Work w;
+            while (work_next(p, BN, wu, w)) {
+                const int kb0 = w.kb0;
                 if (!ptx::mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutMma)) goto mma_done;
                 ptx::tc_fence_after();
                 const uint32_t d = tmem_base + acc * BN;
-                for (int kb = kb0; kb < kb1; kb++) {
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!ptx::mbar_wait(&full[stage], phase, p.err, kErrTimeoutMma)) goto mma_done;
                     ptx::tc_fence_after();
                     const uint32_t sa = ptx::smem_u32(smem + stage * C::STAGE_BYTES);
@@ -453,59 +471,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             stage_store(map, g4, col0, y);
         };
+        // Finish 32 accumulator columns (col0 < N) of this thread's row.
+        auto finish = [&](const Work& w, int col0, float* v) {
+            const int row = w.m0 + r_in_tile;
+            const bool row_ok = row < w.row_end;
+            if (p.tma_out) {
+                // rows >= M and columns >= N of a box are clipped by the
+                // store; a 32-row slab entirely past M issues nothing
+                const int y = w.m0 + lane_grp * 32;
+                if (y >= p.M) return;
+                const int nc = col0 + 32 <= p.N ? 32 : p.N - col0;
+                if (row_ok) epi_pre32<FAST>(p.ep, row, col0, v, nc);
+                if (p.ep.z) {
+                    if (p.ep.z_dtype == kBF16) out_bf16(&tz, v, col0, y);
+                    else out_f32(&tz, v, col0, y);
+                }
+                epi_act32<FAST>(p.ep.act, v);
+                if (p.ep.c32) out_f32(&tc32, v, col0, y);
+                if (p.ep.c16) out_bf16(&tc16, v, col0, y);
+                return;
+            }
+            if (!row_ok) return;
+            const bool full = p.vec_ok && col0 + 32 <= p.N;
+            if (p.splits > 1) {
+                float* ws = p.workspace + ((size_t)w.split * p.M + row) * p.N + col0;
+                if (full) {
+                    store32_f32(ws, v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (col0 + j < p.N) ws[j] = v[j];
+                }
+            } else if (full && !p.ep.col_block) {
+                epi_apply32_vec<FAST>(p.ep, row, col0, v);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    if (col0 + j < p.N) epi_apply(p.ep, row, col0 + j, v[j]);
+            }
+        };
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
-            int m0, n0, kb0, kb1, split, g, row_end;
-            if (!tc_decode(p, u, BN, m0, n0, kb0, kb1, split, g, row_end)) continue;
+        int wu = blockIdx.x;
+        Work w;
+        while (work_next(p, BN, wu, w)) {
             if (!ptx::mbar_wait(&acc_full[acc], acc_phase, p.err, kErrTimeoutEpilogue)) break;
             ptx::tc_fence_after();
-            const int row = m0 + r_in_tile;
-            const bool row_ok = row < row_end;
 #pragma unroll 1
             for (int c = half * HALF_COLS; c < (half + 1) * HALF_COLS; c += 32) {
                 uint32_t r[32];
                 ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + acc * BN + c, r);
                 ptx::tmem_ld_wait();
-                const int col0 = n0 + c;
+                const int col0 = w.n0 + c;
                 if (col0 >= p.N) continue;  // uniform across the warp
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-                if (p.tma_out) {
-                    // rows >= M and columns >= N of a box are clipped by the
-                    // store; a 32-row slab entirely past M issues nothing
-                    const int y = m0 + lane_grp * 32;
-                    if (y >= p.M) continue;
-                    const int nc = col0 + 32 <= p.N ? 32 : p.N - col0;
-                    if (row_ok) epi_pre32<FAST>(p.ep, row, col0, v, nc);
-                    if (p.ep.z) {
-                        if (p.ep.z_dtype == kBF16) out_bf16(&tz, v, col0, y);
-                        else out_f32(&tz, v, col0, y);
-                    }
-                    epi_act32<FAST>(p.ep.act, v);
-                    if (p.ep.c32) out_f32(&tc32, v, col0, y);
-                    if (p.ep.c16) out_bf16(&tc16, v, col0, y);
-                    continue;
-                }
-                if (!row_ok) continue;
-                const bool full = p.vec_ok && col0 + 32 <= p.N;
-                if (p.splits > 1) {
-                    float* w = p.workspace + ((size_t)split * p.M + row) * p.N + col0;
-                    if (full) {
-                        store32_f32(w, v);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (col0 + j < p.N) w[j] = v[j];
-                    }
-                } else if (full && !p.ep.col_block) {
-                    epi_apply32_vec<FAST>(p.ep, row, col0, v);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (col0 + j < p.N) epi_apply(p.ep, row, col0 + j, v[j]);
-                }
+                finish(w, col0, v);
             }
             ptx::tc_fence_before();
             ptx::mbar_arrive(&acc_empty[acc]);
@@ -523,10 +545,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-// Sum split-K partials in split order, then the full epilogue.
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, Epilogue ep) {
+// Sum split-K partials in split order, then the full epilogue; four
+// consecutive columns per thread when N % 4 == 0 and the workspace is aligned.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, Epilogue ep, int vec4) {
+    const size_t total = (size_t)M * N;
+    if (vec4) {
+        const size_t i4 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (4 * i4 >= total) return;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < splits; s++) {
+            const float4 w = __ldcs(reinterpret_cast<const float4*>(ws + (size_t)s * total) + i4);
+            v.x += w.x;
+            v.y += w.y;
+            v.z += w.z;
+            v.w += w.w;
+        }
+        const int row = (int)(4 * i4 / N), col = (int)(4 * i4 % N);
+        epi_apply(ep, row, col, v.x);
+        epi_apply(ep, row, col + 1, v.y);
+        epi_apply(ep, row, col + 2, v.z);
+        epi_apply(ep, row, col + 3, v.w);
+        return;
+    }
     size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    size_t total = (size_t)M * N;
     if (idx >= total) return;
     int row = (int)(idx / N), col = (int)(idx % N);
     float v = 0.f;
@@ -704,7 +745,8 @@ static void pick_splits(const GemmDesc& d, int bn, int& splits, int& kb_per_spli
         const int sms = num_sms();
         if (d.splits > 0) splits = d.splits;
         else if (tiles < sms / 2 && k_blocks >= 16) {
-            splits = (sms + tiles - 1) / tiles;
+            // as many splits as keep every unit in one wave
+            splits = sms / tiles;
             splits = min(splits, k_blocks / 8);
             splits = max(splits, 1);
         }
@@ -717,8 +759,9 @@ size_t gemm_workspace_floats(const GemmDesc& d) {
     if (!gemm_uses_tensor_cores(d)) return 0;
     const int bn = pick_bn(d);
     const int bk = d.a.dtype == kBF16 ? 64 : 32;
+    const int kblocks = (d.K + bk - 1) / bk;
     int splits, kbps;
-    pick_splits(d, bn, splits, kbps, (d.K + bk - 1) / bk);
+    pick_splits(d, bn, splits, kbps, kblocks);
     return splits > 1 ? (size_t)splits * d.M * d.N : 0;
 }
 
@@ -832,7 +875,10 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     if (e != cudaSuccess) return -5;
     if (p.splits > 1) {
         size_t total = (size_t)d.M * d.N;
-        splitk_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(p.workspace, p.splits, d.M, d.N, d.ep);
+        const int vec4 = d.N % 4 == 0 && !(reinterpret_cast<uintptr_t>(p.workspace) & 15);
+        const size_t threads = vec4 ? total / 4 : total;
+        splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p.workspace, p.splits, d.M, d.N, d.ep,
+                                                                             vec4);
         if (cudaGetLastError() != cudaSuccess) return -5;
     }
     return 0;

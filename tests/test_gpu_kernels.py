@@ -92,6 +92,49 @@ def test_gemm_epilogue(mode):
     assert relerr(c16.float().cpu(), ref.cpu()) < 5e-3
 
 
+# Large GEMMs with ragged tile counts and long K: a ragged 474-tile case,
+# 256 tiles, and the weight-gradient layout (both operands MN-major).
+LARGE_SHAPES = [(16384, 512, 512, 0, 0), (10000, 1536, 512, 0, 1), (512, 8192, 2048, 1, 1)]
+
+
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+@pytest.mark.parametrize("M,N,K,a_mn,b_mn", LARGE_SHAPES)
+def test_gemm_large(mode, M, N, K, a_mn, b_mn):
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    A = torch.randn(M, K, device=DEV, generator=g)
+    B = torch.randn(N, K, device=DEV, generator=g)
+    if mode == "bf16":
+        A, B = A.bfloat16().float(), B.bfloat16().float()
+        dt = torch.bfloat16
+    else:
+        A, B = tf32_trunc(A), tf32_trunc(B)
+        dt = torch.float32
+    As, Bs = make_operand(A, a_mn, dt), make_operand(B, b_mn, dt)
+    C = torch.full((M, N), float("nan"), device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    O.gemm(As, Bs, M, N, K, As.stride(0), a_mn, Bs.stride(0), b_mn, c32=C, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = (A.double() @ B.double().t()).cpu().numpy()
+    assert relerr(C.cpu().numpy(), ref) < 1e-5
+
+
+def test_gemm_large_epilogue():
+    M, N, K = 12000, 512, 1024
+    g = torch.Generator(device=DEV).manual_seed(11)
+    A = torch.randn(M, K, device=DEV, generator=g).bfloat16().float()
+    B = torch.randn(N, K, device=DEV, generator=g).bfloat16().float()
+    add = torch.randn(M, N, device=DEV, generator=g)
+    c32 = torch.empty(M, N, device=DEV)
+    c16 = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    O.gemm(A.bfloat16(), B.bfloat16(), M, N, K, K, 0, K, 0, alpha=0.25, add=add, act=6, c32=c32, c16=c16)
+    torch.cuda.synchronize()
+    pre = 0.25 * (A.double() @ B.double().t()) + add.double()
+    ref = 0.5 * pre * (1 + torch.erf(pre / 1.41421356))
+    assert relerr(c32.cpu(), ref.cpu()) < 1e-5
+    assert relerr(c16.float().cpu(), ref.cpu()) < 5e-3
+
+
 def test_gemm_simt_matches_reference_order_exactly():
     """fp32 SIMT GEMM (each output accumulated with fmaf in increasing k)
     against the C oracle of the reference's scalar loop."""
