@@ -1110,6 +1110,31 @@ static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* 
 // ---------------------------------------------------------------------------
 // synchronisation with error / timeout checks
 // ---------------------------------------------------------------------------
+// Wait (bounded by the model's timeout) until the communicator's last call
+// has completed its enqueue; aborts the communicator on error or timeout.
+static int nccl_settle(ns_model* m) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st;
+        nccl().CommGetAsyncError(m->comm, &st);
+        if (st == ncclSuccess) return 0;
+        if (st != ncclInProgress) {
+            nccl().CommAbort(m->comm);
+            m->comm = nullptr;
+            m->group_lost = true;
+            return fail(std::string("NCCL error: ") + nccl().GetErrorString(st));
+        }
+        auto el = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+        if (el.count() > m->timeout_ms) {
+            nccl().CommAbort(m->comm);
+            m->comm = nullptr;
+            m->group_lost = true;
+            return fail("collective enqueue timed out");
+        }
+        std::this_thread::yield();
+    }
+}
+
 static int finish(ns_model* m) {
     auto t0 = std::chrono::steady_clock::now();
     for (;;) {
@@ -1122,12 +1147,14 @@ static int finish(ns_model* m) {
             if (ar != ncclSuccess && ar != ncclInProgress) {
                 nccl().CommAbort(m->comm);
                 m->comm = nullptr;
+                m->group_lost = true;
                 return fail(std::string("NCCL error: ") + nccl().GetErrorString(ar));
             }
             auto el = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
             if (el.count() > m->timeout_ms) {
                 nccl().CommAbort(m->comm);
                 m->comm = nullptr;
+                m->group_lost = true;
                 return fail("collective timed out");
             }
             std::this_thread::sleep_for(std::chrono::microseconds(50));
@@ -1433,10 +1460,15 @@ static int train_core(ns_model* m, int M, const float* d_labels, const int* d_ta
         // the loss sum rides at the end of the gradient blob
         reduce_sum(m->d_rowloss, M, 1.0f, m->d_g + m->spec.total, m->stream);
         int ra = region_begin(m, "allreduce");
+        if (m->world > 1 && !m->comm) return fail("data-parallel group lost (an earlier collective failed)");
         if (m->comm && m->world > 1) {
             launch_counter() += 1;
             ncclResult_t r = nccl().AllReduce(m->d_g, m->d_g, m->spec.total + 1, ncclFloat, ncclSum, m->comm, m->stream);
             if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("allreduce: ") + nccl().GetErrorString(r));
+            // A non-blocking communicator may still be enqueueing the collective
+            // (ncclInProgress): wait until it sits on the stream, so that the
+            // optimizer kernels launched next are ordered after it.
+            if (r == ncclInProgress && nccl_settle(m)) return -1;
         }
         region_end(m, ra);
         int ro = region_begin(m, "optimizer");

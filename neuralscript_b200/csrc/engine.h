@@ -117,6 +117,7 @@ struct ns_model {
     // data parallel
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
+    bool group_lost = false;  // the communicator was aborted; train steps fail from then on
     int timeout_ms = 60000;
     long long launches = 0;
     // per-region CUDA-event timing on the engine stream (opt-in)
