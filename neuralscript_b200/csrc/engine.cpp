@@ -687,6 +687,89 @@ static const void* grad_operand(ns_model* m, const float* g, void* tmp16, size_t
     return tmp16;
 }
 
+// ---------------------------------------------------------------------------
+// data-parallel gradient reduction, overlapped with the backward pass: as a
+// layer's weight gradients are complete, their blob range is all-reduced on
+// the communication stream while the backward of earlier layers continues.
+// All ranks issue the same ranges in the same (reverse layer) order.
+// ---------------------------------------------------------------------------
+static int nccl_settle(ns_model* m);
+static bool dist_active(const ns_model* m) { return m->comm && m->world > 1; }
+
+static cudaEvent_t dist_event(ns_model* m) {
+    if (m->ev_next >= m->dist_events.size()) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        m->dist_events.push_back(e);
+    }
+    return m->dist_events[m->ev_next++];
+}
+
+static int dist_reduce_range(ns_model* m, size_t off, size_t count) {
+    if (!count) return 0;
+    cudaEvent_t ev = dist_event(m);
+    if (!ev) return fail("event creation failed");
+    cudaEventRecord(ev, m->stream);
+    cudaStreamWaitEvent(m->comm_stream, ev, 0);
+    launch_counter() += 1;
+    ncclResult_t r = nccl().AllReduce(m->d_g + off, m->d_g + off, count, ncclFloat, ncclSum, m->comm, m->comm_stream);
+    if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("allreduce: ") + nccl().GetErrorString(r));
+    // a non-blocking communicator may still be enqueueing: wait until the
+    // collective sits on its stream before the next NCCL call
+    if (r == ncclInProgress && nccl_settle(m)) return -1;
+    return 0;
+}
+
+// All-reduce weights [w0, w1) once their gradients are final (the range that
+// ends the blob also carries the loss sum stored after it).
+static int dist_reduce_weights(ns_model* m, int w0, int w1) {
+    const Spec& s = m->spec;
+    for (int w = w0; w < w1; w++)
+        if (m->reduced[w]) return 0;
+    for (int w = w0; w < w1; w++) m->reduced[w] = 1;
+    const size_t off = s.weights[w0].off;
+    size_t end = s.weights[w1 - 1].off + s.weights[w1 - 1].count;
+    if (end == s.total) end += 1;
+    return dist_reduce_range(m, off, end - off);
+}
+
+// Reduce what is left (weights of layers without a gradient op in this
+// step, or layers applied more than once), then order the main stream after
+// every reduction.
+static int dist_reduce_finish(ns_model* m) {
+    const Spec& s = m->spec;
+    const int nw = (int)s.weights.size();
+    int w = 0;
+    while (w < nw) {
+        if (m->reduced[w]) {
+            w++;
+            continue;
+        }
+        int e = w;
+        while (e < nw && !m->reduced[e]) e++;
+        if (dist_reduce_weights(m, w, e)) return -1;
+        w = e;
+    }
+    if (nw == 0 && dist_reduce_range(m, s.total, 1)) return -1;
+    cudaEvent_t done = dist_event(m);
+    if (!done) return fail("event creation failed");
+    cudaEventRecord(done, m->comm_stream);
+    cudaStreamWaitEvent(m->stream, done, 0);
+    return 0;
+}
+
+// Weight index range [w0, w1) of a layer (w0 == w1: none).
+static void layer_weights(const ns_model* m, int layer, int& w0, int& w1) {
+    const Spec& s = m->spec;
+    w0 = w1 = -1;
+    for (size_t wi = 0; wi < s.weights.size(); wi++)
+        if (s.weights[wi].layer == layer) {
+            if (w0 < 0) w0 = (int)wi;
+            w1 = (int)wi + 1;
+        }
+    if (w0 < 0) w0 = w1 = 0;
+}
+
 static int backward(ns_model* m, int M) {
     const Spec& s = m->spec;
     for (int oi = (int)m->ops.size() - 1; oi >= 0; oi--) {
@@ -920,6 +1003,14 @@ static int backward(ns_model* m, int M) {
         }
         region_end(m, reg);
         if (rc) return -1;
+        if (dist_active(m) && op.layer >= 0) {
+            // a layer applied by more than one op is reduced at the end
+            int uses = 0;
+            for (const Op& o2 : m->ops) uses += (!o2.skip && o2.layer == op.layer) ? 1 : 0;
+            int w0, w1;
+            layer_weights(m, op.layer, w0, w1);
+            if (uses == 1 && w1 > w0 && dist_reduce_weights(m, w0, w1)) return -1;
+        }
     }
     return 0;
 }
@@ -1157,7 +1248,9 @@ static int finish(ns_model* m) {
                 m->group_lost = true;
                 return fail("collective timed out");
             }
-            std::this_thread::sleep_for(std::chrono::microseconds(50));
+            // spin (yielding): a timed sleep oversleeps by tens of microseconds,
+            // which would idle the GPU between steps
+            std::this_thread::yield();
         } else {
             cudaError_t e = cudaStreamSynchronize(m->stream);
             if (e != cudaSuccess) return fail(std::string("CUDA error: ") + cudaGetErrorString(e));
@@ -1323,7 +1416,10 @@ void nsb_free(ns_model* m) {
         for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
     }
     if (m->h_loss) cudaFreeHost(m->h_loss);
+    if (m->comm_stream) cudaStreamSynchronize(m->comm_stream);
     if (m->comm) nccl().CommDestroy(m->comm);
+    for (cudaEvent_t e : m->dist_events) cudaEventDestroy(e);
+    if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -1456,20 +1552,18 @@ static int train_core(ns_model* m, int M, const float* d_labels, const int* d_ta
         for (auto& v : m->vals) v.gcur = nullptr;
         Val& o = m->vals[m->out_val];
         o.gcur = o.gbuf;
-        if (backward(m, M)) return -1;
-        // the loss sum rides at the end of the gradient blob
-        reduce_sum(m->d_rowloss, M, 1.0f, m->d_g + m->spec.total, m->stream);
-        int ra = region_begin(m, "allreduce");
         if (m->world > 1 && !m->comm) return fail("data-parallel group lost (an earlier collective failed)");
-        if (m->comm && m->world > 1) {
-            launch_counter() += 1;
-            ncclResult_t r = nccl().AllReduce(m->d_g, m->d_g, m->spec.total + 1, ncclFloat, ncclSum, m->comm, m->stream);
-            if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("allreduce: ") + nccl().GetErrorString(r));
-            // A non-blocking communicator may still be enqueueing the collective
-            // (ncclInProgress): wait until it sits on the stream, so that the
-            // optimizer kernels launched next are ordered after it.
-            if (r == ncclInProgress && nccl_settle(m)) return -1;
+        // the loss sum rides at the end of the gradient blob (reduced with the last range)
+        launch_counter() += 1;
+        reduce_sum(m->d_rowloss, M, 1.0f, m->d_g + m->spec.total, m->stream);
+        if (dist_active(m)) {
+            m->reduced.assign(m->spec.weights.size(), 0);
+            m->ev_next = 0;
         }
+        if (backward(m, M)) return -1;
+        // the part of the gradient all-reduce not hidden behind the backward
+        int ra = region_begin(m, "allreduce");
+        if (dist_active(m) && dist_reduce_finish(m)) return -1;
         region_end(m, ra);
         int ro = region_begin(m, "optimizer");
         if (optimizer_step(m, lr)) return -1;
@@ -1701,6 +1795,17 @@ int nsb_dist_init(ns_model* m, int rank, int world, const void* id128, int timeo
     memcpy(&id, id128, sizeof(id));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
+    // The all-reduces run beside the backward GEMMs: cap the SMs NCCL may
+    // occupy (NS_B200_NCCL_MAX_CTAS, default 16, measured best on two GPUs
+    // against 8 and NCCL's own choice; 0 leaves the choice to NCCL).
+    {
+        const char* e = getenv("NS_B200_NCCL_MAX_CTAS");
+        const int mx = e ? atoi(e) : 16;
+        if (mx > 0) {
+            cfg.maxCTAs = mx;
+            cfg.minCTAs = 1;
+        }
+    }
     ncclComm_t comm = nullptr;
     ncclResult_t r = nccl().CommInitRankConfig(&comm, world, id, rank, &cfg);
     if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("nccl init: ") + nccl().GetErrorString(r));
@@ -1719,6 +1824,10 @@ int nsb_dist_init(ns_model* m, int rank, int world, const void* id128, int timeo
             return fail("nccl init timed out");
         }
         std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (!m->comm_stream && cudaStreamCreateWithFlags(&m->comm_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        nccl().CommAbort(comm);
+        return fail("communication stream creation failed");
     }
     m->comm = comm;
     m->rank = rank;

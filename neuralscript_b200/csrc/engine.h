@@ -118,6 +118,10 @@ struct ns_model {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     bool group_lost = false;  // the communicator was aborted; train steps fail from then on
+    cudaStream_t comm_stream = nullptr;    // gradient all-reduces, overlapped with the backward
+    std::vector<cudaEvent_t> dist_events;  // ordering events between the two streams
+    size_t ev_next = 0;
+    std::vector<char> reduced;             // per weight: its all-reduce was issued this step
     int timeout_ms = 60000;
     long long launches = 0;
     // per-region CUDA-event timing on the engine stream (opt-in)

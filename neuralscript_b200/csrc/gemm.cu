@@ -235,7 +235,7 @@ struct TcCfg {
     static constexpr uint32_t MN_SBO = TF32 ? 512 : 1024;
     // epilogue staging: per epilogue warp two 2 KB buffers (32 rows x 64 B)
     static constexpr int STAGING = 8 * 2 * 2048;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 512 /*barriers, queue*/;
 };
 
 // Decode a work unit into (m0, n0, kb0, kb1, split, group); returns false
@@ -274,16 +274,7 @@ struct Work {
     int m0, n0, kb0, kb1, split, g, row_end;
 };
 
-// Next work unit of this CTA (units blockIdx.x, +gridDim.x, ...), skipping
-// empty grouped tiles.
-__device__ __forceinline__ bool work_next(const TcParams& p, int BN, int& u, Work& o) {
-    while (u < p.total_units) {
-        const int cur = u;
-        u += gridDim.x;
-        if (tc_decode(p, cur, BN, o.m0, o.n0, o.kb0, o.kb1, o.split, o.g, o.row_end)) return true;
-    }
-    return false;
-}
+constexpr int kQueue = 4;  // depth of the work-unit queue from the scheduler to the MMA / epilogue warps
 
 constexpr int kEpiWarps = 8;                    // two per TMEM lane quarter
 constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // producer warp + MMA warp + epilogue
@@ -299,11 +290,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING);
+    uint4* clc_resp = reinterpret_cast<uint4*>(staging + C::STAGING);  // 16-byte aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(clc_resp + 1);
     uint64_t* empty = full + C::STAGES;
     uint64_t* acc_full = empty + C::STAGES;
     uint64_t* acc_empty = acc_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* clc_bar = acc_empty + 2;
+    uint64_t* q_full = clc_bar + 1;
+    uint64_t* q_empty = q_full + kQueue;
+    int* unit_q = reinterpret_cast<int*>(q_empty + kQueue);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(unit_q + kQueue);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -314,6 +310,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int a = 0; a < 2; a++) {
             ptx::mbar_init(&acc_full[a], 1);
             ptx::mbar_init(&acc_empty[a], 32 * kEpiWarps);
+        }
+        ptx::mbar_init(clc_bar, 1);
+        for (int q = 0; q < kQueue; q++) {
+            ptx::mbar_init(&q_full[q], 1);
+            ptx::mbar_init(&q_empty[q], 1 + kEpiWarps);  // the MMA thread + one lane per epilogue warp
         }
         ptx::fence_mbar_init();
     }
@@ -337,39 +338,84 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---------------- TMA producer ----------------
+            // ---------------- scheduler + TMA producer ----------------
+            // Work units are handed out dynamically: this CTA starts with unit
+            // blockIdx.x and then takes over units of CTAs that have not been
+            // launched yet (cluster launch control: try_cancel). SMs busy with
+            // other work (e.g. a collective running beside this GEMM) simply
+            // launch fewer CTAs. Units reach the MMA and epilogue warps in
+            // order through the shared-memory queue.
             int stage = 0;
             uint32_t phase = 0;
-            int wu = blockIdx.x;
-            Work w;
-            while (work_next(p, BN, wu, w)) {
-                const int m0 = w.m0;
-                const int nb = w.g * p.N + w.n0;  // B row (grouped: groups stacked along N)
-                for (int kb = w.kb0; kb < w.kb1; kb++) {
-                    if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) goto producer_done;
-                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
-                    uint8_t* sb = sa + C::A_BYTES;
-                    ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                    if (!A_MN) {
-                        ptx::tma_load_2d(sa, &ta, &full[stage], kb * C::BK, m0);
-                    } else {
+            int qslot = 0;
+            uint32_t qphase = 0, clc_phase = 0;
+            bool alive = true;     // false after a timed-out wait (error recorded)
+            bool pending = false;  // a try_cancel response is in flight
+            auto push = [&](int unit) -> bool {
+                if (!ptx::mbar_wait(&q_empty[qslot], qphase ^ 1, p.err, kErrTimeoutProducer)) return false;
+                unit_q[qslot] = unit;
+                ptx::mbar_arrive(&q_full[qslot]);
+                if (++qslot == kQueue) {
+                    qslot = 0;
+                    qphase ^= 1;
+                }
+                return true;
+            };
+            int unit = blockIdx.x;
+            while (alive) {
+                // ask for the next unit while this one's tiles load
+                ptx::mbar_arrive_expect_tx(clc_bar, 16);
+                ptx::clc_try_cancel(clc_resp, clc_bar);
+                pending = true;
+                Work w;
+                if (tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end)) {
+                    alive = push(unit);
+                    const int m0 = w.m0;
+                    const int nb = w.g * p.N + w.n0;  // B row (grouped: groups stacked along N)
+                    for (int kb = w.kb0; alive && kb < w.kb1; kb++) {
+                        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
+                            alive = false;
+                            break;
+                        }
+                        uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                        uint8_t* sb = sa + C::A_BYTES;
+                        ptx::mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                        if (!A_MN) {
+                            ptx::tma_load_2d(sa, &ta, &full[stage], kb * C::BK, m0);
+                        } else {
 #pragma unroll
-                        for (int c = 0; c < C::BM / C::CHUNK; c++)
-                            ptx::tma_load_2d(sa + c * (C::BK * 128), &ta, &full[stage], m0 + c * C::CHUNK, kb * C::BK);
-                    }
-                    if (!B_MN) {
-                        ptx::tma_load_2d(sb, &tb, &full[stage], kb * C::BK, nb);
-                    } else {
+                            for (int c = 0; c < C::BM / C::CHUNK; c++)
+                                ptx::tma_load_2d(sa + c * (C::BK * 128), &ta, &full[stage], m0 + c * C::CHUNK,
+                                                 kb * C::BK);
+                        }
+                        if (!B_MN) {
+                            ptx::tma_load_2d(sb, &tb, &full[stage], kb * C::BK, nb);
+                        } else {
 #pragma unroll
-                        for (int c = 0; c < BN / C::CHUNK; c++)
-                            ptx::tma_load_2d(sb + c * (C::BK * 128), &tb, &full[stage], nb + c * C::CHUNK, kb * C::BK);
-                    }
-                    if (++stage == C::STAGES) {
-                        stage = 0;
-                        phase ^= 1;
+                            for (int c = 0; c < BN / C::CHUNK; c++)
+                                ptx::tma_load_2d(sb + c * (C::BK * 128), &tb, &full[stage], nb + c * C::CHUNK,
+                                                 kb * C::BK);
+                        }
+                        if (++stage == C::STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
                     }
                 }
+                // the response is awaited on every path, so none is in flight at exit
+                const bool got = ptx::mbar_wait(clc_bar, clc_phase, p.err, kErrTimeoutProducer);
+                pending = false;
+                clc_phase ^= 1;
+                if (!got) {
+                    alive = false;
+                    break;
+                }
+                int next;
+                if (!ptx::clc_query(clc_resp, next)) break;  // no unlaunched CTA left
+                unit = next;
             }
+            (void)pending;
+            if (alive) push(-1);  // end of work
             // Drain: wait until every issued load has landed before the CTA
             // can exit (bounded).
             for (int s = 0; s < C::STAGES; s++) {
@@ -381,7 +427,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     phase ^= 1;
                 }
             }
-        producer_done:;
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -390,9 +435,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            int wu = blockIdx.x;
+            int qslot = 0;
+            uint32_t qphase = 0;
             Work w;
-            while (work_next(p, BN, wu, w)) {
+            for (;;) {
+                if (!ptx::mbar_wait(&q_full[qslot], qphase, p.err, kErrTimeoutMma)) goto mma_done;
+                const int unit = unit_q[qslot];
+                ptx::mbar_arrive(&q_empty[qslot]);
+                if (++qslot == kQueue) {
+                    qslot = 0;
+                    qphase ^= 1;
+                }
+                if (unit < 0) break;
+                tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end);
                 const int kb0 = w.kb0;
                 if (!ptx::mbar_wait(&acc_empty[acc], acc_phase ^ 1, p.err, kErrTimeoutMma)) goto mma_done;
                 ptx::tc_fence_after();
@@ -512,9 +567,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
         int acc = 0;
         uint32_t acc_phase = 0;
-        int wu = blockIdx.x;
+        int qslot = 0;
+        uint32_t qphase = 0;
         Work w;
-        while (work_next(p, BN, wu, w)) {
+        for (;;) {
+            int unit = -1;
+            if (lane == 0) {
+                if (ptx::mbar_wait(&q_full[qslot], qphase, p.err, kErrTimeoutEpilogue)) unit = unit_q[qslot];
+                ptx::mbar_arrive(&q_empty[qslot]);
+            }
+            unit = __shfl_sync(0xffffffffu, unit, 0);
+            if (++qslot == kQueue) {
+                qslot = 0;
+                qphase ^= 1;
+            }
+            if (unit < 0) break;
+            tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end);
             if (!ptx::mbar_wait(&acc_full[acc], acc_phase, p.err, kErrTimeoutEpilogue)) break;
             ptx::tc_fence_after();
 #pragma unroll 1
@@ -779,7 +847,8 @@ static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         attr = true;
     }
-    int grid = min(p.total_units, num_sms());
+    // one CTA per unit; running CTAs take over the units of CTAs not yet launched
+    int grid = p.total_units;
     if (grid <= 0) return cudaSuccess;
     k<<<grid, kTcThreads, C::SMEM, s>>>(ta, tb, om.z, om.c32, om.c16, p);
     return cudaGetLastError();

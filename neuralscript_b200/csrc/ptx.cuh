@@ -93,6 +93,33 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- cluster launch control (dynamic persistent scheduling) ---------------
+// Ask to cancel a not-yet-launched CTA of this grid; the 16-byte response is
+// written to `resp` with completion counted on `bar` (expect 16 bytes).
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+    asm volatile(
+        "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+            smem_u32(resp)),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+// Decode a response: true and the canceled CTA's x index, or false when no
+// CTA was left to cancel.
+__device__ __forceinline__ bool clc_query(const void* resp, int& ctaid_x) {
+    uint32_t ok, x;
+    asm volatile(
+        "{\n\t.reg .b128 rr;\n\t.reg .pred p;\n\t"
+        "ld.shared.b128 rr, [%2];\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, rr;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, rr;\n\t}"
+        : "=r"(ok), "=r"(x)
+        : "r"(smem_u32(resp))
+        : "memory");
+    ctaid_x = (int)x;
+    return ok != 0;
+}
+
 // ---- tcgen05 ----------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
