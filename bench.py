@@ -241,7 +241,7 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
-def region_work(spec, label, M, train):
+def region_work(spec, label, M, train, world=1):
     """Algorithmic work of one engine region: ("flops"|"bytes", amount)."""
     from neuralscript_b200.spec import parse
     s = parse(spec)
@@ -254,7 +254,12 @@ def region_work(spec, label, M, train):
             # fp32 logits read; training also writes the bf16 seed gradient
             return "bytes", M * 8192 * (4 + (2 if train else 0))
         if label == "optimizer":
-            return "bytes", s.weight_count * 4 * 7
+            # data parallel: the first layer's weights are updated separately (optimizer.last)
+            n = s.weight_count - (s.layout()[0][2] if world > 1 else 0)
+            return "bytes", n * 4 * 7
+        if label == "optimizer.last":
+            # data-parallel split: the first layer's update after its all-reduce
+            return "bytes", s.layout()[0][2] * 4 * 7
         return None, 0
     k = l.kind
     bwd = phase == "bwd"
@@ -401,7 +406,7 @@ def run_b200(args):
             kernels.append({"region": "allreduce (exposed)", "us": tot_ms / n * 1e3, "bound": "nvlink",
                             "achieved": None, "peak": None, "unit": None, "frac": None, "work": None})
             continue
-        kind, work = region_work(spec, label, M, train)
+        kind, work = region_work(spec, label, M, train, world)
         if not kind or n == 0:
             continue
         t = tot_ms / n / 1e3

@@ -694,6 +694,7 @@ static const void* grad_operand(ns_model* m, const float* g, void* tmp16, size_t
 // All ranks issue the same ranges in the same (reverse layer) order.
 // ---------------------------------------------------------------------------
 static int nccl_settle(ns_model* m);
+static int optimizer_step(ns_model* m, float lr, const std::vector<char>* sel = nullptr);
 static bool dist_active(const ns_model* m) { return m->comm && m->world > 1; }
 
 static cudaEvent_t dist_event(ns_model* m) {
@@ -717,6 +718,10 @@ static int dist_reduce_range(ns_model* m, size_t off, size_t count) {
     // a non-blocking communicator may still be enqueueing: wait until the
     // collective sits on its stream before the next NCCL call
     if (r == ncclInProgress && nccl_settle(m)) return -1;
+    cudaEvent_t after = dist_event(m);
+    if (!after) return fail("event creation failed");
+    cudaEventRecord(after, m->comm_stream);
+    m->bucket_done.push_back(after);
     return 0;
 }
 
@@ -727,6 +732,7 @@ static int dist_reduce_weights(ns_model* m, int w0, int w1) {
     for (int w = w0; w < w1; w++)
         if (m->reduced[w]) return 0;
     for (int w = w0; w < w1; w++) m->reduced[w] = 1;
+    m->bucket_w.push_back(std::make_pair(w0, w1));
     const size_t off = s.weights[w0].off;
     size_t end = s.weights[w1 - 1].off + s.weights[w1 - 1].count;
     if (end == s.total) end += 1;
@@ -750,11 +756,44 @@ static int dist_reduce_finish(ns_model* m) {
         if (dist_reduce_weights(m, w, e)) return -1;
         w = e;
     }
-    if (nw == 0 && dist_reduce_range(m, s.total, 1)) return -1;
-    cudaEvent_t done = dist_event(m);
-    if (!done) return fail("event creation failed");
-    cudaEventRecord(done, m->comm_stream);
-    cudaStreamWaitEvent(m->stream, done, 0);
+    if (nw == 0) {
+        m->bucket_w.push_back(std::make_pair(0, 0));
+        if (dist_reduce_range(m, s.total, 1)) return -1;
+    }
+    return 0;
+}
+
+// Optimizer step under data parallelism: the weights of every bucket but the
+// last are updated as soon as their all-reduces are done, while the last
+// bucket (the first layer's gradients, finished last by the backward) is
+// still being reduced; then the rest.
+static int dist_optimizer(ns_model* m, float lr) {
+    const size_t nb = m->bucket_w.size();
+    const size_t nw = m->spec.weights.size();
+    if (nb >= 2) {
+        std::vector<char> early(nw, 0);
+        for (size_t b = 0; b + 1 < nb; b++)
+            for (int w = m->bucket_w[b].first; w < m->bucket_w[b].second; w++) early[w] = 1;
+        cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 2], 0);
+        int ro = region_begin(m, "optimizer");
+        if (optimizer_step(m, lr, &early)) return -1;
+        region_end(m, ro);
+        int ra = region_begin(m, "allreduce");  // what is left to wait for
+        cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 1], 0);
+        region_end(m, ra);
+        std::vector<char> late(nw, 0);
+        for (size_t w = 0; w < nw; w++) late[w] = !early[w];
+        int rl = region_begin(m, "optimizer.last");
+        if (optimizer_step(m, lr, &late)) return -1;
+        region_end(m, rl);
+        return 0;
+    }
+    int ra = region_begin(m, "allreduce");
+    if (nb) cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 1], 0);
+    region_end(m, ra);
+    int ro = region_begin(m, "optimizer");
+    if (optimizer_step(m, lr)) return -1;
+    region_end(m, ro);
     return 0;
 }
 
@@ -1068,7 +1107,8 @@ struct AdamTensorLocal {
 
 static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* out);
 
-static int optimizer_step(ns_model* m, float lr) {
+// Optimizer update of all weights, or of those marked in `sel`.
+static int optimizer_step(ns_model* m, float lr, const std::vector<char>* sel) {
     const Spec& s = m->spec;
     const std::string& mode = s.optimizer;
     const bool ref = mode == "reference";
@@ -1086,6 +1126,10 @@ static int optimizer_step(ns_model* m, float lr) {
     std::vector<AdamTensor> at;
     std::vector<char> fresh(s.weights.size(), 0);  // working copy written by the AdamW pass
     for (size_t wi = 0; wi < s.weights.size(); wi++) {
+        if (sel && !(*sel)[wi]) {
+            fresh[wi] = 1;  // not part of this update: leave its working copy alone
+            continue;
+        }
         const WeightInfo& w = s.weights[wi];
         const bool matrix = w.rows > 1 && w.cols > 1;
         const int mn = w.rows < w.cols ? w.rows : w.cols;
@@ -1559,15 +1603,17 @@ static int train_core(ns_model* m, int M, const float* d_labels, const int* d_ta
         if (dist_active(m)) {
             m->reduced.assign(m->spec.weights.size(), 0);
             m->ev_next = 0;
+            m->bucket_w.clear();
+            m->bucket_done.clear();
         }
         if (backward(m, M)) return -1;
-        // the part of the gradient all-reduce not hidden behind the backward
-        int ra = region_begin(m, "allreduce");
-        if (dist_active(m) && dist_reduce_finish(m)) return -1;
-        region_end(m, ra);
-        int ro = region_begin(m, "optimizer");
-        if (optimizer_step(m, lr)) return -1;
-        region_end(m, ro);
+        if (dist_active(m)) {
+            if (dist_reduce_finish(m) || dist_optimizer(m, lr)) return -1;
+        } else {
+            int ro = region_begin(m, "optimizer");
+            if (optimizer_step(m, lr)) return -1;
+            region_end(m, ro);
+        }
         m->host_dirty = true;
         const float gscale = 1.0f / ((float)M * (float)m->world *
                                      (m->spec.loss == "mse" ? (float)m->spec.out_cols : 1.f));

@@ -122,6 +122,8 @@ struct ns_model {
     std::vector<cudaEvent_t> dist_events;  // ordering events between the two streams
     size_t ev_next = 0;
     std::vector<char> reduced;             // per weight: its all-reduce was issued this step
+    std::vector<std::pair<int, int>> bucket_w;  // weight ranges in all-reduce issue order
+    std::vector<cudaEvent_t> bucket_done;       // recorded on the comm stream after each range
     int timeout_ms = 60000;
     long long launches = 0;
     // per-region CUDA-event timing on the engine stream (opt-in)
