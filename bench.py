@@ -401,6 +401,11 @@ def run_b200(args):
     model.region_timing(False)
     kernels = []
     for label, (tot_ms, n) in regs.items():
+        if label.startswith("host:") and n:
+            # host-side intervals (launching, waiting on NCCL / the GPU)
+            kernels.append({"region": label, "us": tot_ms / n * 1e3, "bound": "host",
+                            "achieved": None, "peak": None, "unit": None, "frac": None, "work": None})
+            continue
         if label == "allreduce" and n:
             # the part of the gradient all-reduce not hidden behind the backward
             kernels.append({"region": "allreduce (exposed)", "us": tot_ms / n * 1e3, "bound": "nvlink",

@@ -73,9 +73,10 @@ int nsb_runtime_train_step_idx(ns_model* m, const float* input, const int* targe
 /* Device-resident variants: pointers are device memory, `stream` the
  * caller's cudaStream_t (NULL = the legacy default stream). The work is
  * ordered after prior work on `stream`, and later work on `stream` sees the
- * outputs. eval returns without host synchronisation; the train step
- * synchronises (it reports device errors and, if loss_out is not NULL, the
- * loss). */
+ * outputs; neither call blocks the host on the GPU, except that a train step
+ * given a non-NULL loss_out waits for the step to finish and returns the
+ * loss. Device-side errors of a non-blocking call (a timed-out pipeline
+ * wait, a failed collective) are reported by the next call that waits. */
 int nsb_eval_infer_device(ns_model* m, const float* d_input, float* d_output, size_t input_numel, void* stream);
 int nsb_train_step_device(ns_model* m, const float* d_input, const float* d_labels, const int* d_targets,
                           size_t input_numel, float* loss_out, float lr, void* stream);

@@ -504,6 +504,22 @@ static void region_end(ns_model* m, int idx) {
     cudaEventRecord(m->regions[idx].pending.back().second, m->stream);
 }
 
+// A host-measured interval (e.g. time spent waiting on NCCL), folded into the
+// same per-region totals.
+static void host_region_add(ns_model* m, const char* label, double ms) {
+    if (!m->timing) return;
+    for (auto& r : m->regions)
+        if (r.label == label) {
+            r.ms += ms;
+            r.count++;
+            return;
+        }
+    m->regions.push_back(ns_model::Region());
+    m->regions.back().label = label;
+    m->regions.back().ms = ms;
+    m->regions.back().count = 1;
+}
+
 static void regions_collect(ns_model* m) {
     for (auto& r : m->regions) {
         for (auto& ev : r.pending) {
@@ -1252,7 +1268,11 @@ static int nccl_settle(ns_model* m) {
     for (;;) {
         ncclResult_t st;
         nccl().CommGetAsyncError(m->comm, &st);
-        if (st == ncclSuccess) return 0;
+        if (st == ncclSuccess) {
+            host_region_add(m, "host:nccl_enqueue",
+                            std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+            return 0;
+        }
         if (st != ncclInProgress) {
             nccl().CommAbort(m->comm);
             m->comm = nullptr;
@@ -1461,6 +1481,8 @@ void nsb_free(ns_model* m) {
     }
     if (m->h_loss) cudaFreeHost(m->h_loss);
     if (m->comm_stream) cudaStreamSynchronize(m->comm_stream);
+    if (m->ev_in) cudaEventDestroy(m->ev_in);
+    if (m->ev_out) cudaEventDestroy(m->ev_out);
     if (m->comm) nccl().CommDestroy(m->comm);
     for (cudaEvent_t e : m->dist_events) cudaEventDestroy(e);
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
@@ -1637,7 +1659,13 @@ static int train_entry(ns_model* m, const float* input, const float* labels, con
     if (plan(m, M, true)) return -1;
     cudaMemcpyKind k = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     cudaStream_t us = stream ? (cudaStream_t)stream : cudaStreamLegacy;
-    if (device_ptrs) cudaStreamSynchronize(us);  // inputs produced on the caller's stream
+    if (device_ptrs) {
+        // inputs are produced on the caller's stream: order after it on the GPU
+        if (!m->ev_in && cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming) != cudaSuccess)
+            return fail("event creation failed");
+        cudaEventRecord(m->ev_in, us);
+        cudaStreamWaitEvent(m->stream, m->ev_in, 0);
+    }
     cudaMemcpyAsync(m->d_in, input, sizeof(float) * (size_t)M * m->spec.in_cols, k, m->stream);
     const float* dl = nullptr;
     const int* dt = nullptr;
@@ -1654,9 +1682,24 @@ static int train_entry(ns_model* m, const float* input, const float* labels, con
         if (st < 9223372036854775807LL) m->lr_step = st + 1;
         lr_eff = lr * lr_schedule(m, st);
     }
+    const auto h0 = std::chrono::steady_clock::now();
     int rc = train_core(m, M, dl, dt, loss_out, lr_eff, train);
     m->launches = launch_counter() - l0;
+    const auto h1 = std::chrono::steady_clock::now();
+    if (device_ptrs && !loss_out && !rc) {
+        // stream-ordered: later work on the caller's stream follows this step;
+        // device errors surface at the next synchronising call
+        if (!m->ev_out && cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess)
+            return fail("event creation failed");
+        cudaEventRecord(m->ev_out, m->stream);
+        cudaStreamWaitEvent(us, m->ev_out, 0);
+        host_region_add(m, "host:launch", std::chrono::duration<double, std::milli>(h1 - h0).count());
+        return cudaGetLastError() == cudaSuccess ? 0 : fail("kernel launch failed");
+    }
     int rf = finish(m);
+    host_region_add(m, "host:launch", std::chrono::duration<double, std::milli>(h1 - h0).count());
+    host_region_add(m, "host:wait",
+                    std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - h1).count());
     if (rc || rf) return -1;
     if (loss_out) *loss_out = *m->h_loss;
     return 0;

@@ -118,6 +118,7 @@ struct ns_model {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     bool group_lost = false;  // the communicator was aborted; train steps fail from then on
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;  // ordering with the caller's stream (device entries)
     cudaStream_t comm_stream = nullptr;    // gradient all-reduces, overlapped with the backward
     std::vector<cudaEvent_t> dist_events;  // ordering events between the two streams
     size_t ev_next = 0;
