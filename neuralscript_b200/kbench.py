@@ -6,6 +6,9 @@ events on the launching stream after warm-up.
     python -m neuralscript_b200.kbench gemm --M 16384 --N 8192 --K 512 --out f32
     python -m neuralscript_b200.kbench attention --B 64 --S 256 --H 8 --D 512
     python -m neuralscript_b200.kbench layernorm --M 16384 --D 512
+    python -m neuralscript_b200.kbench ce --M 16384 --C 8192
+    python -m neuralscript_b200.kbench embedding --M 16384 --V 8192 --D 512 --backward
+    python -m neuralscript_b200.kbench adamw --n 11534336
 
 Prints one JSON line per run: average launch time, achieved TFLOP/s or GB/s
 and the fraction of the measured peak (MEASURED_PEAKS.json).
@@ -96,9 +99,59 @@ def layernorm_case(M, D, iters=50):
             "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_kind": kind}
 
 
+def cross_entropy_case(M, C, iters=20):
+    """Single-pass CE over fp32 logits [M, C] with int32 targets, bf16 seed gradient."""
+    import torch
+    from . import ops as O
+    logits = torch.randn(M, C, device="cuda")
+    tgt = torch.randint(0, C, (M,), device="cuda", dtype=torch.int32)
+    row = torch.empty(M, device="cuda")
+    d16 = torch.empty(M, C, device="cuda", dtype=torch.bfloat16)
+    t = _time(lambda: O.cross_entropy(logits, targets=tgt, row_loss=row, d16=d16), iters)
+    pk, kind = _peaks()
+    gbs = M * C * (4 + 2) / t / 1e9
+    return {"kernel": "cross_entropy", "M": M, "C": C, "us": t * 1e6, "gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"],
+            "peak_kind": kind}
+
+
+def embedding_case(M, V, D, iters=20, backward=False):
+    """Gather (fp32 + bf16 out) and the deterministic sort-then-segment gradient."""
+    import torch
+    from . import ops as O
+    W = torch.randn(V, D, device="cuda")
+    ids = torch.randint(0, V, (M,), device="cuda").float()
+    o32 = torch.empty(M, D, device="cuda")
+    o16 = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    t = _time(lambda: O.embedding_fwd(W, ids, o32, o16), iters)
+    pk, kind = _peaks()
+    res = {"kernel": "embedding_fwd", "M": M, "V": V, "D": D, "us": t * 1e6,
+           "gbs": M * D * (4 + 4 + 2) / t / 1e9, "peak_kind": kind}
+    res["frac_of_hbm"] = res["gbs"] / pk["hbm_gbs"]
+    if backward:
+        dW = torch.empty(V, D, device="cuda")
+        tb = _time(lambda: O.embedding_bwd(o32, ids, V, dW), iters)
+        res.update({"bwd_us": tb * 1e6, "bwd_gbs": (M * D + V * D) * 4 / tb / 1e9})
+    return res
+
+
+def adamw_case(n, iters=20):
+    """One AdamW tensor of n parameters (w, g, m, v read; w, m, v written)."""
+    import torch
+    from . import ops as O
+    w, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    v.abs_()
+    t = _time(lambda: O.adamw(w, g, m, v, 1, 1e-4), iters)
+    pk, kind = _peaks()
+    gbs = n * 4 * 7 / t / 1e9
+    return {"kernel": "adamw", "n": n, "us": t * 1e6, "gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_kind": kind}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "layernorm"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "layernorm", "ce", "embedding", "adamw"])
+    ap.add_argument("--C", type=int, default=8192)
+    ap.add_argument("--V", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=11_534_336)
     ap.add_argument("--M", type=int, default=16384)
     ap.add_argument("--N", type=int, default=2048)
     ap.add_argument("--K", type=int, default=512)
@@ -117,8 +170,14 @@ def main():
         r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters, a.out, a.residual)
     elif a.kernel == "attention":
         r = attention_case(a.B, a.S, a.H, a.D, a.iters, a.backward)
-    else:
+    elif a.kernel == "layernorm":
         r = layernorm_case(a.M, a.D, a.iters)
+    elif a.kernel == "ce":
+        r = cross_entropy_case(a.M, a.C, a.iters)
+    elif a.kernel == "embedding":
+        r = embedding_case(a.M, a.V, a.D, a.iters, a.backward)
+    else:
+        r = adamw_case(a.n, a.iters)
     print(json.dumps(r))
 
 
