@@ -180,6 +180,45 @@ __global__ void emb_fill_kernel(const float* __restrict__ ids, int M, int V, con
     }
 }
 
+// Sum of the listed dOut rows (ascending row order) into dst for D = 128*CH:
+// each lane owns CH float4 columns; two rows are loaded before either is
+// added, so a warp keeps 2*CH independent loads in flight while the sums
+// stay in row order (bit-identical to a one-row-at-a-time loop).
+template <int CH>
+__device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int D, const int* rows_sorted, int n,
+                                             float* __restrict__ dst, int lane) {
+    float4 acc[CH];
+#pragma unroll
+    for (int c = 0; c < CH; c++) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int q = 0;
+    for (; q + 1 < n; q += 2) {
+        const float4* r0 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q] * D) + lane;
+        const float4* r1 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q + 1] * D) + lane;
+        float4 t0[CH], t1[CH];
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            t0[c] = __ldcs(r0 + 32 * c);
+            t1[c] = __ldcs(r1 + 32 * c);
+        }
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            acc[c].x += t0[c].x; acc[c].y += t0[c].y; acc[c].z += t0[c].z; acc[c].w += t0[c].w;
+            acc[c].x += t1[c].x; acc[c].y += t1[c].y; acc[c].z += t1[c].z; acc[c].w += t1[c].w;
+        }
+    }
+    if (q < n) {
+        const float4* r0 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q] * D) + lane;
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+            const float4 t = __ldcs(r0 + 32 * c);
+            acc[c].x += t.x; acc[c].y += t.y; acc[c].z += t.z; acc[c].w += t.w;
+        }
+    }
+    float4* d4 = reinterpret_cast<float4*>(dst) + lane;
+#pragma unroll
+    for (int c = 0; c < CH; c++) d4[32 * c] = acc[c];
+}
+
 // One warp per vocabulary row: gather the rows that hit it, order them by
 // row index, and sum their gradients in that order. The sorted row ids are
 // staged in shared memory so the column loops (where only some lanes may be
@@ -214,7 +253,15 @@ __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, 
             }
             sorted[wi][lane] = key;
             __syncwarp();
-            if (vec) {
+            if (vec && D == 512) {
+                emb_sum_rows<4>(dout, D, sorted[wi], n, dst, lane);
+            } else if (vec && D == 256) {
+                emb_sum_rows<2>(dout, D, sorted[wi], n, dst, lane);
+            } else if (vec && D == 128) {
+                emb_sum_rows<1>(dout, D, sorted[wi], n, dst, lane);
+            } else if (vec && D == 1024) {
+                emb_sum_rows<8>(dout, D, sorted[wi], n, dst, lane);
+            } else if (vec) {
                 for (int c = lane * 4; c < D; c += 128) {
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                     for (int q = 0; q < n; q++) {
