@@ -241,6 +241,23 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+# DRAM bytes (read + write) per launch of a region's dominant kernel, from
+# one ncu capture each (profiles/<name>.md, `dram__bytes_read.sum +
+# dram__bytes_write.sum`), for the 16384-row shapes of configs 2 and 4
+# (LayerNorm was captured at 131072 rows and is scaled by 1/8). Writes still
+# in L2 at the end of a captured kernel are not counted by that capture.
+NCU_TRAFFIC = {
+    "fwd:ff1": (33.4e6, "gemm_tc_ff1_16384x2048x512_gelu.md"),
+    "fwd:head": (508.7e6, "gemm_tc_head_16384x8192x512_f32out.md"),
+    "loss": (768.4e6, "cross_entropy_rows_16384x8192.md"),
+    "optimizer": (268.3e6, "adamw_11534336.md"),
+    "fwd:attn.core": (50.6e6, "attn_tc_fwd_b64_s256_h8_d512.md"),
+    "bwd:attn.core": (99.8e6, "attn_tc_bwd_b64_s256_h8_d512.md"),
+    "fwd:ln1": (77.2e6, "layernorm_fwd_vec_131072x512.md"),
+    "fwd:ln2": (77.2e6, "layernorm_fwd_vec_131072x512.md"),
+}
+
+
 def region_work(spec, label, M, train, world=1):
     """Algorithmic work of one engine region: ("flops"|"bytes", amount)."""
     from neuralscript_b200.spec import parse
@@ -427,7 +444,10 @@ def run_b200(args):
     if ranked:
         top = ranked[0]
         roof = {"kernel": top["region"], "bound": top["bound"], "achieved": top["achieved"], "peak": top["peak"],
-                "unit": top["unit"], "frac": top["frac"], "traffic": None,
+                "unit": top["unit"], "frac": top["frac"],
+                "traffic": NCU_TRAFFIC.get(top["region"], (None,))[0] if M == 16384 else None,
+                "traffic_source": (("profiles/" + NCU_TRAFFIC[top["region"]][1])
+                                   if top["region"] in NCU_TRAFFIC and M == 16384 else None),
                 "peak_kind": f"{pk_kind} ({'bf16 burst' if top['bound'] == 'tensor' else 'HBM copy'})",
                 "us_per_launch": top["us"]}
 

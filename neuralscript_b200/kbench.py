@@ -45,14 +45,17 @@ def _time(fn, iters, warmup=3):
     return e0.elapsed_time(e1) / iters / 1e3
 
 
-def gemm_case(M, N, K, act="none", dtype="bf16", iters=20, out="bf16", residual=False):
-    """The engine's forward layout: A [M,K] K-major, W [K,N] row-major (MN-major B);
-    output bf16 or fp32, optionally plus an fp32 residual [M,N]."""
+def gemm_case(M, N, K, act="none", dtype="bf16", iters=20, out="bf16", residual=False, a_mn=0, b_mn=1):
+    """C[M,N] = A B^T with A stored [M,K] (K-major) or [K,M] (a_mn=1) and B
+    stored [N,K] or [K,N] (b_mn=1). Defaults are the engine's forward layout
+    (W [K,N] row-major); input gradients use a_mn=0, b_mn=0 and weight
+    gradients a_mn=1, b_mn=1. Output bf16 or fp32, optionally plus an fp32
+    residual [M,N]."""
     import torch
     from . import ops as O
     dt = torch.bfloat16 if dtype == "bf16" else torch.float32
-    A = torch.randn(M, K, device="cuda").to(dt)
-    B = torch.randn(K, N, device="cuda").to(dt)
+    A = torch.randn(*((K, M) if a_mn else (M, K)), device="cuda").to(dt)
+    B = torch.randn(*((K, N) if b_mn else (N, K)), device="cuda").to(dt)
     kw = {"act": ACTS[act]}
     if out == "bf16":
         kw["c16"] = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -60,12 +63,14 @@ def gemm_case(M, N, K, act="none", dtype="bf16", iters=20, out="bf16", residual=
         kw["c32"] = torch.empty(M, N, device="cuda")
     if residual:
         kw["add"] = torch.randn(M, N, device="cuda")
-    t = _time(lambda: O.gemm(A, B, M, N, K, K, 0, N, 1, **kw), iters)
+    lda, ldb = A.stride(0), B.stride(0)
+    t = _time(lambda: O.gemm(A, B, M, N, K, lda, a_mn, ldb, b_mn, **kw), iters)
     pk, kind = _peaks()
     tf = 2.0 * M * N * K / t / 1e12
     return {"kernel": "gemm", "M": M, "N": N, "K": K, "act": act, "dtype": dtype, "out": out,
             "residual": residual, "us": t * 1e6, "tflops": tf, "frac_of_bf16_peak": tf / pk["bf16_tflops"],
-            "peak_kind": kind, "tensor_cores": O.uses_tensor_cores(A, B, M, N, K, K, 0, N, 1)}
+            "a_mn": a_mn, "b_mn": b_mn, "peak_kind": kind,
+            "tensor_cores": O.uses_tensor_cores(A, B, M, N, K, lda, a_mn, ldb, b_mn)}
 
 
 def attention_case(B, S, H, D, iters=20, backward=False):
@@ -165,9 +170,11 @@ def main():
     ap.add_argument("--backward", action="store_true")
     ap.add_argument("--out", default="bf16", choices=["bf16", "f32"])
     ap.add_argument("--residual", action="store_true")
+    ap.add_argument("--a-mn", type=int, default=0)
+    ap.add_argument("--b-mn", type=int, default=1)
     a = ap.parse_args()
     if a.kernel == "gemm":
-        r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters, a.out, a.residual)
+        r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters, a.out, a.residual, a.a_mn, a.b_mn)
     elif a.kernel == "attention":
         r = attention_case(a.B, a.S, a.H, a.D, a.iters, a.backward)
     elif a.kernel == "layernorm":
