@@ -132,38 +132,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mph ^= 1;
         ptx::tc_fence_after();
         // ---- softmax over this thread's 128 keys of row r ----
+        // all four 32-column TMEM loads in flight, one wait; the row stays in
+        // registers for both the max and the exponentials
         const int c_lo = half * 128;
+        uint32_t sv[128];
+        ptx::tmem_ld32(lane_base + c_lo, sv);
+        ptx::tmem_ld32(lane_base + c_lo + 32, sv + 32);
+        ptx::tmem_ld32(lane_base + c_lo + 64, sv + 64);
+        ptx::tmem_ld32(lane_base + c_lo + 96, sv + 96);
+        ptx::tmem_ld_wait();
         float mx = -INFINITY;
-#pragma unroll 1
-        for (int c = c_lo; c < c_lo + 128; c += 32) {
-            uint32_t v[32];
-            ptx::tmem_ld32(lane_base + c, v);
-            ptx::tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-                if (c + j < S) mx = fmaxf(mx, __uint_as_float(v[j]) * sl2);
-        }
+        for (int j = 0; j < 128; j++)
+            if (c_lo + j < S) mx = fmaxf(mx, __uint_as_float(sv[j]) * sl2);
         xch[half * kQ + r] = mx;
         __syncthreads();
         mx = fmaxf(xch[r], xch[kQ + r]);
         float sum = 0.f;
-#pragma unroll 1
-        for (int c = c_lo; c < c_lo + 128; c += 32) {
-            uint32_t v[32];
-            ptx::tmem_ld32(lane_base + c, v);
-            ptx::tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 128; c += 32) {
             float p[32];
 #pragma unroll
             for (int j = 0; j < 32; j++) {
-                p[j] = (c + j < S) ? ex2_approx(fmaf(__uint_as_float(v[j]), sl2, -mx)) : 0.f;
+                p[j] = (c_lo + c + j < S) ? ex2_approx(fmaf(__uint_as_float(sv[c + j]), sl2, -mx)) : 0.f;
                 sum += p[j];
             }
-            // 32 keys = 4 granules of 16 bytes in 64-key chunk c/64, granule
-            // index (c%64)/8 + g, XOR-swizzled by row % 8 (128-byte swizzle)
-            uint8_t* chunk = sP + (c >> 6) * kPChunk + r * 128;
+            // 32 keys = 4 granules of 16 bytes in 64-key chunk (c_lo+c)/64,
+            // granule index ((c_lo+c)%64)/8 + g, XOR-swizzled by row % 8
+            uint8_t* chunk = sP + ((c_lo + c) >> 6) * kPChunk + r * 128;
 #pragma unroll
             for (int g = 0; g < 4; g++) {
-                const int gi = ((c & 63) >> 3) + g;
+                const int gi = (((c_lo + c) & 63) >> 3) + g;
                 uint4 pk;
                 __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
@@ -416,12 +415,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const bool kval = kg < S;
         uint8_t* prow = sP + half * kTile + r * 128;
         uint8_t* drow = sD + half * kTile + r * 128;
-#pragma unroll 1
+        // both 32-column halves of S^T and dP^T in flight, one wait
+        uint32_t sva[64], pva[64];
+        ptx::tmem_ld32(lane_base + half * 64, sva);
+        ptx::tmem_ld32(lane_base + half * 64 + 32, sva + 32);
+        ptx::tmem_ld32(lane_base + kBT + half * 64, pva);
+        ptx::tmem_ld32(lane_base + kBT + half * 64 + 32, pva + 32);
+        ptx::tmem_ld_wait();
+#pragma unroll
         for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
-            uint32_t sv[32], pv[32];
-            ptx::tmem_ld32(lane_base + c0, sv);
-            ptx::tmem_ld32(lane_base + kBT + c0, pv);
-            ptx::tmem_ld_wait();
+            const uint32_t* sv = sva + (c0 - half * 64);
+            const uint32_t* pv = pva + (c0 - half * 64);
             float p[32], ds[32];
 #pragma unroll
             for (int e = 0; e < 32; e++) {
