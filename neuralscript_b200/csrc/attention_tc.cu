@@ -62,8 +62,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint8_t* sP = smem + 2 * kBufBytes;
     float* xch = reinterpret_cast<float*>(sP + kPBytes);  // [2][kQ] half-row max / sum exchange
     uint64_t* ld_bar = reinterpret_cast<uint64_t*>(xch + 2 * kQ);  // [2]
-    uint64_t* mma_bar = ld_bar + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+    uint64_t* s_bar = ld_bar + 2;  // S = QK^T of the current item done
+    uint64_t* o_bar = s_bar + 1;   // O = PV of the current item done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_bar + 1);
 
     const int t = threadIdx.x, warp = t >> 5;
     const int lg = warp & 3, half = warp >> 2;
@@ -74,7 +75,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (t == 0) {
         ptx::mbar_init(&ld_bar[0], 1);
         ptx::mbar_init(&ld_bar[1], 1);
-        ptx::mbar_init(mma_bar, 1);
+        ptx::mbar_init(s_bar, 1);
+        ptx::mbar_init(o_bar, 1);
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tqkv);
     }
@@ -107,8 +109,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
 
     bool ok = true;
-    uint32_t mph = 0;
+    uint32_t sph = 0, oph = 0;
     const float sl2 = scale * kLog2e;  // score -> log2 units
+    // S = Q K^T of the item in buffer `b` into TMEM columns [0, 256)
+    auto issue_s = [&](int b) {
+        const uint32_t q = ptx::smem_u32(smem + b * kBufBytes), k = q + kQBytes;
+#pragma unroll
+        for (int st = 0; st < kDh / 16; st++)
+            ptx::mma_bf16(tmem, ptx::smem_desc(q + st * 32, 16, 1024, 2), ptx::smem_desc(k + st * 32, 16, 1024, 2),
+                          kIdescS, st > 0);
+    };
+    // The S MMA of the next item is issued right behind this item's PV MMA,
+    // so it runs while this item's epilogue reads O.
+    if (t == 0 && (int)blockIdx.x < items) {
+        ok = ptx::mbar_wait(&ld_bar[0], 0, err, kErrTimeoutAttn) && ok;
+        ptx::tc_fence_after();
+        if (ok) issue_s(0);
+        ptx::mma_commit(s_bar);
+    }
     int li = 0;
 #pragma unroll 1
     for (int it = blockIdx.x; it < items; it += gridDim.x, li++) {
@@ -117,19 +135,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int row0 = b * S, q0 = qt * kQ;
         const uint32_t aQ = ptx::smem_u32(smem + buf * kBufBytes);
         const uint32_t aK = aQ + kQBytes, aV = aK + kKBytes;
-        if (t == 0) {
-            ok = ptx::mbar_wait(&ld_bar[buf], (li >> 1) & 1, err, kErrTimeoutAttn) && ok;
-            ptx::tc_fence_after();
-            if (ok) {
-#pragma unroll
-                for (int s = 0; s < kDh / 16; s++)
-                    ptx::mma_bf16(tmem, ptx::smem_desc(aQ + s * 32, 16, 1024, 2), ptx::smem_desc(aK + s * 32, 16, 1024, 2),
-                                  kIdescS, s > 0);
-            }
-            ptx::mma_commit(mma_bar);
-        }
-        ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
-        mph ^= 1;
+        (void)aK;
+        ok = ptx::mbar_wait(s_bar, sph, err, kErrTimeoutAttn) && ok;
+        sph ^= 1;
         ptx::tc_fence_after();
         // ---- softmax over this thread's 128 keys of row r ----
         // all four 32-column TMEM loads in flight, one wait; the row stays in
@@ -141,21 +149,44 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ptx::tmem_ld32(lane_base + c_lo + 64, sv + 64);
         ptx::tmem_ld32(lane_base + c_lo + 96, sv + 96);
         ptx::tmem_ld_wait();
-        float mx = -INFINITY;
+        // eight independent partial maxima of the raw scores (short dependency
+        // chains), scaled once; a key tile that lies wholly inside the
+        // sequence needs no per-element mask
+        const bool full_tile = c_lo + 128 <= S;
+        float m8[8];
 #pragma unroll
-        for (int j = 0; j < 128; j++)
-            if (c_lo + j < S) mx = fmaxf(mx, __uint_as_float(sv[j]) * sl2);
+        for (int q = 0; q < 8; q++) m8[q] = -INFINITY;
+        if (full_tile) {
+#pragma unroll
+            for (int j = 0; j < 128; j++) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(sv[j]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 128; j++)
+                if (c_lo + j < S) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(sv[j]));
+        }
+        float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        mx *= sl2;  // scale > 0: max of the scaled scores (-inf when no key is valid)
         xch[half * kQ + r] = mx;
         __syncthreads();
         mx = fmaxf(xch[r], xch[kQ + r]);
-        float sum = 0.f;
+        float s8[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) s8[q] = 0.f;
 #pragma unroll
         for (int c = 0; c < 128; c += 32) {
             float p[32];
+            if (full_tile) {
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                p[j] = (c_lo + c + j < S) ? ex2_approx(fmaf(__uint_as_float(sv[c + j]), sl2, -mx)) : 0.f;
-                sum += p[j];
+                for (int j = 0; j < 32; j++) {
+                    p[j] = ex2_approx(fmaf(__uint_as_float(sv[c + j]), sl2, -mx));
+                    s8[j & 7] += p[j];
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    p[j] = (c_lo + c + j < S) ? ex2_approx(fmaf(__uint_as_float(sv[c + j]), sl2, -mx)) : 0.f;
+                    s8[j & 7] += p[j];
+                }
             }
             // 32 keys = 4 granules of 16 bytes in 64-key chunk (c_lo+c)/64,
             // granule index ((c_lo+c)%64)/8 + g, XOR-swizzled by row % 8
@@ -170,12 +201,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 *reinterpret_cast<uint4*>(chunk + ((gi ^ (r & 7)) << 4)) = pk;
             }
         }
+        const float sum_part = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
         __syncthreads();  // everyone has read the max exchange
-        xch[half * kQ + r] = sum;
+        xch[half * kQ + r] = sum_part;
         ptx::fence_proxy_async();  // generic-proxy P writes -> tensor-core (async proxy) reads
         ptx::tc_fence_before();
         __syncthreads();
-        sum = xch[r] + xch[kQ + r];
+        const float sum = xch[r] + xch[kQ + r];
         if (t == 0) {
             ptx::tc_fence_after();
             if (ok) {
@@ -187,10 +219,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     ptx::mma_bf16(tmem + kKeys, ad, bd, kIdescO, s > 0);
                 }
             }
-            ptx::mma_commit(mma_bar);
+            ptx::mma_commit(o_bar);
+            // the next item's S (its Q/K were loaded two items ago)
+            if (it + (int)gridDim.x < items) {
+                ok = ptx::mbar_wait(&ld_bar[buf ^ 1], ((li + 1) >> 1) & 1, err, kErrTimeoutAttn) && ok;
+                ptx::tc_fence_after();
+                if (ok) issue_s(buf ^ 1);
+                ptx::mma_commit(s_bar);
+            }
         }
-        ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
-        mph ^= 1;
+        ok = ptx::mbar_wait(o_bar, oph, err, kErrTimeoutAttn) && ok;
+        oph ^= 1;
         ptx::tc_fence_after();
         // this item's Q/K/V buffer is free: load the item two steps ahead
         if (t == 0 && it + 2 * (int)gridDim.x < items) issue_load(it + 2 * gridDim.x, buf);
@@ -422,18 +461,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ptx::tmem_ld32(lane_base + kBT + half * 64, pva);
         ptx::tmem_ld32(lane_base + kBT + half * 64 + 32, pva + 32);
         ptx::tmem_ld_wait();
+        // a (key tile, query tile) pair wholly inside the sequence needs no masks
+        const bool full_pair = (j + 1) * kBT <= S && (i + 1) * kBT <= S;
 #pragma unroll
         for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
             const uint32_t* sv = sva + (c0 - half * 64);
             const uint32_t* pv = pva + (c0 - half * 64);
             float p[32], ds[32];
+            // per-query lse and rowdot(dO, O), four at a time (broadcast reads)
+            const float4* l4 = reinterpret_cast<const float4*>(lse_s + i * kBT + c0);
+            const float4* d4 = reinterpret_cast<const float4*>(dv_s + i * kBT + c0);
+            if (full_pair) {
 #pragma unroll
-            for (int e = 0; e < 32; e++) {
-                const int qg = i * kBT + c0 + e;
-                const bool v = kval && qg < S;
-                const float pe = v ? ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -lse_s[qg])) : 0.f;
-                p[e] = pe;
-                ds[e] = v ? pe * (__uint_as_float(pv[e]) - dv_s[qg]) : 0.f;
+                for (int e4 = 0; e4 < 8; e4++) {
+                    const float4 L = l4[e4], Dd = d4[e4];
+                    const float Ls[4] = {L.x, L.y, L.z, L.w}, Ds[4] = {Dd.x, Dd.y, Dd.z, Dd.w};
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int e = 4 * e4 + q;
+                        const float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -Ls[q]));
+                        p[e] = pe;
+                        ds[e] = pe * (__uint_as_float(pv[e]) - Ds[q]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    const int qg = i * kBT + c0 + e;
+                    const bool v = kval && qg < S;
+                    const float pe = v ? ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -lse_s[qg])) : 0.f;
+                    p[e] = pe;
+                    ds[e] = v ? pe * (__uint_as_float(pv[e]) - dv_s[qg]) : 0.f;
+                }
             }
 #pragma unroll
             for (int g = 0; g < 4; g++) {
