@@ -307,7 +307,8 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t
 }
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
-    attn_tc_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo, int S,
+    attn_tc_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
+                       const __grid_constant__ CUtensorMap tctx, int S,
                        int H, int D, float scale, const __nv_bfloat16* __restrict__ ctx, long long ld_ctx,
                        const __nv_bfloat16* __restrict__ dctx, long long ld_dctx, const float* __restrict__ lse,
                        __nv_bfloat16* __restrict__ dqkv, long long ld_dqkv, int* err) {
@@ -322,8 +323,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     float* lse_s = reinterpret_cast<float*>(sD + 2 * kTile);
     float* dv_s = lse_s + 256;
     uint64_t* ld_bar = reinterpret_cast<uint64_t*>(dv_s + 256);
-    uint64_t* mma_bar = ld_bar + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+    uint64_t* mma_bar = ld_bar + 1;  // MMA1 (S^T, dP^T) of the current step done
+    uint64_t* o_bar = mma_bar + 1;   // MMA2 (dV, dK, dQ) of the previous step done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_bar + 1);
 
     const int h = blockIdx.x, b = blockIdx.y;
     const int t = threadIdx.x, warp = t >> 5;
@@ -335,9 +337,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (t == 0) {
         ptx::mbar_init(ld_bar, 1);
         ptx::mbar_init(mma_bar, 1);
+        ptx::mbar_init(o_bar, 1);
         ptx::fence_mbar_init();
         ptx::prefetch_tmap(&tqkv);
         ptx::prefetch_tmap(&tdo);
+        ptx::prefetch_tmap(&tctx);
     }
     if (warp == 0) {
         ptx::tmem_alloc(tmem_slot, 512);
@@ -349,32 +353,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = tmem + ((uint32_t)(lg * 32) << 16);
 
+    // Q, K, V, dO of the whole sequence, and O (ctx) into the P^T buffer,
+    // which is free until the first step: rowdot(dO, O) is then computed
+    // from shared memory instead of a second, latency-bound pass over global.
     if (t == 0) {
-        ptx::mbar_arrive_expect_tx(ld_bar, nt * 4 * kTile);
+        ptx::mbar_arrive_expect_tx(ld_bar, nt * 5 * kTile);
         for (int x = 0; x < nt; x++) {
             const int y = row0 + x * kBT;
             ptx::tma_load_2d(sQ + x * kTile, &tqkv, ld_bar, h * kDh, y);
             ptx::tma_load_2d(sK + x * kTile, &tqkv, ld_bar, D + h * kDh, y);
             ptx::tma_load_2d(sV + x * kTile, &tqkv, ld_bar, 2 * D + h * kDh, y);
             ptx::tma_load_2d(sO + x * kTile, &tdo, ld_bar, h * kDh, y);
+            ptx::tma_load_2d(sP + x * kTile, &tctx, ld_bar, h * kDh, y);
         }
     }
-    // lse and rowdot(dO, O) of every query, while the tiles load
+    bool ok = true;
     {
         const int q = t;
-        float L = 0.f, dd = 0.f;
-        if (q < S) {
-            L = lse[((size_t)b * H + h) * S + q];
-            const uint4* go = reinterpret_cast<const uint4*>(dctx + (size_t)(row0 + q) * ld_dctx + h * kDh);
-            const uint4* oo = reinterpret_cast<const uint4*>(ctx + (size_t)(row0 + q) * ld_ctx + h * kDh);
+        const float L = q < S ? lse[((size_t)b * H + h) * S + q] : 0.f;
+        ok = ptx::mbar_wait(ld_bar, 0, err, kErrTimeoutAttn);
+        float dd = 0.f;
+        if (ok && q < S) {
+            // row q of the dO and O tiles; 16-byte granule g sits at g ^ (row % 8)
+            const int rr = q & (kBT - 1);
+            const uint8_t* go = sO + (q / kBT) * kTile + rr * 128;
+            const uint8_t* oo = sP + (q / kBT) * kTile + rr * 128;
 #pragma unroll
             for (int g = 0; g < kDh / 8; g++) {
-                uint4 a = go[g], c = oo[g];
+                const uint4 a = *reinterpret_cast<const uint4*>(go + ((g ^ (rr & 7)) << 4));
+                const uint4 c = *reinterpret_cast<const uint4*>(oo + ((g ^ (rr & 7)) << 4));
                 const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
                 const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c);
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    float2 fa = __bfloat1622float2(a2[e]), fc = __bfloat1622float2(c2[e]);
+                    const float2 fa = __bfloat1622float2(a2[e]), fc = __bfloat1622float2(c2[e]);
                     dd = fmaf(fa.x, fc.x, dd);
                     dd = fmaf(fa.y, fc.y, dd);
                 }
@@ -385,11 +397,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             dv_s[q] = dd;
         }
     }
-    __syncthreads();
+    __syncthreads();  // O has been read: the P^T buffer is free again
 
     const uint32_t aQ = ptx::smem_u32(sQ), aK = ptx::smem_u32(sK), aV = ptx::smem_u32(sV), aO = ptx::smem_u32(sO);
     const uint32_t aP = ptx::smem_u32(sP), aD = ptx::smem_u32(sD);
-    bool ok = true;
     auto mma1 = [&](int j, int i) {
 #pragma unroll
         for (int s = 0; s < kDh / 16; s++)
@@ -435,12 +446,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     };
 
     if (t == 0) {
-        ok = ptx::mbar_wait(ld_bar, 0, err, kErrTimeoutAttn);
         ptx::tc_fence_after();
         if (ok) mma1(0, 0);
         ptx::mma_commit(mma_bar);
     }
-    uint32_t mph = 0;
+    // Per step: wait for MMA1 of this step, compute P^T and dS^T in registers
+    // (the previous step's MMA2 runs meanwhile), wait for that MMA2 (it reads
+    // the P^T / dS^T buffers), store them, then issue the next step's MMA1
+    // ahead of this step's MMA2.
+    uint32_t mph = 0, oph = 0;
     const float sl2 = scale * kLog2e;
     const int steps = nt * nt;
 #pragma unroll 1
@@ -449,11 +463,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
         mph ^= 1;
         ptx::tc_fence_after();
-        if (st > 0 && i == 0) write_kv(j - 1);  // MMA2 of key tile j-1 has completed
         const int kg = j * kBT + r;
         const bool kval = kg < S;
-        uint8_t* prow = sP + half * kTile + r * 128;
-        uint8_t* drow = sD + half * kTile + r * 128;
         // both 32-column halves of S^T and dP^T in flight, one wait
         uint32_t sva[64], pva[64];
         ptx::tmem_ld32(lane_base + half * 64, sva);
@@ -463,15 +474,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         ptx::tmem_ld_wait();
         // a (key tile, query tile) pair wholly inside the sequence needs no masks
         const bool full_pair = (j + 1) * kBT <= S && (i + 1) * kBT <= S;
+        uint32_t pk[32], dk[32];  // 64 bf16 of P^T and of dS^T, packed in pairs
 #pragma unroll
-        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
-            const uint32_t* sv = sva + (c0 - half * 64);
-            const uint32_t* pv = pva + (c0 - half * 64);
+        for (int c0 = 0; c0 < 64; c0 += 32) {
+            const uint32_t* sv = sva + c0;
+            const uint32_t* pv = pva + c0;
+            const int q0 = i * kBT + half * 64 + c0;
             float p[32], ds[32];
-            // per-query lse and rowdot(dO, O), four at a time (broadcast reads)
-            const float4* l4 = reinterpret_cast<const float4*>(lse_s + i * kBT + c0);
-            const float4* d4 = reinterpret_cast<const float4*>(dv_s + i * kBT + c0);
             if (full_pair) {
+                // per-query lse and rowdot(dO, O), four at a time (broadcast reads)
+                const float4* l4 = reinterpret_cast<const float4*>(lse_s + q0);
+                const float4* d4 = reinterpret_cast<const float4*>(dv_s + q0);
 #pragma unroll
                 for (int e4 = 0; e4 < 8; e4++) {
                     const float4 L = l4[e4], Dd = d4[e4];
@@ -487,7 +500,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             } else {
 #pragma unroll
                 for (int e = 0; e < 32; e++) {
-                    const int qg = i * kBT + c0 + e;
+                    const int qg = q0 + e;
                     const bool v = kval && qg < S;
                     const float pe = v ? ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -lse_s[qg])) : 0.f;
                     p[e] = pe;
@@ -495,33 +508,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 }
             }
 #pragma unroll
-            for (int g = 0; g < 4; g++) {
-                const int gi = ((c0 & 63) >> 3) + g;
-                uint4 pk, dk;
-                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-                __nv_bfloat162* d2 = reinterpret_cast<__nv_bfloat162*>(&dk);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    p2[e] = __floats2bfloat162_rn(p[8 * g + 2 * e], p[8 * g + 2 * e + 1]);
-                    d2[e] = __floats2bfloat162_rn(ds[8 * g + 2 * e], ds[8 * g + 2 * e + 1]);
-                }
-                *reinterpret_cast<uint4*>(prow + ((gi ^ (r & 7)) << 4)) = pk;
-                *reinterpret_cast<uint4*>(drow + ((gi ^ (r & 7)) << 4)) = dk;
+            for (int e = 0; e < 16; e++) {
+                __nv_bfloat162 a = __floats2bfloat162_rn(p[2 * e], p[2 * e + 1]);
+                __nv_bfloat162 d = __floats2bfloat162_rn(ds[2 * e], ds[2 * e + 1]);
+                pk[c0 / 2 + e] = *reinterpret_cast<uint32_t*>(&a);
+                dk[c0 / 2 + e] = *reinterpret_cast<uint32_t*>(&d);
             }
+        }
+        if (st > 0) {
+            ok = ptx::mbar_wait(o_bar, oph, err, kErrTimeoutAttn) && ok;  // MMA2 of step st-1
+            oph ^= 1;
+            ptx::tc_fence_after();
+            if (i == 0) write_kv(j - 1);  // key tile j-1 is complete
+        }
+        // 64 queries = 8 granules of 16 bytes in this half's chunk, XOR-swizzled by row % 8
+        uint8_t* prow = sP + half * kTile + r * 128;
+        uint8_t* drow = sD + half * kTile + r * 128;
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            *reinterpret_cast<uint4*>(prow + ((g ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+            *reinterpret_cast<uint4*>(drow + ((g ^ (r & 7)) << 4)) =
+                make_uint4(dk[4 * g], dk[4 * g + 1], dk[4 * g + 2], dk[4 * g + 3]);
         }
         ptx::fence_proxy_async();  // generic-proxy P/dS writes -> tensor-core reads
         ptx::tc_fence_before();
         __syncthreads();
         if (t == 0) {
             ptx::tc_fence_after();
-            if (ok) {
-                mma2(j, i);
-                if (st + 1 < steps) mma1((st + 1) / nt, (st + 1) % nt);
+            if (st + 1 < steps) {
+                if (ok) mma1((st + 1) / nt, (st + 1) % nt);  // S^T/dP^T columns were read before the barrier
+                ptx::mma_commit(mma_bar);
             }
-            ptx::mma_commit(mma_bar);
+            if (ok) mma2(j, i);
+            ptx::mma_commit(o_bar);
         }
     }
-    ok = ptx::mbar_wait(mma_bar, mph, err, kErrTimeoutAttn) && ok;
+    ok = ptx::mbar_wait(o_bar, oph, err, kErrTimeoutAttn) && ok;
     ptx::tc_fence_after();
     write_kv(nt - 1);
     // dQ_i: warps of the first half write columns [0,32), the second [32,64)
@@ -605,9 +628,10 @@ bool attention_tc_bwd_supported(const AttnArgs& a) {
 }
 
 int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err) {
-    CUtensorMap mq, mo;
+    CUtensorMap mq, mo, mc;
     const long long rows = (long long)a.B * a.S;
-    if (!bf16_tmap(&mq, a.qkv, 3LL * a.D, rows, a.ld_qkv) || !bf16_tmap(&mo, a.dctx, a.D, rows, a.ld_dctx))
+    if (!bf16_tmap(&mq, a.qkv, 3LL * a.D, rows, a.ld_qkv) || !bf16_tmap(&mo, a.dctx, a.D, rows, a.ld_dctx) ||
+        !bf16_tmap(&mc, a.ctx, a.D, rows, a.ld_ctx))
         return -2;
     static bool attr = false;
     if (!attr) {
@@ -616,7 +640,7 @@ int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err) {
     }
     dim3 grid(a.H, a.B);
     attn_tc_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(
-        mq, mo, a.S, a.H, a.D, a.scale, reinterpret_cast<const __nv_bfloat16*>(a.ctx), a.ld_ctx,
+        mq, mo, mc, a.S, a.H, a.D, a.scale, reinterpret_cast<const __nv_bfloat16*>(a.ctx), a.ld_ctx,
         reinterpret_cast<const __nv_bfloat16*>(a.dctx), a.ld_dctx, a.lse, reinterpret_cast<__nv_bfloat16*>(a.dqkv),
         a.ld_dqkv, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -5;
