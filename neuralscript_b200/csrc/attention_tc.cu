@@ -308,7 +308,7 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const uint32_t
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_tc_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
-                       const __grid_constant__ CUtensorMap tctx, int S,
+                       const __grid_constant__ CUtensorMap tctx, const __grid_constant__ CUtensorMap tdqkv, int S,
                        int H, int D, float scale, const __nv_bfloat16* __restrict__ ctx, long long ld_ctx,
                        const __nv_bfloat16* __restrict__ dctx, long long ld_dctx, const float* __restrict__ lse,
                        __nv_bfloat16* __restrict__ dqkv, long long ld_dqkv, int* err) {
@@ -546,15 +546,66 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     ok = ptx::mbar_wait(o_bar, oph, err, kErrTimeoutAttn) && ok;
     ptx::tc_fence_after();
-    write_kv(nt - 1);
-    // dQ_i: warps of the first half write columns [0,32), the second [32,64)
+    // Final dK/dV tile and the dQ tiles. A tile that lies wholly inside the
+    // sequence is staged (bf16, 128-byte swizzle) in the P^T / dS^T buffers,
+    // free now, and written by TMA stores; a ragged tile is written row by
+    // row (a 128-row box would run into the next sequence's rows).
+    const int jl = nt - 1;
+    if ((jl + 1) * kBT <= S) {
+        uint32_t v[64];
+        ptx::tmem_ld32(lane_base + 256 + half * 64, v);
+        ptx::tmem_ld32(lane_base + 256 + half * 64 + 32, v + 32);
+        ptx::tmem_ld_wait();
+        const float mul = half == 0 ? 1.f : scale;  // dV | dK
+        uint8_t* row = sP + half * kTile + r * 128;
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            uint4 pk;
+            __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                h2[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * e]) * mul,
+                                              __uint_as_float(v[8 * g + 2 * e + 1]) * mul);
+            *reinterpret_cast<uint4*>(row + ((g ^ (r & 7)) << 4)) = pk;
+        }
+    } else {
+        write_kv(jl);
+    }
 #pragma unroll 1
     for (int i = 0; i < nt; i++) {
         uint32_t v[32];
         ptx::tmem_ld32(lane_base + 384 + 64 * i + half * 32, v);
         ptx::tmem_ld_wait();
         const int qg = i * kBT + r;
-        if (ok && qg < S) store_bf16x32(dqkv + (size_t)(row0 + qg) * ld_dqkv + h * kDh + half * 32, v, scale);
+        if ((i + 1) * kBT <= S) {
+            // dQ_i: warps of the first half hold columns [0,32), the second [32,64)
+            uint8_t* row = sD + i * kTile + r * 128;
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                uint4 pk;
+                __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    h2[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * e]) * scale,
+                                                  __uint_as_float(v[8 * g + 2 * e + 1]) * scale);
+                const int gi = half * 4 + g;
+                *reinterpret_cast<uint4*>(row + ((gi ^ (r & 7)) << 4)) = pk;
+            }
+        } else if (ok && qg < S) {
+            store_bf16x32(dqkv + (size_t)(row0 + qg) * ld_dqkv + h * kDh + half * 32, v, scale);
+        }
+    }
+    ptx::fence_proxy_async();  // staged tiles -> TMA (async proxy) reads
+    __syncthreads();
+    if (t == 0 && ok) {
+        if ((jl + 1) * kBT <= S) {
+            ptx::tma_store_2d(&tdqkv, sP, 2 * D + h * kDh, row0 + jl * kBT);          // dV
+            ptx::tma_store_2d(&tdqkv, sP + kTile, D + h * kDh, row0 + jl * kBT);      // dK
+        }
+        for (int i = 0; i < nt; i++)
+            if ((i + 1) * kBT <= S) ptx::tma_store_2d(&tdqkv, sD + i * kTile, h * kDh, row0 + i * kBT);  // dQ
+        ptx::bulk_commit();
+        ptx::bulk_wait_all();  // the staging buffers must outlive the stores
     }
     ptx::tc_fence_before();
     __syncthreads();
@@ -628,10 +679,10 @@ bool attention_tc_bwd_supported(const AttnArgs& a) {
 }
 
 int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err) {
-    CUtensorMap mq, mo, mc;
+    CUtensorMap mq, mo, mc, md;
     const long long rows = (long long)a.B * a.S;
     if (!bf16_tmap(&mq, a.qkv, 3LL * a.D, rows, a.ld_qkv) || !bf16_tmap(&mo, a.dctx, a.D, rows, a.ld_dctx) ||
-        !bf16_tmap(&mc, a.ctx, a.D, rows, a.ld_ctx))
+        !bf16_tmap(&mc, a.ctx, a.D, rows, a.ld_ctx) || !bf16_tmap(&md, a.dqkv, 3LL * a.D, rows, a.ld_dqkv))
         return -2;
     static bool attr = false;
     if (!attr) {
@@ -640,7 +691,7 @@ int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err) {
     }
     dim3 grid(a.H, a.B);
     attn_tc_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(
-        mq, mo, mc, a.S, a.H, a.D, a.scale, reinterpret_cast<const __nv_bfloat16*>(a.ctx), a.ld_ctx,
+        mq, mo, mc, md, a.S, a.H, a.D, a.scale, reinterpret_cast<const __nv_bfloat16*>(a.ctx), a.ld_ctx,
         reinterpret_cast<const __nv_bfloat16*>(a.dctx), a.ld_dctx, a.lse, reinterpret_cast<__nv_bfloat16*>(a.dqkv),
         a.ld_dqkv, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -5;
