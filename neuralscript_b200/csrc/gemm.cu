@@ -495,9 +495,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // also conflict-free for the row-per-thread writes
         uint8_t* stg = staging + (warp - 2) * 4096;
         int sbuf = 0;
+        // bf16 boxes (2 KB) alternate between the two halves of the warp's
+        // 4 KB buffer; an fp32 box (32 rows x 128 B, 128-byte swizzle: granule
+        // j of row r at j ^ (r & 7)) takes the whole buffer, so it waits for
+        // every earlier box, and the box after it waits for it
+        bool last_full = false;
         auto stage_store = [&](const CUtensorMap* map, const uint4* g4, int x, int y) {
             uint8_t* buf = stg + sbuf * 2048;
-            if (lane == 0) ptx::bulk_wait_read1();
+            if (lane == 0) {
+                if (last_full) ptx::bulk_wait_read0();
+                else ptx::bulk_wait_read1();
+            }
             __syncwarp();
             uint8_t* rowp = buf + lane * 64;
 #pragma unroll
@@ -509,12 +517,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ptx::bulk_commit();
             }
             sbuf ^= 1;
+            last_full = false;
         };
-        // boxes that start at or beyond N are not issued (the first one of a
-        // chunk always starts inside: col0 < N)
         auto out_f32 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
-            stage_store(map, reinterpret_cast<const uint4*>(v), col0, y);
-            if (col0 + 16 < p.N) stage_store(map, reinterpret_cast<const uint4*>(v + 16), col0 + 16, y);
+            if (lane == 0) ptx::bulk_wait_read0();
+            __syncwarp();
+            uint8_t* rowp = stg + lane * 128;
+            const uint4* g8 = reinterpret_cast<const uint4*>(v);
+#pragma unroll
+            for (int j = 0; j < 8; j++) *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = g8[j];
+            ptx::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                ptx::tma_store_2d(map, stg, col0, y);
+                ptx::bulk_commit();
+            }
+            last_full = true;
         };
         auto out_bf16 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
             uint4 g4[4];
@@ -769,19 +787,21 @@ static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner
 }
 
 // Output map for the TMA-store epilogue: row-major [rows, cols] with leading
-// dimension ld; 32-row boxes of 64 bytes (16 fp32 or 32 bf16), 64-byte swizzle.
+// dimension ld; 32 x 32 boxes (fp32: 128-byte rows, 128-byte swizzle; bf16:
+// 64-byte rows, 64-byte swizzle).
 static bool make_out_map(CUtensorMap* m, const void* ptr, int dtype, long long cols, long long rows, long long ld) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
     const int es = dtype == kBF16 ? 2 : 4;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
-    cuuint32_t box[2] = {(cuuint32_t)(64 / es), 32};
+    (void)es;
+    cuuint32_t box[2] = {32, 32};
     cuuint32_t estr[2] = {1, 1};
     return enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+               dtype == kBF16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static bool operand_tc_ok(const GemmOperand& o) {
