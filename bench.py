@@ -171,6 +171,81 @@ def ref_lib_path():
     return p if os.path.exists(p) else None
 
 
+def ref_abi_rows_per_s(name, w, rows, in_cols, out_cols):
+    """Reference CPU emit (oracle/_ref/libref_<name>.so) through its own
+    ns_eval_infer on `rows` rows, one core: rows/s."""
+    import ctypes as C
+    from neuralscript_b200 import synth
+    p = os.path.join(ROOT, "oracle", "_ref", f"libref_{name}.so")
+    if not os.path.exists(p):
+        return None
+    L = C.CDLL(p)
+    L.ns_runtime_init.restype = C.c_void_p
+    L.ns_runtime_init.argtypes = [C.c_void_p, C.c_size_t]
+    L.ns_eval_infer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]
+    L.ns_free.argtypes = [C.c_void_p]
+    w = np.ascontiguousarray(w, np.float32)
+    m = L.ns_runtime_init(w.ctypes.data, w.size)
+    x = synth.uniform(rows * in_cols, 9001, -1.0, 1.0)
+    out = np.empty(rows * out_cols, np.float32)
+    t0 = time.perf_counter()
+    L.ns_eval_infer(m, x.ctypes.data, out.ctypes.data, x.size)
+    dt = time.perf_counter() - t0
+    L.ns_free(m)
+    return {"value": rows / dt, "unit": "rows/s", "cores": 1, "kind": "reference",
+            "sample": f"{rows} rows through the reference CPU emit's ns_eval_infer (libref_{name}.so), 1 core"}
+
+
+def _oracle():
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib
+    return oracle_lib
+
+
+def oracle_moe_tokens_per_s(w, tokens):
+    """C oracle (the reference CPU emit's MoE helpers restated) on `tokens`
+    tokens of the config-3 layer: forward plus the four gradient helpers,
+    each recomputing routing and the expert FFN as the reference's do."""
+    O = _oracle()
+    D, E, H = 1024, 8, 1024
+    Wg = w[:D * E].reshape(D, E)
+    We1 = w[D * E:D * E + E * D * H].reshape(E, D * H)
+    We2 = w[D * E + E * D * H:].reshape(E, H * D)
+    x = _randn(tokens * D, 9001, 1.0).reshape(tokens, D)
+    dy = _randn(tokens * D, 9002, 1.0).reshape(tokens, D)
+    t0 = time.perf_counter()
+    O.moe_fwd(x, Wg, We1, We2, H)
+    O.moe_grads(dy, x, Wg, We1, We2, H)
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{tokens} tokens: forward + grad_x/wg/we1/we2 of the C restatement of the reference "
+                      "CPU emit's MoE helpers, 1 core"}
+
+
+def oracle_mlp_rows_per_s(rows_step):
+    """C oracle on a bounded sample of the config-5 step, scaled to one
+    step of `rows_step` rows: one 4096^2 layer's forward, input and weight
+    gradient at 16 rows (x 8 layers, x rows_step/16), plus Newton-Schulz-5
+    on a 512^2 matrix scaled by (4096/512)^3 (x 8 matrices)."""
+    O = _oracle()
+    n, r = 4096, 16
+    Wm = _randn(n * n, 9003, 1.0 / 64).reshape(n, n)
+    x = _randn(r * n, 9004, 1.0).reshape(r, n)
+    t0 = time.perf_counter()
+    y = O.matmul(x, Wm)
+    O.matmul_grad_a(y, Wm)
+    O.matmul_grad_w(x, y)
+    t_layer = time.perf_counter() - t0
+    G = _randn(512 * 512, 9005, 1.0).reshape(512, 512)
+    t0 = time.perf_counter()
+    O.newton_schulz5(G, 5)
+    t_ns = (time.perf_counter() - t0) * (n // 512) ** 3
+    step = 8 * t_layer * rows_step / r + 8 * t_ns
+    return {"value": rows_step / step, "unit": "rows/s", "cores": 1, "kind": "port",
+            "sample": f"C restatement, 1 core: one 4096^2 layer fwd + grad_a + grad_w at {r} rows and one "
+                      f"Newton-Schulz-5 at 512^2, scaled to 8 layers x {rows_step} rows and 8 matrices of 4096^2"}
+
+
 class RefPool:
     """Reference CPU emit for config 2 on `workers` processes (the emitted
     code is single-threaded and keeps file-scope buffers, so parallelism is
@@ -206,10 +281,48 @@ class RefPool:
             self.pool.join()
 
 
+REF_METRICS = {"c1": "rows_per_s_ns_eval_infer_c1", "c3": "tokens_per_s_moe_train_step_c3",
+               "c4": "tokens_per_s_ns_runtime_train_step_c4", "c5": "rows_per_s_muon_train_step_c5"}
+
+
+def run_reference_other(args):
+    """Configs 1, 3 and 5: the bounded single-core CPU sample of the B200
+    arm's cpu_baseline (reference emit for c1, the C restatement for c3/c5)."""
+    from neuralscript_b200 import synth
+    from neuralscript_b200.spec import CONFIGS, parse
+    cfg = args.config
+    if cfg == "c4":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference CPU emit cannot train the config-4 "
+                          "residual block (its + has no backward); config 2 is the reference arm"}))
+        return 0
+    s = parse(CONFIGS[cfg])
+    if cfg == "c1":
+        w = np.concatenate([synth.normal(c, 311 + i, 0.0, float(r) ** -0.5)
+                            for i, (_, _, c, (r, _)) in enumerate(s.layout())])
+        cpu = ref_abi_rows_per_s("c1", w, 128, 784, 10)
+    elif cfg == "c3":
+        w = np.concatenate([_randn(c, 311 + i, 0.02 if i == 0 else 1.0 / 32) for i, (_, _, c, _) in enumerate(s.layout())])
+        cpu = oracle_moe_tokens_per_s(w, 64)
+    else:
+        cpu = oracle_mlp_rows_per_s(8192)
+    if cpu is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
+        return 0
+    v, unit = cpu["value"], cpu["unit"]
+    print(json.dumps({"impl": "reference", "metric": REF_METRICS[cfg], "value": v, "unit": unit, "n_gpus": 1,
+                      "steps": 1, "warmup": 0, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": cpu["sample"]}, "cpu_baseline": cpu,
+                      "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+    return 0
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
+    if args.config != "c2":
+        return run_reference_other(args)
     metric, unit = "tokens_per_s_ns_eval_infer_c2", "tokens/s"
     if ref_lib_path() is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
@@ -267,9 +380,17 @@ def region_work(spec, label, M, train, world=1):
     try:
         l = s.layer(lname)
     except KeyError:
+        if label == "loss" and s.loss == "mse":
+            # fp32 predictions and targets read, fp32 seed gradient written
+            from neuralscript_b200.spec import out_cols
+            return "bytes", M * out_cols(s) * (4 + 4 + (4 if train else 0))
         if label == "loss":
             # fp32 logits read; training also writes the bf16 seed gradient
             return "bytes", M * 8192 * (4 + (2 if train else 0))
+        if label == "optimizer" and s.optimizer == "muon":
+            # Newton-Schulz-5 on every matrix: 5 iterations x 3 GEMMs x 2 n^3
+            return "flops", sum(5 * 3 * 2.0 * r * c * min(r, c) for _, _, _, (r, c) in s.layout()
+                                if min(r, c) >= 8)
         if label == "optimizer":
             # data parallel: the first layer's weights are updated separately (optimizer.last)
             n = s.weight_count - (s.layout()[0][2] if world > 1 else 0)
@@ -280,9 +401,25 @@ def region_work(spec, label, M, train, world=1):
         return None, 0
     k = l.kind
     bwd = phase == "bwd"
+    # a layer reading the network input computes no input gradient
+    first = any(o.fn == lname and o.args and o.args[0] == "x" for o in s.ops)
     if k == "dense":
         f = 2.0 * M * l.i("in") * l.i("out")
-        return "flops", 2 * f if bwd else f
+        return "flops", (f if first else 2 * f) if bwd else f
+    if k == "moe":
+        D, E, F = l.i("dim"), l.i("experts"), l.i("ffn", 4 * l.i("dim"))
+        router = 2.0 * M * D * E
+        experts = ((6.0 if first else 8.0) if bwd else 4.0) * M * D * F
+        if part == "route":
+            # fp32 x read by the router; bf16 rows gathered into expert order
+            return "bytes", M * D * (4 + 2 + 2)
+        if part == "experts":
+            # fwd: GELU(x We1) We2; bwd: dpre2, dWe2, dWe1 (+ dX unless fed by the input)
+            return "flops", experts
+        if part == "gate":
+            # dWg = x^T dg: fp32 x read once
+            return "bytes", M * D * 4
+        return "flops", router + experts
     if k == "attention":
         D, S = l.i("dim"), l.i("seq", 0) or M
         if bwd:
@@ -299,50 +436,161 @@ def region_work(spec, label, M, train, world=1):
     return None, 0
 
 
+def _randn(n, seed, sd):
+    """Seeded N(0, sd^2) host array (torch's CPU generator: fast at the
+    tens-of-millions sizes of configs 3 and 5)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(n, generator=g) * sd).numpy()
+
+
+def setup_workload(args, rank, world, dist):
+    """Model, device inputs, the timed step and the end-to-end call of one
+    benchmark configuration (synthetic, seeded)."""
+    import torch
+    import neuralscript_b200 as nsb
+    from neuralscript_b200 import synth
+    from neuralscript_b200.spec import CONFIGS, parse
+    from types import SimpleNamespace as NS
+
+    cfg = args.config
+    spec = CONFIGS[cfg]
+    W = NS(cfg=cfg, seq_len=None, labels_kind=None, cpu=None)
+    if cfg in ("c2", "c4"):
+        s = parse(spec)
+        w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
+    elif cfg == "c1":
+        # N(0, 1/fan_in) weights (sd = fan_in^-1/2), no biases, dropout off
+        s = parse(spec)
+        w = np.concatenate([synth.normal(c, 311 + i, 0.0, float(r) ** -0.5)
+                            for i, (_, _, c, (r, _)) in enumerate(s.layout())])
+    elif cfg == "c3":
+        # the MoE layer trained on MSE against N(0,1) targets: forward, dWg,
+        # dWe1, dWe2 (the input gradient of the network input is not formed)
+        spec = spec + "loss mse\noptimizer adamw\n"
+        s = parse(spec)
+        w = np.concatenate([_randn(c, 311 + i, 0.02 if i == 0 else 1.0 / 32)
+                            for i, (_, _, c, _) in enumerate(s.layout())])
+    else:  # c5: fp32 master weights N(0, (1/64)^2), Muon NS-5, MSE
+        s = parse(spec)
+        w = np.concatenate([_randn(c, 311 + i, 1.0 / 64) for i, (_, _, c, _) in enumerate(s.layout())])
+    model = nsb.Model(spec, w, precision=args.precision)
+    W.spec, W.model = spec, model
+    train = cfg in ("c3", "c4", "c5")
+    W.train = train
+    if train and world > 1:
+        uid = nsb.dist_unique_id() if rank == 0 else bytes(128)
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        model.dist_init(rank, world, obj[0], 120000)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    if cfg in ("c2", "c4"):
+        B, S = 64, 256
+        M = B * S
+        W.seq_len = S
+        tok = torch.from_numpy(synth.tokens(M, 301 + 7919 * rank, 8192)).cuda()
+        tok_h = tok.cpu().pin_memory().numpy()
+        if cfg == "c4":
+            tgt = torch.from_numpy(synth.tokens(M, 401 + 7919 * rank, 8192).astype(np.int32)).cuda()
+            labels = None
+            if args.one_hot:
+                labels = torch.zeros(M, 8192, device="cuda")
+                labels[torch.arange(M), tgt.long()] = 1.0
+            W.labels_kind = "one-hot" if args.one_hot else "int32 targets"
+            W.step = lambda: model.train_step_device(tok, labels=labels, targets=None if labels is not None else tgt,
+                                                     lr=3e-4, stream=sp, want_loss=False)
+            tgt_h = tgt.cpu().pin_memory().numpy()
+            y1h = None
+            if args.e2e_one_hot:
+                y1h = torch.zeros(M, 8192).pin_memory().numpy()
+                y1h[np.arange(M), tgt_h] = 1.0
+            W.e2e_fn = (lambda: model.train_step(tok_h, y1h, 3e-4)) if y1h is not None else \
+                (lambda: model.train_step_idx(tok_h, tgt_h, 3e-4))
+            W.h2d = tok_h.nbytes + (y1h.nbytes if y1h is not None else tgt_h.nbytes)
+            W.d2h = 4
+            W.metric = "tokens_per_s_ns_runtime_train_step_c4"
+            W.workload = "config 4 AOT train step (c2 block + 512->8192 head, CE, AdamW, cosine)"
+            W.flops_per_row = c4_flops_per_token()
+        else:
+            out = torch.empty(M, 512, device="cuda")
+            W.step = lambda: model.infer_device(tok, out, stream=sp)
+            out_h = torch.empty(M * 512, dtype=torch.float32).pin_memory().numpy()
+            W.e2e_fn = lambda: model.infer(tok_h, out_h)
+            W.h2d, W.d2h = tok_h.nbytes, M * 512 * 4
+            W.metric = "tokens_per_s_ns_eval_infer_c2"
+            W.workload = "config 2 transformer block forward (ns_eval_infer)"
+            W.flops_per_row = c2_flops_per_token()
+            if args.cpu_baseline and rank == 0 and ref_lib_path():
+                def cpu():
+                    pool = RefPool(1)
+                    v, _ = pool.step(8, 9001)
+                    return None if v is None else {
+                        "value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                        "sample": "8 sequences x 256 tokens through the reference CPU emit (libref_c2.so), 1 core"}
+                W.cpu = cpu
+        W.M, W.global_batch = M, B * world
+        return W
+
+    if cfg == "c1":
+        M, cols, outc = 4096, 784, 10
+        x = torch.from_numpy(synth.uniform(M * cols, 101 + 7919 * rank, -1.0, 1.0)).cuda()
+        out = torch.empty(M, outc, device="cuda")
+        W.step = lambda: model.infer_device(x, out, stream=sp)
+        x_h = x.cpu().pin_memory().numpy()
+        out_h = torch.empty(M * outc, dtype=torch.float32).pin_memory().numpy()
+        W.e2e_fn = lambda: model.infer(x_h, out_h)
+        W.h2d, W.d2h = x_h.nbytes, M * outc * 4
+        W.metric = "rows_per_s_ns_eval_infer_c1"
+        W.workload = "config 1 MLP 784-1024-1024-10 ReLU forward (ns_eval_infer), batch 4096"
+        W.flops_per_row = 2 * (784 * 1024 + 1024 * 1024 + 1024 * 10)
+        if args.cpu_baseline and rank == 0:
+            W.cpu = lambda: ref_abi_rows_per_s("c1", w, 128, 784, 10)
+    else:
+        M, cols = (65536, 1024) if cfg == "c3" else (8192, 4096)
+        g = torch.Generator(device="cuda").manual_seed(501 + 7919 * rank)
+        x = torch.randn(M, cols, device="cuda", generator=g)
+        y = torch.randn(M, cols, device="cuda", generator=g)
+        W.step = lambda: model.train_step_device(x, labels=y, lr=1e-4, stream=sp, want_loss=False)
+        x_h, y_h = x.cpu().pin_memory().numpy(), y.cpu().pin_memory().numpy()
+        W.e2e_fn = lambda: model.train_step(x_h, y_h, 1e-4)
+        W.h2d, W.d2h = x_h.nbytes + y_h.nbytes, 4
+        W.labels_kind = "fp32 N(0,1) targets (MSE)"
+        if cfg == "c3":
+            D, E, F = 1024, 8, 1024
+            W.metric = "tokens_per_s_moe_train_step_c3"
+            W.workload = ("config 3 top-1 MoE layer (D 1024, 8 experts, FFN 1024) forward + backward "
+                          "(dWg, dWe1, dWe2) + AdamW, MSE against N(0,1) targets")
+            W.flops_per_row = 2 * D * E * 2 + 10 * D * F
+            if args.cpu_baseline and rank == 0:
+                W.cpu = lambda: oracle_moe_tokens_per_s(w, 64)
+        else:
+            n = 4096
+            W.metric = "rows_per_s_muon_train_step_c5"
+            W.workload = ("config 5 deep MLP 8 x 4096^2 ReLU, MSE, Muon (momentum 0.95, Newton-Schulz-5), "
+                          "8192 rows per GPU")
+            W.flops_per_row = 2 * n * n * (8 + 15) + 8 * 5 * 3 * 2.0 * n ** 3 / M
+            if args.cpu_baseline and rank == 0:
+                W.cpu = lambda: oracle_mlp_rows_per_s(M)
+    W.M, W.global_batch = M, M * world
+    return W
+
+
 def run_b200(args):
     import torch
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
-    import neuralscript_b200 as nsb
-    from neuralscript_b200 import synth
-    from neuralscript_b200.spec import CONFIGS, parse
-
+    dist = None
     if world > 1:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    cfg = args.config
-    spec = CONFIGS[cfg]
-    s = parse(spec)
-    w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
-    model = nsb.Model(spec, w, precision=args.precision)
-    B, S = 64, 256
-    M = B * S
-    tok = torch.from_numpy(synth.tokens(M, 301 + 7919 * rank, 8192)).cuda()
-    train = cfg == "c4"
-    if train:
-        if world > 1:
-            uid = nsb.dist_unique_id() if rank == 0 else bytes(128)
-            obj = [uid]
-            dist.broadcast_object_list(obj, src=0)
-            model.dist_init(rank, world, obj[0], 120000)
-        tgt = torch.from_numpy(synth.tokens(M, 401 + 7919 * rank, 8192).astype(np.int32)).cuda()
-        labels = None
-        if args.one_hot:
-            labels = torch.zeros(M, 8192, device="cuda")
-            labels[torch.arange(M), tgt.long()] = 1.0
-    out = torch.empty(M, s.out_cols if hasattr(s, "out_cols") else 512, device="cuda")
+    W = setup_workload(args, rank, world, dist)
+    model, spec, M, train, step = W.model, W.spec, W.M, W.train, W.step
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-
-    def step():
-        if train:
-            model.train_step_device(tok, labels=labels, targets=None if labels is not None else tgt, lr=3e-4,
-                                    stream=sp, want_loss=False)
-        else:
-            model.infer_device(tok, out, stream=sp)
 
     for _ in range(args.warmup):
         step()
@@ -370,25 +618,11 @@ def run_b200(args):
     ms_step = ms / args.steps
     tokens_step = M * world
     value = tokens_step / (ms_step / 1e3)
+    unit = W.metric.split("_per_s")[0] + "/s"
 
     # end to end through the reference-facing ABI with host buffers
-    # host buffers are page-locked, as a serving caller would hold them
-    tok_h = tok.cpu().pin_memory().numpy()
-    if train:
-        tgt_h = tgt.cpu().pin_memory().numpy()
-        y1h = None
-        if args.e2e_one_hot:
-            y1h = torch.zeros(M, 8192).pin_memory().numpy()
-            y1h[np.arange(M), tgt_h] = 1.0
-        e2e_fn = (lambda: model.train_step(tok_h, y1h, 3e-4)) if y1h is not None else \
-            (lambda: model.train_step_idx(tok_h, tgt_h, 3e-4))
-        h2d = tok_h.nbytes + (y1h.nbytes if y1h is not None else tgt_h.nbytes)
-        d2h = 4
-    else:
-        out_h = torch.empty(M * 512, dtype=torch.float32).pin_memory().numpy()
-        e2e_fn = lambda: model.infer(tok_h, out_h)
-        h2d = tok_h.nbytes
-        d2h = M * 512 * 4
+    # (page-locked, as a serving caller would hold them)
+    e2e_fn = W.e2e_fn
     for _ in range(2):
         e2e_fn()
     if world > 1:
@@ -402,8 +636,8 @@ def run_b200(args):
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": tokens_step / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
-           "d2h_bytes_per_step": int(d2h)}
+    e2e = {"value": tokens_step / e2e_s, "unit": unit, "h2d_bytes_per_step": int(W.h2d),
+           "d2h_bytes_per_step": int(W.d2h)}
 
     # per-region device time inside the engine (CUDA events on the engine
     # stream) over the same number of steps; the dominant region's kernel is
@@ -433,11 +667,11 @@ def run_b200(args):
             continue
         t = tot_ms / n / 1e3
         if kind == "flops":
-            ach, peak, unit, bound = work / t / 1e12, pk["bf16_tflops"], "TFLOP/s", "tensor"
+            ach, peak, kunit, bound = work / t / 1e12, pk["bf16_tflops"], "TFLOP/s", "tensor"
         else:
-            ach, peak, unit, bound = work / t / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
+            ach, peak, kunit, bound = work / t / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
         kernels.append({"region": label, "us": t * 1e6, "bound": bound, "achieved": ach, "peak": peak,
-                        "unit": unit, "frac": ach / peak, "work": work})
+                        "unit": kunit, "frac": ach / peak, "work": work})
     kernels.sort(key=lambda k: -k["us"])
     roof = None
     ranked = [k for k in kernels if k["frac"] is not None]
@@ -453,23 +687,16 @@ def run_b200(args):
 
     result = None
     if rank == 0:
-        cpu = None
-        if args.cpu_baseline and not train and ref_lib_path():
-            pool = RefPool(1)
-            v, _ = pool.step(8, 9001)
-            if v is not None:
-                cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
-                       "sample": "8 sequences x 256 tokens through the reference CPU emit (libref_c2.so), 1 core"}
-        fl = c4_flops_per_token() if train else c2_flops_per_token()
+        cpu = W.cpu() if (W.cpu and world == 1) else None
+        fl = W.flops_per_row
         result = {
-            "metric": "tokens_per_s_ns_runtime_train_step_c4" if train else "tokens_per_s_ns_eval_infer_c2",
-            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "metric": W.metric,
+            "value": value, "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": args.precision, "data": "synthetic",
-            "config": {"workload": ("config 4 AOT train step (c2 block + 512->8192 head, CE, AdamW, cosine)"
-                                    if train else "config 2 transformer block forward (ns_eval_infer)"),
-                       "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
-                       "labels": ("one-hot" if args.one_hot else "int32 targets") if train else None,
+            "config": {"workload": W.workload,
+                       "global_batch": W.global_batch, "seq_len": W.seq_len, "parallelism": f"dp{world}",
+                       "labels": W.labels_kind,
                        "l2": "flushed between steps (512 MB write outside timing)"},
             "model_tflops": fl * value / 1e12,
             "step_frac_of_bf16_peak": fl * value / world / 1e12 / pk["bf16_tflops"],
@@ -492,7 +719,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c4"])
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
     ap.add_argument("--one-hot", action="store_true", help="c4: dense one-hot labels on the device path")
     ap.add_argument("--e2e-one-hot", action="store_true", help="c4: e2e through the one-hot ABI")

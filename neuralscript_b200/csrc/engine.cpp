@@ -504,6 +504,9 @@ static void region_end(ns_model* m, int idx) {
     cudaEventRecord(m->regions[idx].pending.back().second, m->stream);
 }
 
+int nsb::region_open(ns_model* m, const std::string& label) { return region_begin(m, label); }
+void nsb::region_close(ns_model* m, int idx) { region_end(m, idx); }
+
 // A host-measured interval (e.g. time spent waiting on NCCL), folded into the
 // same per-region totals.
 static void host_region_add(ns_model* m, const char* label, double ms) {
@@ -1122,6 +1125,7 @@ struct AdamTensorLocal {
 };
 
 static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* out);
+static size_t ns_scratch_floats(size_t mat, size_t gram);
 
 // Optimizer update of all weights, or of those marked in `sel`.
 static int optimizer_step(ns_model* m, float lr, const std::vector<char>* sel) {
@@ -1197,64 +1201,109 @@ static int optimizer_step(ns_model* m, float lr, const std::vector<char>* sel) {
     return refresh_working(m, &fresh);
 }
 
-// X (r x c, fp32) -> out = NS5(X / ||X||). Uses m->d_ns as scratch.
+// Scratch floats newton_schulz needs for a matrix of `mat` elements whose
+// Gram matrix has `gram` elements (every sub-buffer 256-byte aligned).
+static size_t ns_round(size_t x) { return (x + 63) & ~(size_t)63; }
+static size_t ns_scratch_floats(size_t mat, size_t gram) {
+    // fp32: Gram A, polynomial B, two iterates, norm partials;
+    // bf16 operand copies: two iterates, A and B (half a float each)
+    return 2 * ns_round(gram) + 2 * ns_round(mat) + 1024 + ns_round(mat) + ns_round(gram);
+}
+
+// X (r x c, fp32) -> out = NS5(X / ||X||), the quintic Newton-Schulz
+// iteration Y' = a Y + (b A + c A^2) Y with A = Y Y^T (Y^T Y when r > c).
+// Uses m->d_ns as scratch. In bf16 mode the three GEMMs of an iteration
+// take bf16 operands (fp32 accumulation; the a Y and b A terms are added in
+// fp32 from fp32 copies), as Muon's orthogonalisation is usually run;
+// otherwise they run on fp32 operands (TF32 tensor cores, or the SIMT
+// kernel in the fp32 parity mode).
 static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* out) {
     const bool tr = r > c;
     const int R = tr ? c : r;  // Gram size
+    const size_t gram = ns_round((size_t)R * R), mat = ns_round((size_t)r * c);
     float* A = m->d_ns;
-    float* B = A + (size_t)R * R;
-    float* Y0 = B + (size_t)R * R;
-    float* Y1 = Y0 + (size_t)r * c;
-    float* part = Y1 + (size_t)r * c;
+    float* B = A + gram;
+    float* Y0 = B + gram;
+    float* Y1 = Y0 + mat;
+    float* part = Y1 + mat;
+    const bool h = m->wdt == kBF16;
+    __nv_bfloat16* Y0h = reinterpret_cast<__nv_bfloat16*>(part + 1024);
+    __nv_bfloat16* Y1h = Y0h + mat;
+    __nv_bfloat16* Ah = Y1h + mat;
+    __nv_bfloat16* Bh = Ah + gram;
+    const int dt = h ? kBF16 : kF32;
     launch_counter() += 2;
     frob_normalize(X, (long long)r * c, 1e-7f, Y0, part, m->stream);
+    if (h) {
+        launch_counter() += 1;
+        if (act_fwd_f32(Y0, (size_t)r * c, kIdentity, nullptr, Y0h, m->stream)) return fail("bf16 copy failed");
+    }
     const float a = 3.4445f, b = -4.7750f, cc = 2.0315f;
     float* cur = Y0;
     float* nxt = Y1;
+    __nv_bfloat16* curh = Y0h;
+    __nv_bfloat16* nxth = Y1h;
     for (int it = 0; it < steps; it++) {
+        const bool last = it + 1 == steps;
+        const void* Yop = h ? (const void*)curh : (const void*)cur;
         GemmDesc g1;  // A = Y Y^T  (or Y^T Y)
         g1.M = R;
         g1.N = R;
         g1.K = tr ? r : c;
-        g1.a = opnd(cur, kF32, c, tr);
-        g1.b = opnd(cur, kF32, c, tr);
+        g1.a = opnd(Yop, dt, c, tr);
+        g1.b = opnd(Yop, dt, c, tr);
         g1.ep.c32 = A;
         g1.ep.ld_c32 = R;
+        if (h) {
+            g1.ep.c16 = Ah;
+            g1.ep.ld_c16 = R;
+        }
         if (run_gemm(m, g1)) return -1;
         GemmDesc g2;  // B = b A + c A A (A symmetric)
         g2.M = R;
         g2.N = R;
         g2.K = R;
-        g2.a = opnd(A, kF32, R, false);
-        g2.b = opnd(A, kF32, R, false);
+        g2.a = opnd(h ? (const void*)Ah : (const void*)A, dt, R, false);
+        g2.b = opnd(h ? (const void*)Ah : (const void*)A, dt, R, false);
         g2.ep.alpha = cc;
         g2.ep.add = A;
         g2.ep.ld_add = R;
         g2.ep.add_scale = b;
-        g2.ep.c32 = B;
-        g2.ep.ld_c32 = R;
+        if (h) {
+            g2.ep.c16 = Bh;
+            g2.ep.ld_c16 = R;
+        } else {
+            g2.ep.c32 = B;
+            g2.ep.ld_c32 = R;
+        }
         if (run_gemm(m, g2)) return -1;
+        const void* Bop = h ? (const void*)Bh : (const void*)B;
         GemmDesc g3;  // Y' = a Y + B Y   (or a Y + Y B)
         g3.M = r;
         g3.N = c;
         if (!tr) {
             g3.K = R;
-            g3.a = opnd(B, kF32, R, false);
-            g3.b = opnd(cur, kF32, c, true);
+            g3.a = opnd(Bop, dt, R, false);
+            g3.b = opnd(Yop, dt, c, true);
         } else {
             g3.K = R;
-            g3.a = opnd(cur, kF32, c, false);
-            g3.b = opnd(B, kF32, R, false);
+            g3.a = opnd(Yop, dt, c, false);
+            g3.b = opnd(Bop, dt, R, false);
         }
         g3.ep.add = cur;
         g3.ep.ld_add = c;
         g3.ep.add_scale = a;
-        g3.ep.c32 = nxt;
+        g3.ep.c32 = last ? out : nxt;  // the last iterate goes straight to the output
         g3.ep.ld_c32 = c;
+        if (h && !last) {
+            g3.ep.c16 = nxth;
+            g3.ep.ld_c16 = c;
+        }
         if (run_gemm(m, g3)) return -1;
         std::swap(cur, nxt);
+        std::swap(curh, nxth);
     }
-    cudaMemcpyAsync(out, cur, sizeof(float) * (size_t)r * c, cudaMemcpyDeviceToDevice, m->stream);
+    if (steps <= 0) cudaMemcpyAsync(out, cur, sizeof(float) * (size_t)r * c, cudaMemcpyDeviceToDevice, m->stream);
     return 0;
 }
 
@@ -1441,7 +1490,7 @@ ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_fl
         if (g * g > maxgram) maxgram = g * g;
     }
     ok = ok && (m->d_o = (float*)persist_alloc(sizeof(float) * (maxmat + 1)));
-    m->ns_floats = 2 * maxgram + 2 * maxmat + 1024;
+    m->ns_floats = ns_scratch_floats(maxmat, maxgram);
     if (m->spec.optimizer == "muon") ok = ok && (m->d_ns = (float*)persist_alloc(sizeof(float) * m->ns_floats));
     m->adam_t.assign(m->spec.weights.size(), 0);
     m->h_w.assign(weights, weights + n);

@@ -40,6 +40,11 @@ struct MoeScratch;
 // allocation helper bound to a model's plan (freed on re-plan / free)
 void* plan_alloc(ns_model* m, size_t bytes);
 
+// Per-region timing around part of an operation (no-op unless the model's
+// region timing is on): the index from region_open goes to region_close.
+int region_open(ns_model* m, const std::string& label);
+void region_close(ns_model* m, int idx);
+
 struct Op {
     int kind = OP_DENSE;
     int layer = -1;

@@ -73,10 +73,15 @@ __device__ __forceinline__ void epi_apply(const Epilogue& ep, int row, int col, 
 // use 16-byte loads (leading dimensions multiples of 8 elements, col0 a
 // multiple of 32).
 template <bool FAST>
-__device__ __forceinline__ void epi_pre32(const Epilogue& ep, int row, int col0, float* v, int ncols) {
+__device__ __forceinline__ void epi_pre32(const Epilogue& ep, int row, int col0, float* v, int ncols,
+                                          const float* pre_add = nullptr, const uint4* pre_dz = nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; j++) v[j] *= ep.alpha;
-    if (ep.add) {
+    if (ep.add && pre_add) {
+        // residual already loaded (full chunk)
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] += ep.add_scale * pre_add[j];
+    } else if (ep.add) {
         const float* a = ep.add + (size_t)row * ep.ld_add + col0;
         if (ncols == 32) {
 #pragma unroll
@@ -101,8 +106,9 @@ __device__ __forceinline__ void epi_pre32(const Epilogue& ep, int row, int col0,
     if (ep.dz) {
         float z[32];
         if (ncols == 32 && ep.dz_dtype == kBF16) {
-            const uint4* a = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ep.dz) +
-                                                            (size_t)row * ep.ld_dz + col0);
+            const uint4* a = pre_dz ? pre_dz
+                                    : reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ep.dz) +
+                                                                     (size_t)row * ep.ld_dz + col0);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 uint4 t = a[j];
@@ -214,6 +220,19 @@ struct TcParams {
     const int* seg_end;
     int max_m_tiles_per_group;
     int tma_out;  // outputs leave through the TMA-store epilogue (tz / tc32 / tc16)
+    int bk;       // K elements per k-block
+    // grouped, MN-major B: group g's [K, N] matrix starts at row g * K of
+    // the B tensor map (groups stacked along K)
+    int b_kgroup;
+    // grouped over K: unit -> (group, m tile, n tile), k-blocks over the
+    // group's rows [seg[g], seg_end[g]) rounded up to a k-block; C of group g
+    // at ep.c32 + g * c_group_stride
+    int group_k;
+    long long c_group_stride;
+    // static round-robin units (grid = min(units, SMs)) instead of cluster
+    // launch control; for grouped GEMMs, whose many empty units are then
+    // skipped without a scheduling round trip
+    int static_sched;
 };
 
 template <int BN, bool TF32>
@@ -245,6 +264,17 @@ __device__ __forceinline__ bool tc_decode(const TcParams& p, int u, int BN, int&
     split = u % p.splits;
     int tile = u / p.splits;
     int m_blk, n_blk;
+    if (p.group_k) {
+        const int per_group = p.m_tiles * p.n_tiles;
+        g = tile / per_group;
+        const int t = tile % per_group;
+        m0 = (t / p.n_tiles) * 128;
+        n0 = (t % p.n_tiles) * BN;
+        row_end = p.M;
+        kb0 = p.seg[g] / p.bk;
+        kb1 = (p.seg_end[g] + p.bk - 1) / p.bk;
+        return true;
+    }
     if (p.groups > 1) {
         // tile -> (group, m within group, n)
         int per_group = p.max_m_tiles_per_group * p.n_tiles;
@@ -364,14 +394,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int unit = blockIdx.x;
             while (alive) {
                 // ask for the next unit while this one's tiles load
-                ptx::mbar_arrive_expect_tx(clc_bar, 16);
-                ptx::clc_try_cancel(clc_resp, clc_bar);
-                pending = true;
+                if (!p.static_sched) {
+                    ptx::mbar_arrive_expect_tx(clc_bar, 16);
+                    ptx::clc_try_cancel(clc_resp, clc_bar);
+                    pending = true;
+                }
                 Work w;
                 if (tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end)) {
                     alive = push(unit);
                     const int m0 = w.m0;
-                    const int nb = w.g * p.N + w.n0;  // B row (grouped: groups stacked along N)
+                    // B row (row-grouped, K-major B: groups stacked along N)
+                    const int nb = (p.groups > 1 && !p.group_k && !p.b_kgroup) ? w.g * p.N + w.n0 : w.n0;
+                    const int kb_row = p.b_kgroup ? w.g * p.K : 0;  // MN-major grouped B: stacked along K
                     for (int kb = w.kb0; alive && kb < w.kb1; kb++) {
                         if (!ptx::mbar_wait(&empty[stage], phase ^ 1, p.err, kErrTimeoutProducer)) {
                             alive = false;
@@ -394,13 +428,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                             for (int c = 0; c < BN / C::CHUNK; c++)
                                 ptx::tma_load_2d(sb + c * (C::BK * 128), &tb, &full[stage], nb + c * C::CHUNK,
-                                                 kb * C::BK);
+                                                 kb_row + kb * C::BK);
                         }
                         if (++stage == C::STAGES) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
+                }
+                if (p.static_sched) {
+                    unit += gridDim.x;
+                    if (unit >= p.total_units) break;
+                    continue;
                 }
                 // the response is awaited on every path, so none is in flight at exit
                 const bool got = ptx::mbar_wait(clc_bar, clc_phase, p.err, kErrTimeoutProducer);
@@ -492,20 +531,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         constexpr bool FAST = !TF32;
         // TMA-store staging: two 2 KB buffers of 32 rows x 64 bytes, 64-byte
         // swizzle (16-byte granule j of row r at j ^ ((r >> 1) & 3)), which is
-        // also conflict-free for the row-per-thread writes
+        // also conflict-free for the row-per-thread writes. Every box (32
+        // bf16 or 16 fp32 columns) fills one buffer; the buffers alternate,
+        // so writing one overlaps the store of the other.
         uint8_t* stg = staging + (warp - 2) * 4096;
         int sbuf = 0;
-        // bf16 boxes (2 KB) alternate between the two halves of the warp's
-        // 4 KB buffer; an fp32 box (32 rows x 128 B, 128-byte swizzle: granule
-        // j of row r at j ^ (r & 7)) takes the whole buffer, so it waits for
-        // every earlier box, and the box after it waits for it
-        bool last_full = false;
         auto stage_store = [&](const CUtensorMap* map, const uint4* g4, int x, int y) {
             uint8_t* buf = stg + sbuf * 2048;
-            if (lane == 0) {
-                if (last_full) ptx::bulk_wait_read0();
-                else ptx::bulk_wait_read1();
-            }
+            if (lane == 0) ptx::bulk_wait_read1();
             __syncwarp();
             uint8_t* rowp = buf + lane * 64;
 #pragma unroll
@@ -517,22 +550,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ptx::bulk_commit();
             }
             sbuf ^= 1;
-            last_full = false;
         };
         auto out_f32 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
-            if (lane == 0) ptx::bulk_wait_read0();
-            __syncwarp();
-            uint8_t* rowp = stg + lane * 128;
             const uint4* g8 = reinterpret_cast<const uint4*>(v);
-#pragma unroll
-            for (int j = 0; j < 8; j++) *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = g8[j];
-            ptx::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-                ptx::tma_store_2d(map, stg, col0, y);
-                ptx::bulk_commit();
-            }
-            last_full = true;
+            stage_store(map, g8, col0, y);
+            if (col0 + 16 < p.N) stage_store(map, g8 + 4, col0 + 16, y);  // uniform
         };
         auto out_bf16 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
             uint4 g4[4];
@@ -544,28 +566,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             stage_store(map, g4, col0, y);
         };
-        // Finish 32 accumulator columns (col0 < N) of this thread's row.
+        // TMA-store path, after epi_pre32: the pre-activation, the
+        // activation and the outputs of 32 columns (col0 < N); rows >= M and
+        // columns >= N of a box are clipped by the store
+        auto store_tma = [&](int col0, int y, float* v) {
+            if (p.ep.z) {
+                if (p.ep.z_dtype == kBF16) out_bf16(&tz, v, col0, y);
+                else out_f32(&tz, v, col0, y);
+            }
+            epi_act32<FAST>(p.ep.act, v);
+            if (p.ep.c32) out_f32(&tc32, v, col0, y);
+            if (p.ep.c16) out_bf16(&tc16, v, col0, y);
+        };
+        // Direct-store path: finish 32 accumulator columns (col0 < N) of
+        // this thread's row.
         auto finish = [&](const Work& w, int col0, float* v) {
             const int row = w.m0 + r_in_tile;
-            const bool row_ok = row < w.row_end;
-            if (p.tma_out) {
-                // rows >= M and columns >= N of a box are clipped by the
-                // store; a 32-row slab entirely past M issues nothing
-                const int y = w.m0 + lane_grp * 32;
-                if (y >= p.M) return;
-                const int nc = col0 + 32 <= p.N ? 32 : p.N - col0;
-                if (row_ok) epi_pre32<FAST>(p.ep, row, col0, v, nc);
-                if (p.ep.z) {
-                    if (p.ep.z_dtype == kBF16) out_bf16(&tz, v, col0, y);
-                    else out_f32(&tz, v, col0, y);
+            if (row >= w.row_end) return;
+            const bool full = p.vec_ok && col0 + 32 <= p.N;
+            if (p.group_k) {
+                // per-group weight gradient: plain fp32 store
+                float* dst = p.ep.c32 + (size_t)w.g * p.c_group_stride + (size_t)row * p.ep.ld_c32 + col0;
+                if (full) {
+                    store32_f32(dst, v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (col0 + j < p.N) dst[j] = v[j];
                 }
-                epi_act32<FAST>(p.ep.act, v);
-                if (p.ep.c32) out_f32(&tc32, v, col0, y);
-                if (p.ep.c16) out_bf16(&tc16, v, col0, y);
                 return;
             }
-            if (!row_ok) return;
-            const bool full = p.vec_ok && col0 + 32 <= p.N;
             if (p.splits > 1) {
                 float* ws = p.workspace + ((size_t)w.split * p.M + row) * p.N + col0;
                 if (full) {
@@ -582,6 +612,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int j = 0; j < 32; j++)
                     if (col0 + j < p.N) epi_apply(p.ep, row, col0 + j, v[j]);
             }
+        };
+        // Epilogue operands of a full 32-column chunk of this thread's row
+        // (the fp32 residual, the bf16 activation input of act'), loaded one
+        // chunk ahead of their use (TMA-store path, vectorisable operands).
+        const bool ahead_add = p.tma_out && p.vec_ok && p.ep.add != nullptr;
+        const bool ahead_dz = p.tma_out && p.vec_ok && p.ep.dz != nullptr && p.ep.dz_dtype == kBF16;
+        float addv[32];
+        uint4 dzv[4];
+        auto load_ahead = [&](const Work& w, int col0) -> bool {
+            const int row = w.m0 + r_in_tile;
+            if (!(ahead_add || ahead_dz) || row >= w.row_end || col0 + 32 > p.N) return false;
+            if (ahead_add) {
+                const float4* a = reinterpret_cast<const float4*>(p.ep.add + (size_t)row * p.ep.ld_add + col0);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float4 t = a[j];
+                    addv[4 * j] = t.x;
+                    addv[4 * j + 1] = t.y;
+                    addv[4 * j + 2] = t.z;
+                    addv[4 * j + 3] = t.w;
+                }
+            }
+            if (ahead_dz) {
+                const uint4* a = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.ep.dz) +
+                                                                (size_t)row * p.ep.ld_dz + col0);
+#pragma unroll
+                for (int j = 0; j < 4; j++) dzv[j] = a[j];
+            }
+            return true;
         };
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -601,19 +660,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (unit < 0) break;
             tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end);
+            const int c_begin = half * HALF_COLS, c_end = (half + 1) * HALF_COLS;
+            // the first chunk's operands load while this tile's MMAs run
+            bool have = load_ahead(w, w.n0 + c_begin);
             if (!ptx::mbar_wait(&acc_full[acc], acc_phase, p.err, kErrTimeoutEpilogue)) break;
             ptx::tc_fence_after();
 #pragma unroll 1
-            for (int c = half * HALF_COLS; c < (half + 1) * HALF_COLS; c += 32) {
+            for (int c = c_begin; c < c_end; c += 32) {
                 uint32_t r[32];
                 ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + acc * BN + c, r);
                 ptx::tmem_ld_wait();
                 const int col0 = w.n0 + c;
                 if (col0 >= p.N) continue;  // uniform across the warp
                 float v[32];
+                const bool no_k = w.kb1 <= w.kb0;  // empty k range (a group with no rows): C = 0
 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-                finish(w, col0, v);
+                for (int j = 0; j < 32; j++) v[j] = no_k ? 0.f : __uint_as_float(r[j]);
+                if (p.tma_out) {
+                    const int y = w.m0 + lane_grp * 32;
+                    if (y >= p.M) continue;  // slab entirely past M: nothing to store (uniform)
+                    const int row = w.m0 + r_in_tile;
+                    const int nc = col0 + 32 <= p.N ? 32 : p.N - col0;
+                    if (row < w.row_end)
+                        epi_pre32<FAST>(p.ep, row, col0, v, nc, have && ahead_add ? addv : nullptr,
+                                        have && ahead_dz ? dzv : nullptr);
+                    // the next chunk's operands load while this chunk is stored
+                    have = c + 32 < c_end && load_ahead(w, col0 + 32);
+                    store_tma(col0, y, v);
+                } else {
+                    finish(w, col0, v);
+                }
             }
             ptx::tc_fence_before();
             ptx::mbar_arrive(&acc_empty[acc]);
@@ -680,6 +756,82 @@ struct SimtParams {
 __device__ __forceinline__ float ld_op(const GemmOperand& o, long long i, long long k) {
     size_t idx = o.mn_major ? (size_t)(k * o.ld + i) : (size_t)(i * o.ld + k);
     return ld_any(o.ptr, o.dtype, idx);
+}
+
+// Narrow outputs (N <= 32, e.g. a 10-class head) with a K-major A: each
+// warp owns kNarrowRows rows of C; lane l takes the 8 consecutive k of
+// every 256-wide k step starting at 8 l (one 16-byte load of bf16 A per
+// row, two for fp32); B is staged in shared memory per 256-k step as fp32
+// with an odd row stride; one butterfly reduction per output at the end.
+// For the tensor-core precision modes only: its summation order differs
+// from the k-sequential fp32 parity kernel.
+constexpr int kNarrowK = 256;
+constexpr int kNarrowWarps = 8;
+constexpr int kNarrowRows = 4;
+template <int NMAX, typename TA>
+__global__ void __launch_bounds__(32 * kNarrowWarps) gemm_narrow_kernel(const SimtParams p) {
+    __shared__ float Bs[kNarrowK * (NMAX + 1)];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * kNarrowWarps + warp) * kNarrowRows;
+    const TA* A = reinterpret_cast<const TA*>(p.a.ptr);
+    float acc[kNarrowRows][NMAX];
+#pragma unroll
+    for (int r = 0; r < kNarrowRows; r++)
+#pragma unroll
+        for (int n = 0; n < NMAX; n++) acc[r][n] = 0.f;
+    for (int k0 = 0; k0 < p.K; k0 += kNarrowK) {
+        const int kn = min(kNarrowK, p.K - k0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < kNarrowK * NMAX; i += blockDim.x) {
+            const int kk = i / NMAX, n = i % NMAX;
+            Bs[kk * (NMAX + 1) + n] = (n < p.N && kk < kn) ? ld_op(p.b, n, k0 + kk) : 0.f;
+        }
+        __syncthreads();
+        const int kl = 8 * lane;  // this lane's 8 k within the step
+        if (kl >= kn) continue;
+#pragma unroll
+        for (int r = 0; r < kNarrowRows; r++) {
+            const int row = row0 + r;
+            if (row >= p.M) break;
+            float a[8];
+            const TA* src = A + (size_t)row * p.a.ld + k0 + kl;
+            if (kl + 8 <= kn) {
+                if constexpr (sizeof(TA) == 2) {
+                    const uint4 t = *reinterpret_cast<const uint4*>(src);
+                    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&t);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) a[j] = bf2f(h[j]);
+                } else {
+                    const float4 t0 = reinterpret_cast<const float4*>(src)[0];
+                    const float4 t1 = reinterpret_cast<const float4*>(src)[1];
+                    a[0] = t0.x; a[1] = t0.y; a[2] = t0.z; a[3] = t0.w;
+                    a[4] = t1.x; a[5] = t1.y; a[6] = t1.z; a[7] = t1.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++) a[j] = kl + j < kn ? ld_any(src, p.a.dtype, j) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float* b = Bs + (kl + j) * (NMAX + 1);
+#pragma unroll
+                for (int n = 0; n < NMAX; n++) acc[r][n] = fmaf(a[j], b[n], acc[r][n]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kNarrowRows; r++) {
+        const int row = row0 + r;
+        float mine = 0.f;
+#pragma unroll
+        for (int n = 0; n < NMAX; n++) {
+            float s = acc[r][n];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == n) mine = s;
+        }
+        if (row < p.M && lane < p.N) epi_apply(p.ep, row, lane, mine);
+    }
 }
 
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
@@ -787,20 +939,19 @@ static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner
 }
 
 // Output map for the TMA-store epilogue: row-major [rows, cols] with leading
-// dimension ld; 32 x 32 boxes (fp32: 128-byte rows, 128-byte swizzle; bf16:
-// 64-byte rows, 64-byte swizzle).
+// dimension ld; boxes of 32 rows x 64 bytes with 64-byte swizzle (bf16: 32
+// columns, fp32: 16 columns), so every box fills one 2 KB staging buffer.
 static bool make_out_map(CUtensorMap* m, const void* ptr, int dtype, long long cols, long long rows, long long ld) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
     const int es = dtype == kBF16 ? 2 : 4;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
-    (void)es;
-    cuuint32_t box[2] = {32, 32};
+    cuuint32_t box[2] = {(cuuint32_t)(64 / es), 32};
     cuuint32_t estr[2] = {1, 1};
     return enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               dtype == kBF16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_SWIZZLE_64B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -818,9 +969,21 @@ bool gemm_uses_tensor_cores(const GemmDesc& d) {
     if (d.M <= 0 || d.N <= 0 || d.K <= 0) return false;
     // very narrow outputs waste a 128-wide tile; the SIMT kernel is cheaper
     if (d.N < 32) return false;
-    // grouped: only row groups with a K-major B (one 2D tensor map)
-    if (d.group_k) return false;
-    if (d.groups > 1 && (d.b.mn_major || d.b_group_stride != (long long)d.N * d.b.ld)) return false;
+    if (d.groups > 1) {
+        const int bk = d.a.dtype == kBF16 ? 64 : 32;
+        if (d.group_k) {
+            // both operands stored token-major ([K rows][M or N]); segment
+            // starts are multiples of 128 rows and rows past a segment's end
+            // up to the next k-block are zero (MoE dispatch padding)
+            if (!d.a.mn_major || !d.b.mn_major || !d.seg || !d.seg_end || !d.ep.c32) return false;
+            if (d.ep.add || d.ep.c16 || d.ep.z || d.ep.act || d.ep.dz || d.ep.row_scale || d.ep.out_rows) return false;
+            return true;
+        }
+        // row groups: one 2D tensor map over all groups' B matrices, stacked
+        // along N (K-major) or along K (MN-major, K a whole number of k-blocks)
+        if (!d.b.mn_major) return d.b_group_stride == (long long)d.N * d.b.ld;
+        return d.b_group_stride == (long long)d.K * d.b.ld && d.K % bk == 0;
+    }
     return true;
 }
 
@@ -867,8 +1030,9 @@ static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         attr = true;
     }
-    // one CTA per unit; running CTAs take over the units of CTAs not yet launched
-    int grid = p.total_units;
+    // one CTA per unit; running CTAs take over the units of CTAs not yet
+    // launched (static scheduling: one CTA per SM, units round-robin)
+    int grid = p.static_sched ? min(p.total_units, num_sms()) : p.total_units;
     if (grid <= 0) return cudaSuccess;
     k<<<grid, kTcThreads, C::SMEM, s>>>(ta, tb, om.z, om.c32, om.c16, p);
     return cudaGetLastError();
@@ -907,9 +1071,11 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     if (!d.a.mn_major) ok = make_map(&ta, d.a.ptr, d.a.dtype, d.K, d.M, d.a.ld, bk, 128);
     else ok = make_map(&ta, d.a.ptr, d.a.dtype, d.M, d.K, d.a.ld, chunk, bk, tf32);
     if (!ok) return -2;
-    const long long brows = (long long)d.N * d.groups;
+    const bool b_kgroup = d.groups > 1 && !d.group_k && d.b.mn_major;
+    const long long brows = (d.groups > 1 && !d.group_k && !b_kgroup) ? (long long)d.N * d.groups : d.N;
+    const long long bk_rows = b_kgroup ? (long long)d.K * d.groups : d.K;
     if (!d.b.mn_major) ok = make_map(&tb, d.b.ptr, d.b.dtype, d.K, brows, d.b.ld, bk, bn);
-    else ok = make_map(&tb, d.b.ptr, d.b.dtype, brows, d.K, d.b.ld, chunk, bk, tf32);
+    else ok = make_map(&tb, d.b.ptr, d.b.dtype, brows, bk_rows, d.b.ld, chunk, bk, tf32);
     if (!ok) return -2;
 
     TcParams p;
@@ -926,16 +1092,20 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     p.seg = d.seg;
     p.seg_end = d.seg_end;
     p.max_m_tiles_per_group = p.m_tiles;
+    p.bk = bk;
+    p.b_kgroup = b_kgroup ? 1 : 0;
+    p.group_k = d.group_k ? 1 : 0;
+    p.c_group_stride = d.c_group_stride;
+    p.static_sched = d.groups > 1 ? 1 : 0;
     p.workspace = nullptr;
     if (p.splits > 1) {
         if (!d.workspace || d.workspace_floats < (size_t)p.splits * d.M * d.N) return -3;
         p.workspace = d.workspace;
     }
     p.vec_ok = ep_vec_ok(d) ? 1 : 0;
-    if (d.groups > 1) {
-        // groups are stacked along B's rows: only a K-major B whose group
-        // stride is exactly N rows can be described by one 2D tensor map
-        if (d.b.mn_major || d.b_group_stride != (long long)d.N * d.b.ld) return -4;
+    if (d.group_k) {
+        p.total_units = d.groups * p.m_tiles * p.n_tiles;
+    } else if (d.groups > 1) {
         p.total_units = d.groups * p.max_m_tiles_per_group * p.n_tiles * p.splits;
     } else {
         p.total_units = p.m_tiles * p.n_tiles * p.splits;
@@ -975,6 +1145,11 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
 
 static int gemm_simt(const GemmDesc& d, cudaStream_t s) {
     SimtParams p;
+    // narrow kernel: K-major A whose rows are 16-byte aligned
+    const int aes = d.a.dtype == kBF16 ? 2 : 4;
+    const bool narrow = d.engine != kEngineSimt && d.groups == 1 && d.N <= 32 && !d.ep.out_rows &&
+                        !d.ep.col_block && !d.a.mn_major && (reinterpret_cast<uintptr_t>(d.a.ptr) & 15) == 0 &&
+                        (d.a.ld * aes) % 16 == 0;
     p.M = d.M;
     p.N = d.N;
     p.K = d.K;
@@ -987,6 +1162,19 @@ static int gemm_simt(const GemmDesc& d, cudaStream_t s) {
     p.b_group_stride = d.b_group_stride;
     p.group_k = d.group_k;
     p.c_group_stride = d.c_group_stride;
+    if (narrow) {
+        const int rows = kNarrowWarps * kNarrowRows;
+        const unsigned blocks = (unsigned)((d.M + rows - 1) / rows);
+        const bool h = d.a.dtype == kBF16;
+        if (d.N <= 16) {
+            if (h) gemm_narrow_kernel<16, __nv_bfloat16><<<blocks, 32 * kNarrowWarps, 0, s>>>(p);
+            else gemm_narrow_kernel<16, float><<<blocks, 32 * kNarrowWarps, 0, s>>>(p);
+        } else {
+            if (h) gemm_narrow_kernel<32, __nv_bfloat16><<<blocks, 32 * kNarrowWarps, 0, s>>>(p);
+            else gemm_narrow_kernel<32, float><<<blocks, 32 * kNarrowWarps, 0, s>>>(p);
+        }
+        return cudaGetLastError() == cudaSuccess ? 0 : -5;
+    }
     dim3 grid((d.N + 63) / 64, (d.M + 63) / 64, d.groups);
     if (grid.x == 0 || grid.y == 0) return 0;
     gemm_simt_kernel<<<grid, 256, 0, s>>>(p);

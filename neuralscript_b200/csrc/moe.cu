@@ -52,11 +52,14 @@ struct MoeScratch {
     void* hp = nullptr;
     float* dg = nullptr;
     float* t1 = nullptr;
+    float* wg_part = nullptr;  // [ceil(rows / kWgTokens), D, E] partial gate-weight gradients
 };
 
 namespace {
 constexpr int kRouteTokens = 128;
 constexpr int kChunk = 256;  // tokens per dispatch chunk (one warp each)
+constexpr int kWgTokens = 128;  // tokens per partial gate-weight-gradient block
+constexpr int kWgMaxE = 8;      // experts handled by the two-pass gate-weight gradient
 
 inline int launch_ok() { return cudaGetLastError() == cudaSuccess ? 0 : -5; }
 }  // namespace
@@ -154,24 +157,47 @@ __global__ void moe_hist_kernel(const int* __restrict__ best, int M, int E, int*
     for (int e = threadIdx.x; e < E; e += 32) hist[(size_t)c * E + e] = cnt[e];
 }
 
-// segment starts (padded to 128 rows) and per-chunk bases, single thread
-// per expert column.
+// Segment starts (each padded to 128 rows) and per-chunk bases: hist[c][e]
+// (tokens of chunk c routed to expert e) becomes the position of chunk c's
+// first such token. One warp per expert column scans the chunks 32 at a
+// time with shuffles; the segment starts then follow from the expert
+// totals in expert order.
 __global__ void moe_scan_kernel(int* __restrict__ hist, int chunks, int E, int* __restrict__ seg,
                                 int* __restrict__ seg_end) {
-    if (threadIdx.x != 0) return;
-    int start = 0;
-    for (int e = 0; e < E; e++) {
-        int run = start;
-        for (int c = 0; c < chunks; c++) {
-            int v = hist[(size_t)c * E + e];
-            hist[(size_t)c * E + e] = run;
-            run += v;
+    extern __shared__ int tot[];  // [E] totals, then [E] segment starts
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int e = warp; e < E; e += nw) {
+        int carry = 0;
+        for (int c0 = 0; c0 < chunks; c0 += 32) {
+            const int c = c0 + lane;
+            const int v = c < chunks ? hist[(size_t)c * E + e] : 0;
+            int inc = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += n;
+            }
+            if (c < chunks) hist[(size_t)c * E + e] = carry + inc - v;  // exclusive
+            carry += __shfl_sync(0xffffffffu, inc, 31);
         }
-        seg[e] = start;
-        seg_end[e] = run;
-        start = start + (run - start + 127) / 128 * 128;
+        if (lane == 0) tot[e] = carry;
     }
-    seg[E] = start;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int start = 0;
+        for (int e = 0; e < E; e++) {
+            tot[E + e] = start;
+            seg[e] = start;
+            seg_end[e] = start + tot[e];
+            start += (tot[e] + 127) / 128 * 128;
+        }
+        seg[E] = start;
+    }
+    __syncthreads();
+    for (int e = warp; e < E; e += nw) {
+        const int base = tot[E + e];
+        for (int c = lane; c < chunks; c += 32) hist[(size_t)c * E + e] += base;
+    }
 }
 
 // stable placement: chunk c's tokens in token order, ranks from warp matches
@@ -310,6 +336,55 @@ void moe_release(Op& op) {
     op.moe = nullptr;
 }
 
+// Gate-weight gradient dWg[D, E] = x^T dg over all tokens, in two passes
+// with a fixed summation order (deterministic, no atomics): block (c, y)
+// sums tokens [c * kWgTokens, +kWgTokens) in ascending order for 4
+// consecutive columns d per thread and every expert; the reduce kernel then
+// adds the chunks in ascending order. x is read once, coalesced (a token row
+// is 4 KB across the block at D = 1024).
+__global__ void __launch_bounds__(256) moe_wg_partial_kernel(const float* __restrict__ x,
+                                                             const float* __restrict__ dg, int M, int D, int E,
+                                                             float* __restrict__ part) {
+    __shared__ float sdg[kWgTokens * kWgMaxE];
+    const int c = blockIdx.x;
+    const int t0 = c * kWgTokens;
+    const int nt = min(kWgTokens, M - t0);
+    for (int i = threadIdx.x; i < nt * E; i += blockDim.x) sdg[(i / E) * kWgMaxE + i % E] = dg[(size_t)t0 * E + i];
+    __syncthreads();
+    const int d = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+    if (d >= D) return;
+    float acc[4][kWgMaxE];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int e = 0; e < kWgMaxE; e++) acc[i][e] = 0.f;
+    const float* xp = x + (size_t)t0 * D + d;
+#pragma unroll 4
+    for (int t = 0; t < nt; t++) {
+        const float4 xv = *reinterpret_cast<const float4*>(xp + (size_t)t * D);
+        const float* g = sdg + t * kWgMaxE;
+#pragma unroll
+        for (int e = 0; e < kWgMaxE; e++) {
+            acc[0][e] = fmaf(xv.x, g[e], acc[0][e]);
+            acc[1][e] = fmaf(xv.y, g[e], acc[1][e]);
+            acc[2][e] = fmaf(xv.z, g[e], acc[2][e]);
+            acc[3][e] = fmaf(xv.w, g[e], acc[3][e]);
+        }
+    }
+    float* out = part + ((size_t)c * D + d) * E;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        for (int e = 0; e < E; e++) out[i * E + e] = acc[i][e];
+}
+
+__global__ void moe_wg_reduce_kernel(const float* __restrict__ part, int chunks, int n, float* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float s = 0.f;
+    for (int c = 0; c < chunks; c++) s += part[(size_t)c * n + i];
+    out[i] = s;
+}
+
 int moe_plan(ns_model* m, Op& op, int mmax, bool train) {
     const LayerSpec& l = m->spec.layers[op.layer];
     MoeScratch* s = new MoeScratch();
@@ -344,6 +419,8 @@ int moe_plan(ns_model* m, Op& op, int mmax, bool train) {
         s->dpb = (float*)A(P * 4);
         s->dg = (float*)A(R * s->E * 4);
         s->t1 = (float*)A(R * s->D * 4);
+        if (s->E <= kWgMaxE && s->D % 4 == 0)
+            s->wg_part = (float*)A((R + kWgTokens - 1) / kWgTokens * (size_t)s->D * s->E * 4);
         if (s->linear) {
             s->dH = A(P * s->D * es);  // pb-scaled dY in the GEMM dtype
         } else {
@@ -384,13 +461,15 @@ int moe_forward(ns_model* m, Op& op, int M, bool train) {
         if (out.h16) cudaMemsetAsync(out.h16, 0, 2 * (size_t)M * D, st);
         return 0;
     }
+    const std::string lname = sp.layers[op.layer].name;
+    int reg = region_open(m, "fwd:" + lname + ".route");
     launch_counter() += 1;
     if (moe_route(in.f32, m->d_w + wg.off, m->d_active, M, D, E, s->best, s->pb, s->probs, st)) return -1;
     const int chunks = (M + kChunk - 1) / kChunk;
     const int mpad = M + E * 128;
     launch_counter() += 4;
     moe_hist_kernel<<<chunks, 32, sizeof(int) * E, st>>>(s->best, M, E, s->hist);
-    moe_scan_kernel<<<1, 32, 0, st>>>(s->hist, chunks, E, s->seg, s->seg_end);
+    moe_scan_kernel<<<1, 32 * (E < 32 ? E : 32), sizeof(int) * 2 * E, st>>>(s->hist, chunks, E, s->seg, s->seg_end);
     fill_int_kernel<<<(mpad + 255) / 256, 256, 0, st>>>(s->perm, mpad, -1);
     moe_place_kernel<<<chunks, 32, sizeof(int) * E, st>>>(s->best, M, E, s->hist, s->perm, s->pos);
     launch_counter() += 1;
@@ -400,7 +479,9 @@ int moe_forward(ns_model* m, Op& op, int M, bool train) {
     else
         moe_gather_kernel<float, float><<<rows_grid(mpad), 256, 0, st>>>(in.f32, s->perm, mpad, D, nullptr,
                                                                           (float*)s->xs, s->pb, s->pbs);
+    region_close(m, reg);
     if (launch_ok()) return -1;
+    reg = region_open(m, "fwd:" + lname + ".experts");
     const WeightInfo& w1 = sp.weights[op.widx + 1];
     if (s->linear) {
         GemmDesc g;  // ys = xs We[e]   (unscaled; scaled + scattered below)
@@ -418,6 +499,7 @@ int moe_forward(ns_model* m, Op& op, int M, bool train) {
         if (gemm_run(m, g)) return -1;
         launch_counter() += 1;
         moe_scale_scatter_kernel<<<rows_grid(mpad), 256, 0, st>>>(s->ys, s->pbs, s->perm, mpad, D, out.f32, out.h16);
+        region_close(m, reg);
         (void)w1;
         return launch_ok();
     }
@@ -461,7 +543,9 @@ int moe_forward(ns_model* m, Op& op, int M, bool train) {
     g2.ep.ld_c32 = D;
     g2.ep.c16 = out.h16;
     g2.ep.ld_c16 = D;
-    return gemm_run(m, g2);
+    const int rc = gemm_run(m, g2);
+    region_close(m, reg);
+    return rc;
 }
 
 int moe_backward(ns_model* m, Op& op, int M) {
@@ -481,6 +565,8 @@ int moe_backward(ns_model* m, Op& op, int M) {
         return 0;
     }
     const float* dY = out.gcur;
+    const std::string lname = sp.layers[op.layer].name;
+    int reg = region_open(m, "bwd:" + lname + ".experts");
     launch_counter() += 1;
     if (s->linear) {
         moe_gather_kernel<float, float><<<rows_grid(mpad), 256, 0, st>>>(dY, s->perm, mpad, D, nullptr,
@@ -554,19 +640,31 @@ int moe_backward(ns_model* m, Op& op, int M) {
     gw1.ep.c32 = m->d_g + w1.off;
     gw1.ep.ld_c32 = H;
     if (gemm_run(m, gw1)) return -1;
+    region_close(m, reg);
+    reg = region_open(m, "bwd:" + lname + ".gate");
     // gate path
     launch_counter() += 1;
     moe_gate_grad_kernel<<<(M + 255) / 256, 256, 0, st>>>(s->probs, s->best, s->pb, s->pos, s->dpb, M, E, s->dg);
-    GemmDesc gg;  // dWg = x^T dg
-    gg.M = D;
-    gg.N = E;
-    gg.K = M;
-    gg.a = op_of(in.f32, kF32, D, true);
-    gg.b = op_of(s->dg, kF32, E, true);
-    gg.engine = kEngineSimt;
-    gg.ep.c32 = m->d_g + wg.off;
-    gg.ep.ld_c32 = E;
-    if (gemm_run(m, gg)) return -1;
+    if (s->wg_part && m->precision != 0 && !(reinterpret_cast<uintptr_t>(in.f32) & 15)) {
+        // dWg = x^T dg: two fixed-order passes over the tokens
+        const int chunks = (M + kWgTokens - 1) / kWgTokens;
+        launch_counter() += 2;
+        moe_wg_partial_kernel<<<dim3(chunks, (D / 4 + 255) / 256), 256, 0, st>>>(in.f32, s->dg, M, D, E, s->wg_part);
+        moe_wg_reduce_kernel<<<(D * E + 255) / 256, 256, 0, st>>>(s->wg_part, chunks, D * E, m->d_g + wg.off);
+        if (launch_ok()) return -1;
+    } else {
+        GemmDesc gg;  // dWg = x^T dg (fp32 parity mode: k-sequential FMA order)
+        gg.M = D;
+        gg.N = E;
+        gg.K = M;
+        gg.a = op_of(in.f32, kF32, D, true);
+        gg.b = op_of(s->dg, kF32, E, true);
+        gg.engine = kEngineSimt;
+        gg.ep.c32 = m->d_g + wg.off;
+        gg.ep.ld_c32 = E;
+        if (gemm_run(m, gg)) return -1;
+    }
+    region_close(m, reg);
     if (!in.gbuf) return 0;
     GemmDesc gx;  // t1 = dH We1[e]^T scattered to tokens (+ running total)
     gx.M = mpad;
