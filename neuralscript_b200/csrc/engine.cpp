@@ -353,6 +353,7 @@ static void free_plan(ns_model* m) {
     }
     m->d_in = m->d_labels = m->d_rowloss = m->d_loss = nullptr;
     m->d_targets = nullptr;
+    m->d_stage = nullptr;
     m->d_ws = nullptr;
     m->ws_floats = 0;
     m->d_scratch = nullptr;
@@ -1534,6 +1535,11 @@ void nsb_free(ns_model* m) {
     if (m->ev_out) cudaEventDestroy(m->ev_out);
     if (m->comm) nccl().CommDestroy(m->comm);
     for (cudaEvent_t e : m->dist_events) cudaEventDestroy(e);
+    for (cudaEvent_t e : m->chunk_events) cudaEventDestroy(e);
+    if (m->copy_stream) {
+        cudaStreamSynchronize(m->copy_stream);
+        cudaStreamDestroy(m->copy_stream);
+    }
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -1636,6 +1642,63 @@ int nsb_eval_infer_device(ns_model* m, const float* d_input, float* d_output, si
     return rc;
 }
 
+// Rows per chunk of a pipelined host-buffer inference (0: one pass). Worth
+// it when the output copy to page-locked host memory is large enough to
+// dominate the call (8 MB and up): the rows are split into four chunks, in
+// whole attention sequences (or 128-row tiles), and each chunk's output is
+// copied back while the next chunk computes. Rows are independent, so the
+// result is that of one pass up to the fp32 summation order of a GEMM that
+// splits K at the smaller row count.
+static int infer_chunk_rows(const ns_model* m, int M, const float* output) {
+    const size_t out_bytes = (size_t)M * m->spec.out_cols * sizeof(float);
+    if (out_bytes < (8u << 20)) return 0;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, output) != cudaSuccess || at.type != cudaMemoryTypeHost) {
+        cudaGetLastError();
+        return 0;  // pageable destination: copies would block the host
+    }
+    int unit = 128;
+    for (const auto& l : m->spec.layers)
+        if (l.kind == "attention") {
+            const int S = (int)l.geti("seq", 0);
+            if (S <= 0) return 0;  // one sequence spans the call
+            unit = S;
+        }
+    const int chunk = (M / 4 + unit - 1) / unit * unit;
+    return chunk > 0 && chunk < M && M % unit == 0 ? chunk : 0;
+}
+
+static int eval_pipelined(ns_model* m, const float* input, float* output, int M, int chunk) {
+    const Spec& s = m->spec;
+    if (!m->copy_stream && cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail("stream creation failed");
+    if (!m->d_stage && !(m->d_stage = (float*)plan_alloc(m, sizeof(float) * (size_t)m->mmax * s.out_cols)))
+        return fail("device allocation failed");
+    const int n = (M + chunk - 1) / chunk;
+    while ((int)m->chunk_events.size() < n + 1) {
+        cudaEvent_t e;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return fail("event creation failed");
+        m->chunk_events.push_back(e);
+    }
+    const float* out_dev = m->vals[m->out_val].f32;
+    for (int c = 0; c < n; c++) {
+        const int r0 = c * chunk, mc = M - r0 < chunk ? M - r0 : chunk;
+        cudaMemcpyAsync(m->d_in, input + (size_t)r0 * s.in_cols, sizeof(float) * (size_t)mc * s.in_cols,
+                        cudaMemcpyHostToDevice, m->stream);
+        if (forward(m, mc, false)) return -1;
+        float* st = m->d_stage + (size_t)r0 * s.out_cols;
+        cudaMemcpyAsync(st, out_dev, sizeof(float) * (size_t)mc * s.out_cols, cudaMemcpyDeviceToDevice, m->stream);
+        cudaEventRecord(m->chunk_events[c], m->stream);
+        cudaStreamWaitEvent(m->copy_stream, m->chunk_events[c], 0);
+        cudaMemcpyAsync(output + (size_t)r0 * s.out_cols, st, sizeof(float) * (size_t)mc * s.out_cols,
+                        cudaMemcpyDeviceToHost, m->copy_stream);
+    }
+    // the engine stream (which finish() waits on) ends after the last copy
+    cudaEventRecord(m->chunk_events[n], m->copy_stream);
+    cudaStreamWaitEvent(m->stream, m->chunk_events[n], 0);
+    return 0;
+}
+
 int nsb_eval_infer(ns_model* m, const float* input, float* output, size_t input_numel) {
     if (!m) return -1;
     g_err.clear();
@@ -1644,6 +1707,14 @@ int nsb_eval_infer(ns_model* m, const float* input, float* output, size_t input_
     if (M <= 0) return 0;
     if (!input || !output) return fail("null input/output");
     if (plan(m, M, false)) return -1;
+    if (const int chunk = infer_chunk_rows(m, M, output)) {
+        if (eval_pipelined(m, input, output, M, chunk)) {
+            finish(m);
+            return -1;
+        }
+        m->launches = launch_counter() - l0;
+        return finish(m);
+    }
     cudaMemcpyAsync(m->d_in, input, sizeof(float) * (size_t)M * m->spec.in_cols, cudaMemcpyHostToDevice, m->stream);
     if (forward(m, M, false)) {
         finish(m);

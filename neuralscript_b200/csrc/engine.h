@@ -125,6 +125,11 @@ struct ns_model {
     bool group_lost = false;  // the communicator was aborted; train steps fail from then on
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;  // ordering with the caller's stream (device entries)
     cudaStream_t comm_stream = nullptr;    // gradient all-reduces, overlapped with the backward
+    // pipelined host-buffer inference: output rows staged per chunk and
+    // copied to the caller on copy_stream while the next chunk computes
+    cudaStream_t copy_stream = nullptr;
+    float* d_stage = nullptr;  // plan allocation, mmax x out_cols
+    std::vector<cudaEvent_t> chunk_events;
     std::vector<cudaEvent_t> dist_events;  // ordering events between the two streams
     size_t ev_next = 0;
     std::vector<char> reduced;             // per weight: its all-reduce was issued this step

@@ -703,9 +703,46 @@ __global__ void mse_kernel(const float* __restrict__ p, const float* __restrict_
     }
 }
 
+// Warp per row, 4 columns per lane per step (C a multiple of 4, rows
+// 16-byte aligned): no block-wide reduction per row.
+__global__ void mse_vec_kernel(const float* __restrict__ p, const float* __restrict__ y, int M, int C, float denom,
+                               float* __restrict__ row_loss, float* __restrict__ d32,
+                               __nv_bfloat16* __restrict__ d16) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        const float4* pr = reinterpret_cast<const float4*>(p + (size_t)r * C);
+        const float4* yr = reinterpret_cast<const float4*>(y + (size_t)r * C);
+        float acc = 0.f;
+        for (int j = lane; j < C / 4; j += 32) {
+            const float4 a = pr[j], b = yr[j];
+            const float e0 = a.x - b.x, e1 = a.y - b.y, e2 = a.z - b.z, e3 = a.w - b.w;
+            acc += e0 * e0;
+            acc += e1 * e1;
+            acc += e2 * e2;
+            acc += e3 * e3;
+            const float4 d = make_float4(2.0f * e0 / denom, 2.0f * e1 / denom, 2.0f * e2 / denom, 2.0f * e3 / denom);
+            if (d32) reinterpret_cast<float4*>(d32 + (size_t)r * C)[j] = d;
+            if (d16) {
+                uint2 h;
+                reinterpret_cast<__nv_bfloat162*>(&h)[0] = __floats2bfloat162_rn(d.x, d.y);
+                reinterpret_cast<__nv_bfloat162*>(&h)[1] = __floats2bfloat162_rn(d.z, d.w);
+                reinterpret_cast<uint2*>(d16 + (size_t)r * C)[j] = h;
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) row_loss[r] = acc;
+    }
+}
+
 int mse_fwd_bwd(const float* p, const float* y, int M, int C, float denom, float* row_loss, float* d32,
                 __nv_bfloat16* d16, cudaStream_t s) {
     if (M <= 0) return 0;
+    auto al = [](const void* q) { return !(reinterpret_cast<uintptr_t>(q) & 15); };
+    if (C % 4 == 0 && al(p) && al(y) && (!d32 || al(d32)) && (!d16 || al(d16))) {
+        const int blocks = min((M + 7) / 8, num_sms() * 16);
+        mse_vec_kernel<<<blocks, 256, 0, s>>>(p, y, M, C, denom, row_loss, d32, d16);
+        return launch_ok();
+    }
     mse_kernel<<<(unsigned)min(M, num_sms() * 8), 256, 0, s>>>(p, y, M, C, denom, row_loss, d32, d16);
     return launch_ok();
 }
@@ -787,8 +824,29 @@ __global__ void f2bf_kernel(const float* __restrict__ x, size_t n, __nv_bfloat16
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         o[i] = f2bf(x[i]);
 }
+// 8 elements per thread per step: two 16-byte loads, one 16-byte store
+__global__ void f2bf_x8_kernel(const float4* __restrict__ x, size_t n8, uint4* __restrict__ o) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 a = x[2 * i], b = x[2 * i + 1];
+        uint4 r;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
+        h[0] = __floats2bfloat162_rn(a.x, a.y);
+        h[1] = __floats2bfloat162_rn(a.z, a.w);
+        h[2] = __floats2bfloat162_rn(b.x, b.y);
+        h[3] = __floats2bfloat162_rn(b.z, b.w);
+        o[i] = r;
+    }
+}
 int f32_to_bf16(const float* x, size_t n, __nv_bfloat16* out, cudaStream_t s) {
     if (n == 0) return 0;
+    if (n % 8 == 0 && !(reinterpret_cast<uintptr_t>(x) & 15) && !(reinterpret_cast<uintptr_t>(out) & 15)) {
+        const size_t n8 = n / 8;
+        const size_t cap = (size_t)num_sms() * 16;
+        const size_t blocks = (n8 + 255) / 256;
+        f2bf_x8_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, s>>>(reinterpret_cast<const float4*>(x), n8,
+                                                                               reinterpret_cast<uint4*>(out));
+        return launch_ok();
+    }
     f2bf_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, out);
     return launch_ok();
 }

@@ -57,6 +57,7 @@ struct MoeScratch {
 
 namespace {
 constexpr int kRouteTokens = 128;
+constexpr int kRouteRegE = 8;  // expert count whose logits the router keeps in registers
 constexpr int kChunk = 256;  // tokens per dispatch chunk (one warp each)
 constexpr int kWgTokens = 128;  // tokens per partial gate-weight-gradient block
 constexpr int kWgMaxE = 8;      // experts handled by the two-pass gate-weight gradient
@@ -91,10 +92,26 @@ __global__ void __launch_bounds__(kRouteTokens) moe_router_kernel(const float* _
         }
         __syncthreads();
         const int kn = min(32, D - k0);
-        for (int e = 0; e < E; e++) {
-            float a = acc[t * E + e];
-            for (int kk = 0; kk < kn; kk++) a = fmaf(xt[t * 33 + kk], wt[kk * E + e], a);
-            acc[t * E + e] = a;
+        if (E == kRouteRegE && kn == 32) {
+            // the usual case: logits in registers, x read once per k, Wg
+            // broadcast; each logit still accumulates in increasing k
+            float a[kRouteRegE];
+#pragma unroll
+            for (int e = 0; e < kRouteRegE; e++) a[e] = acc[t * kRouteRegE + e];
+#pragma unroll 8
+            for (int kk = 0; kk < 32; kk++) {
+                const float xv = xt[t * 33 + kk];
+#pragma unroll
+                for (int e = 0; e < kRouteRegE; e++) a[e] = fmaf(xv, wt[kk * kRouteRegE + e], a[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < kRouteRegE; e++) acc[t * kRouteRegE + e] = a[e];
+        } else {
+            for (int e = 0; e < E; e++) {
+                float a = acc[t * E + e];
+                for (int kk = 0; kk < kn; kk++) a = fmaf(xt[t * 33 + kk], wt[kk * E + e], a);
+                acc[t * E + e] = a;
+            }
         }
     }
     const int tok = t0 + t;
@@ -130,9 +147,124 @@ __global__ void __launch_bounds__(kRouteTokens) moe_router_kernel(const float* _
             probs[(size_t)tok * E + e] = ((!active || active[e]) && sum > 0.f) ? acc[t * E + e] / sum : 0.f;
 }
 
+// Softmax over live experts and the first-max top-1 rule of the reference
+// router (codegen.cpp:1915-1945) from fp32 logits a[0..E).
+__device__ __forceinline__ void route_finish(float* a, const uint8_t* __restrict__ active, int E, int tok,
+                                             int* __restrict__ best, float* __restrict__ pb,
+                                             float* __restrict__ probs) {
+    float mx = -1.0e30f;
+    for (int e = 0; e < E; e++)
+        if ((!active || active[e]) && a[e] > mx) mx = a[e];
+    float sum = 0.f;
+    int b = -1;
+    float wb = 0.f;
+    for (int e = 0; e < E; e++) {
+        if (active && !active[e]) {
+            a[e] = 0.f;
+            continue;
+        }
+        // exp in double then rounded (see moe_router_kernel)
+        const float w = (float)exp((double)(a[e] - mx));
+        a[e] = w;
+        sum += w;
+        if (b < 0 || w > wb) {
+            b = e;
+            wb = w;
+        }
+    }
+    best[tok] = b;
+    pb[tok] = (sum > 0.f && b >= 0) ? wb / sum : 0.f;
+    if (probs)
+        for (int e = 0; e < E; e++)
+            probs[(size_t)tok * E + e] = ((!active || active[e]) && sum > 0.f) ? a[e] / sum : 0.f;
+}
+
+// Router for 8 experts: a block of 128 threads owns 64 tokens, two
+// adjacent threads per token, each accumulating 4 of the logits over all k
+// in increasing order with fmaf (the same chain as moe_router_kernel, so
+// logits are bit-identical). x streams through shared memory in
+// [64 tokens x 128 k] stages, double-buffered with cp.async (coalesced
+// 16-byte copies, the next stage in flight while this one is used); Wg
+// sits in shared memory as two float4 per k.
+constexpr int kR8Tok = 64, kR8K = 128, kR8Ld = kR8K + 4;  // row stride 528 B (16-byte aligned)
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(2 * kR8Tok) moe_router8_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ Wg,
+                                                                  const uint8_t* __restrict__ active, int M, int D,
+                                                                  int* __restrict__ best, float* __restrict__ pb,
+                                                                  float* __restrict__ probs) {
+    extern __shared__ float4 w4[];  // [D][2], then two x stages [kR8Tok][kR8Ld]
+    float* xs = reinterpret_cast<float*>(w4 + 2 * D);
+    const int t0 = blockIdx.x * kR8Tok;
+    const int nt = min(kR8Tok, M - t0);
+    const int nst = D / kR8K;
+    auto stage = [&](int s) {
+        float* dst = xs + (s & 1) * kR8Tok * kR8Ld;
+        // 64 rows x 32 16-byte pieces; rows past M are not copied (their
+        // tokens are never finished)
+        for (int i = threadIdx.x; i < kR8Tok * (kR8K / 4); i += blockDim.x) {
+            const int r = i / (kR8K / 4), q = i % (kR8K / 4);
+            if (r < nt) cp_async16(dst + r * kR8Ld + 4 * q, x + (size_t)(t0 + r) * D + s * kR8K + 4 * q);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0);
+    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
+        const float* w = Wg + (size_t)(i >> 1) * 8 + (i & 1) * 4;
+        w4[i] = make_float4(w[0], w[1], w[2], w[3]);
+    }
+    const int tok = threadIdx.x >> 1, half = threadIdx.x & 1;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int s = 0; s < nst; s++) {
+        if (s + 1 < nst) {
+            stage(s + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const float4* xr = reinterpret_cast<const float4*>(xs + (s & 1) * kR8Tok * kR8Ld + tok * kR8Ld);
+        const float4* wp = w4 + (size_t)s * kR8K * 2 + half;
+#pragma unroll 8
+        for (int k4 = 0; k4 < kR8K / 4; k4++) {
+            const float4 xv = xr[k4];
+            const float xk[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float4 w = wp[(4 * k4 + j) * 2];
+                a0 = fmaf(xk[j], w.x, a0);
+                a1 = fmaf(xk[j], w.y, a1);
+                a2 = fmaf(xk[j], w.z, a2);
+                a3 = fmaf(xk[j], w.w, a3);
+            }
+        }
+        __syncthreads();  // this stage's buffer is refilled two stages on
+    }
+    // both halves of the pair gather all 8 logits; the even thread finishes
+    const float o0 = __shfl_xor_sync(0xffffffffu, a0, 1), o1 = __shfl_xor_sync(0xffffffffu, a1, 1);
+    const float o2 = __shfl_xor_sync(0xffffffffu, a2, 1), o3 = __shfl_xor_sync(0xffffffffu, a3, 1);
+    if (tok >= nt || half) return;
+    float a[8] = {a0, a1, a2, a3, o0, o1, o2, o3};
+    route_finish(a, active, 8, t0 + tok, best, pb, probs);
+}
+
 int moe_route(const float* x, const float* Wg, const uint8_t* active, int M, int D, int E, int* best, float* pb,
               float* probs, cudaStream_t s) {
     if (M <= 0) return 0;
+    const size_t smem8 = (size_t)D * 32 + 2 * sizeof(float) * kR8Tok * kR8Ld;
+    if (E == 8 && D % kR8K == 0 && !(reinterpret_cast<uintptr_t>(x) & 15) && smem8 <= 200 * 1024) {
+        if (smem8 > 48 * 1024)
+            cudaFuncSetAttribute(moe_router8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem8);
+        moe_router8_kernel<<<(unsigned)((M + kR8Tok - 1) / kR8Tok), 2 * kR8Tok, smem8, s>>>(x, Wg, active, M, D, best,
+                                                                                          pb, probs);
+        return launch_ok();
+    }
     size_t smem = sizeof(float) * ((size_t)kRouteTokens * 33 + 32 * E + (size_t)kRouteTokens * E);
     if (smem > 48 * 1024) cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     moe_router_kernel<<<(M + kRouteTokens - 1) / kRouteTokens, kRouteTokens, smem, s>>>(x, Wg, active, M, D, E, best,
@@ -281,6 +413,49 @@ __global__ void moe_hidden_grad_kernel(const T* __restrict__ hs, const T* __rest
     }
 }
 
+// bf16 form of the above for H a multiple of 256: lane l handles 8
+// consecutive columns of every 256-column step (16-byte loads and stores).
+__global__ void moe_hidden_grad_bf16x8_kernel(const __nv_bfloat16* __restrict__ hs,
+                                              const __nv_bfloat16* __restrict__ hpre,
+                                              const float* __restrict__ dpre2, const float* __restrict__ pbs,
+                                              const int* __restrict__ perm, int mpad, int H,
+                                              float* __restrict__ dpb, __nv_bfloat16* __restrict__ dH,
+                                              __nv_bfloat16* __restrict__ hp) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < mpad; p += gridDim.x * warps) {
+        const bool real = perm[p] >= 0;
+        const float pbv = pbs[p];
+        float acc = 0.f;
+        for (int a0 = 8 * lane; a0 < H; a0 += 256) {
+            const size_t i = (size_t)p * H + a0;
+            uint4 go = make_uint4(0, 0, 0, 0), ho = make_uint4(0, 0, 0, 0);
+            if (real) {
+                const uint4 hv = *reinterpret_cast<const uint4*>(hs + i);
+                const uint4 zv = *reinterpret_cast<const uint4*>(hpre + i);
+                const float4 d0 = *reinterpret_cast<const float4*>(dpre2 + i);
+                const float4 d1 = *reinterpret_cast<const float4*>(dpre2 + i + 4);
+                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&hv);
+                const __nv_bfloat16* z = reinterpret_cast<const __nv_bfloat16*>(&zv);
+                const float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+                __nv_bfloat16* g16 = reinterpret_cast<__nv_bfloat16*>(&go);
+                __nv_bfloat16* h16 = reinterpret_cast<__nv_bfloat16*>(&ho);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float hf = __bfloat162float(h[j]);
+                    acc += hf * d[j];
+                    g16[j] = __float2bfloat16_rn(d[j] * pbv * act_deriv(__bfloat162float(z[j]), kGeluMoe));
+                    h16[j] = __float2bfloat16_rn(hf * pbv);
+                }
+            }
+            *reinterpret_cast<uint4*>(dH + i) = go;
+            *reinterpret_cast<uint4*>(hp + i) = ho;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) dpb[p] = acc;
+    }
+}
+
 // linear experts: dpb = sum_j ys * dys (fp32), per sorted row
 __global__ void moe_rowdot_kernel(const float* __restrict__ a, const float* __restrict__ b, int mpad, int D,
                                   float* __restrict__ out) {
@@ -381,6 +556,7 @@ __global__ void moe_wg_reduce_kernel(const float* __restrict__ part, int chunks,
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     float s = 0.f;
+#pragma unroll 8
     for (int c = 0; c < chunks; c++) s += part[(size_t)c * n + i];
     out[i] = s;
 }
@@ -600,7 +776,11 @@ int moe_backward(ns_model* m, Op& op, int M) {
         g.ep.ld_c32 = H;
         if (gemm_run(m, g)) return -1;
         launch_counter() += 1;
-        if (dt == kBF16)
+        if (dt == kBF16 && H % 256 == 0)
+            moe_hidden_grad_bf16x8_kernel<<<rows_grid(mpad), 256, 0, st>>>(
+                (const __nv_bfloat16*)s->hs, (const __nv_bfloat16*)s->hpre, s->dpre2, s->pbs, s->perm, mpad, H,
+                s->dpb, (__nv_bfloat16*)s->dH, (__nv_bfloat16*)s->hp);
+        else if (dt == kBF16)
             moe_hidden_grad_kernel<__nv_bfloat16><<<rows_grid(mpad), 256, 0, st>>>(
                 (const __nv_bfloat16*)s->hs, (const __nv_bfloat16*)s->hpre, s->dpre2, s->pbs, s->perm, mpad, H,
                 s->dpb, (__nv_bfloat16*)s->dH, (__nv_bfloat16*)s->hp);

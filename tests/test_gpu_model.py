@@ -87,6 +87,23 @@ def test_c2_forward_full_batch_matches_oracle_tf32():
     assert np.all(np.isfinite(out))
 
 
+def test_c2_pipelined_host_inference_equals_one_pass():
+    """ns_eval_infer into page-locked host memory splits the batch into row
+    chunks and copies each chunk's output back while the next one computes;
+    rows are independent, so it matches the single-pass result (pageable
+    output) up to the fp32 summation order of a GEMM whose K is split at the
+    smaller row count."""
+    w = make_weights(C2, 311, default_sd=0.02)
+    tok = synth.tokens(64 * 256, 303, 8192)
+    m = nsb.Model(C2, w, precision="bf16")
+    one = m.infer(tok).copy()
+    pinned = torch.empty(64 * 256 * 512, dtype=torch.float32).pin_memory().numpy()
+    got = m.infer(tok, pinned).copy()
+    assert np.allclose(got, one, rtol=1e-5, atol=1e-5), float(np.max(np.abs(got - one)))
+    got2 = m.infer(tok, pinned)  # second call reuses the staging buffer and events
+    assert np.array_equal(got2, got)
+
+
 @pytest.mark.parametrize("tag", ["tmlp", "ttfm"])
 def test_train_fp32_matches_reference_runtime(tag):
     spec = SMALL[tag]
