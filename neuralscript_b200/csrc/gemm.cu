@@ -180,9 +180,9 @@ __device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float* v)
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         uint4 t;
-        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&t);
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&t);
 #pragma unroll
-        for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
+        for (int q = 0; q < 4; q++) h[q] = __floats2bfloat162_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
         reinterpret_cast<uint4*>(dst)[j] = t;
     }
 }
@@ -560,9 +560,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint4 g4[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&g4[j]);
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&g4[j]);
 #pragma unroll
-                for (int q = 0; q < 8; q++) h[q] = f2bf(v[8 * j + q]);
+                for (int q = 0; q < 4; q++) h[q] = __floats2bfloat162_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
             }
             stage_store(map, g4, col0, y);
         };
@@ -760,10 +760,9 @@ __device__ __forceinline__ float ld_op(const GemmOperand& o, long long i, long l
 
 // Narrow outputs (N <= 32, e.g. a 10-class head) with a K-major A: each
 // warp owns kNarrowRows rows of C; lane l takes the 8 consecutive k of
-// every 256-wide k step starting at 8 l (16-byte loads of bf16 A, all rows'
-// loads issued before the FMAs); B is staged in shared memory per step as
-// fp32, row k at k * NMAX + k / 8, so for every (j, n) the 32 lanes read 32
-// different banks; one butterfly reduction per output at the end.
+// every 256-wide k step starting at 8 l (one 16-byte load of bf16 A per
+// row, two for fp32); B is staged in shared memory per 256-k step as fp32
+// with an odd row stride; one butterfly reduction per output at the end.
 // For the tensor-core precision modes only: its summation order differs
 // from the k-sequential fp32 parity kernel.
 constexpr int kNarrowK = 256;
@@ -771,12 +770,10 @@ constexpr int kNarrowWarps = 8;
 constexpr int kNarrowRows = 4;
 template <int NMAX, typename TA>
 __global__ void __launch_bounds__(32 * kNarrowWarps) gemm_narrow_kernel(const SimtParams p) {
-    __shared__ float Bs[kNarrowK * NMAX + kNarrowK / 8];
+    __shared__ float Bs[kNarrowK * (NMAX + 1)];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x * kNarrowWarps + warp) * kNarrowRows;
     const TA* A = reinterpret_cast<const TA*>(p.a.ptr);
-    // 16-byte row segments: aligned base and a leading dimension of 16 bytes
-    const bool vec = !(reinterpret_cast<uintptr_t>(p.a.ptr) & 15) && (p.a.ld * (long long)sizeof(TA)) % 16 == 0;
     float acc[kNarrowRows][NMAX];
 #pragma unroll
     for (int r = 0; r < kNarrowRows; r++)
@@ -785,53 +782,41 @@ __global__ void __launch_bounds__(32 * kNarrowWarps) gemm_narrow_kernel(const Si
     for (int k0 = 0; k0 < p.K; k0 += kNarrowK) {
         const int kn = min(kNarrowK, p.K - k0);
         __syncthreads();
-        // all of this step's B loads in flight at once, then the stores
-        constexpr int kPer = kNarrowK * NMAX / (32 * kNarrowWarps);
-        float bv[kPer];
-#pragma unroll
-        for (int j = 0; j < kPer; j++) {
-            const int i = threadIdx.x + j * 32 * kNarrowWarps;
+        for (int i = threadIdx.x; i < kNarrowK * NMAX; i += blockDim.x) {
             const int kk = i / NMAX, n = i % NMAX;
-            bv[j] = (n < p.N && kk < kn) ? ld_op(p.b, n, k0 + kk) : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < kPer; j++) {
-            const int i = threadIdx.x + j * 32 * kNarrowWarps;
-            const int kk = i / NMAX;
-            Bs[kk * NMAX + i % NMAX + (kk >> 3)] = bv[j];
+            Bs[kk * (NMAX + 1) + n] = (n < p.N && kk < kn) ? ld_op(p.b, n, k0 + kk) : 0.f;
         }
         __syncthreads();
-        const int kl = 8 * lane;
-        float a[kNarrowRows][8];
+        const int kl = 8 * lane;  // this lane's 8 k within the step
+        if (kl >= kn) continue;
 #pragma unroll
         for (int r = 0; r < kNarrowRows; r++) {
             const int row = row0 + r;
-            const TA* src = A + (size_t)(row < p.M ? row : 0) * p.a.ld + k0 + kl;
-            const bool ok = row < p.M && kl < kn;
-            if (ok && kl + 8 <= kn && vec) {
+            if (row >= p.M) break;
+            float a[8];
+            const TA* src = A + (size_t)row * p.a.ld + k0 + kl;
+            if (kl + 8 <= kn) {
                 if constexpr (sizeof(TA) == 2) {
                     const uint4 t = *reinterpret_cast<const uint4*>(src);
                     const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&t);
 #pragma unroll
-                    for (int j = 0; j < 8; j++) a[r][j] = bf2f(h[j]);
+                    for (int j = 0; j < 8; j++) a[j] = bf2f(h[j]);
                 } else {
                     const float4 t0 = reinterpret_cast<const float4*>(src)[0];
                     const float4 t1 = reinterpret_cast<const float4*>(src)[1];
-                    a[r][0] = t0.x; a[r][1] = t0.y; a[r][2] = t0.z; a[r][3] = t0.w;
-                    a[r][4] = t1.x; a[r][5] = t1.y; a[r][6] = t1.z; a[r][7] = t1.w;
+                    a[0] = t0.x; a[1] = t0.y; a[2] = t0.z; a[3] = t0.w;
+                    a[4] = t1.x; a[5] = t1.y; a[6] = t1.z; a[7] = t1.w;
                 }
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; j++) a[r][j] = ok && kl + j < kn ? ld_any(src, p.a.dtype, j) : 0.f;
+                for (int j = 0; j < 8; j++) a[j] = kl + j < kn ? ld_any(src, p.a.dtype, j) : 0.f;
             }
-        }
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float* b = Bs + (kl + j) * NMAX + lane;  // (kl + j) / 8 == lane
+            for (int j = 0; j < 8; j++) {
+                const float* b = Bs + (kl + j) * (NMAX + 1);
 #pragma unroll
-            for (int n = 0; n < NMAX; n++)
-#pragma unroll
-                for (int r = 0; r < kNarrowRows; r++) acc[r][n] = fmaf(a[r][j], b[n], acc[r][n]);
+                for (int n = 0; n < NMAX; n++) acc[r][n] = fmaf(a[j], b[n], acc[r][n]);
+            }
         }
     }
 #pragma unroll
@@ -1166,9 +1151,11 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
 
 static int gemm_simt(const GemmDesc& d, cudaStream_t s) {
     SimtParams p;
-    // narrow kernel: K-major A
+    // narrow kernel: K-major A whose rows are 16-byte aligned
+    const int aes = d.a.dtype == kBF16 ? 2 : 4;
     const bool narrow = d.engine != kEngineSimt && d.groups == 1 && d.N <= 32 && !d.ep.out_rows &&
-                        !d.ep.col_block && !d.a.mn_major;
+                        !d.ep.col_block && !d.a.mn_major && (reinterpret_cast<uintptr_t>(d.a.ptr) & 15) == 0 &&
+                        (d.a.ld * aes) % 16 == 0;
     p.M = d.M;
     p.N = d.N;
     p.K = d.K;
