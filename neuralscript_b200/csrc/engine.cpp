@@ -1234,11 +1234,8 @@ static int newton_schulz(ns_model* m, float* X, int r, int c, int steps, float* 
     __nv_bfloat16* Bh = Ah + gram;
     const int dt = h ? kBF16 : kF32;
     launch_counter() += 2;
-    frob_normalize(X, (long long)r * c, 1e-7f, Y0, part, m->stream);
-    if (h) {
-        launch_counter() += 1;
-        if (act_fwd_f32(Y0, (size_t)r * c, kIdentity, nullptr, Y0h, m->stream)) return fail("bf16 copy failed");
-    }
+    if (frob_normalize(X, (long long)r * c, 1e-7f, Y0, part, m->stream, h ? Y0h : nullptr))
+        return fail("normalisation launch failed");
     const float a = 3.4445f, b = -4.7750f, cc = 2.0315f;
     float* cur = Y0;
     float* nxt = Y1;

@@ -1054,16 +1054,28 @@ int muon_apply(float* w, const float* o, float* m, long long n, float le, float 
     return launch_ok();
 }
 
-__global__ void sumsq_partial_kernel(const float* __restrict__ x, long long n, float* part) {
+// Frobenius normalisation out = x / (||x|| + eps): per-block partial sums
+// of squares, then a scaling pass that also writes the bf16 copy the
+// Newton-Schulz GEMMs read (when out16 is given). 16-byte accesses when n is
+// a multiple of 4 and the buffers are aligned.
+__global__ void sumsq_partial_kernel(const float* __restrict__ x, long long n, int vec, float* part) {
     __shared__ float sh[33];
     float acc = 0.f;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        acc += x[i] * x[i];
+    const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x, st = (long long)gridDim.x * blockDim.x;
+    if (vec) {
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (long long i = t0; i < n / 4; i += st) {
+            const float4 v = x4[i];
+            acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    } else {
+        for (long long i = t0; i < n; i += st) acc += x[i] * x[i];
+    }
     acc = block_sum(acc, sh);
     if (threadIdx.x == 0) part[blockIdx.x] = acc;
 }
-__global__ void scale_by_norm_kernel(const float* __restrict__ x, long long n, const float* part, int nparts, float eps,
-                                     float* out) {
+__global__ void scale_by_norm_kernel(const float* __restrict__ x, long long n, int vec, const float* part, int nparts,
+                                     float eps, float* __restrict__ out, __nv_bfloat16* __restrict__ out16) {
     __shared__ float inv;
     if (threadIdx.x == 0) {
         float s = 0.f;
@@ -1071,13 +1083,38 @@ __global__ void scale_by_norm_kernel(const float* __restrict__ x, long long n, c
         inv = 1.f / (sqrtf(s) + eps);
     }
     __syncthreads();
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        out[i] = x[i] * inv;
+    const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x, st = (long long)gridDim.x * blockDim.x;
+    if (vec) {
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (long long i = t0; i < n / 4; i += st) {
+            float4 v = x4[i];
+            v.x *= inv;
+            v.y *= inv;
+            v.z *= inv;
+            v.w *= inv;
+            reinterpret_cast<float4*>(out)[i] = v;
+            if (out16) {
+                uint2 h;
+                reinterpret_cast<__nv_bfloat162*>(&h)[0] = __floats2bfloat162_rn(v.x, v.y);
+                reinterpret_cast<__nv_bfloat162*>(&h)[1] = __floats2bfloat162_rn(v.z, v.w);
+                reinterpret_cast<uint2*>(out16)[i] = h;
+            }
+        }
+    } else {
+        for (long long i = t0; i < n; i += st) {
+            out[i] = x[i] * inv;
+            if (out16) out16[i] = f2bf(out[i]);
+        }
+    }
 }
-int frob_normalize(const float* x, long long n, float eps, float* out, float* scratch, cudaStream_t s) {
+int frob_normalize(const float* x, long long n, float eps, float* out, float* scratch, cudaStream_t s,
+                   __nv_bfloat16* out16) {
     const int parts = 512;
-    sumsq_partial_kernel<<<parts, 256, 0, s>>>(x, n, scratch);
-    scale_by_norm_kernel<<<grid_for((size_t)n, 256), 256, 0, s>>>(x, n, scratch, parts, eps, out);
+    auto al = [](const void* q, int b) { return !(reinterpret_cast<uintptr_t>(q) & (b - 1)); };
+    const int vec = n % 4 == 0 && al(x, 16) && al(out, 16) && (!out16 || al(out16, 8));
+    sumsq_partial_kernel<<<parts, 256, 0, s>>>(x, n, vec, scratch);
+    const size_t work = vec ? (size_t)n / 4 : (size_t)n;
+    scale_by_norm_kernel<<<grid_for(work, 256), 256, 0, s>>>(x, n, vec, scratch, parts, eps, out, out16);
     return launch_ok();
 }
 

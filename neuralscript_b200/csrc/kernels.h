@@ -96,6 +96,8 @@ int mgs_orthonormalize(float* G, int r, int c, cudaStream_t s);
 int muon_apply(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m,
                cudaStream_t s);
 // X /= (||X||_F + eps) as a two-kernel deterministic reduction; scratch >= 1024 floats.
-int frob_normalize(const float* x, long long n, float eps, float* out, float* scratch, cudaStream_t s);
+// out = x / (||x||_F + eps); out16 (optional) receives the same values in bf16
+int frob_normalize(const float* x, long long n, float eps, float* out, float* scratch, cudaStream_t s,
+                   __nv_bfloat16* out16 = nullptr);
 
 }  // namespace nsb
