@@ -1169,8 +1169,15 @@ static int optimizer_step(ns_model* m, float lr, const std::vector<char>* sel) {
                 muon_apply(W, m->d_m + w.off, m->d_m + w.off, (long long)w.count, le, mdec * lr, 1, m->stream);
             } else {
                 if (newton_schulz(m, m->d_m + w.off, w.rows, w.cols, (int)s.optv("steps", 5), m->d_o)) return -1;
+                // a flat bf16 working copy is written by the same pass
+                const WkTarget wt = working_target(m, (int)wi);
+                __nv_bfloat16* w16 = nullptr;
+                if (wt.dst && wt.rows == 1 && m->wdt == kBF16) {
+                    w16 = reinterpret_cast<__nv_bfloat16*>(wt.dst);
+                    fresh[wi] = 1;
+                }
                 launch_counter() += 1;
-                muon_apply(W, m->d_o, nullptr, (long long)w.count, le, mdec * lr, 0, m->stream);
+                muon_apply(W, m->d_o, nullptr, (long long)w.count, le, mdec * lr, 0, m->stream, w16);
             }
         } else {
             long long t = ++m->adam_t[wi];

@@ -1041,16 +1041,20 @@ int mgs_orthonormalize(float* G, int r, int c, cudaStream_t s) {
     return launch_ok();
 }
 
-__global__ void muon_apply_kernel(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m) {
+__global__ void muon_apply_kernel(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m,
+                                  __nv_bfloat16* __restrict__ w16) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const float wi = w[i];
-        w[i] = wi - (le * o[i] + decay_lr * wi);
+        const float wn = wi - (le * o[i] + decay_lr * wi);
+        w[i] = wn;
+        if (w16) w16[i] = f2bf(wn);
         if (zero_m) m[i] = 0.f;
     }
 }
-int muon_apply(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m, cudaStream_t s) {
+int muon_apply(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m, cudaStream_t s,
+               __nv_bfloat16* w16) {
     if (n <= 0) return 0;
-    muon_apply_kernel<<<grid_for((size_t)n, 256), 256, 0, s>>>(w, o, m, n, le, decay_lr, zero_m);
+    muon_apply_kernel<<<grid_for((size_t)n, 256), 256, 0, s>>>(w, o, m, n, le, decay_lr, zero_m, w16);
     return launch_ok();
 }
 

@@ -92,9 +92,10 @@ int muon_momentum(float* m, const float* g, long long n, float momentum, cudaStr
 // Modified Gram-Schmidt on an r x c matrix in place (columns if r >= c,
 // rows otherwise), one CTA per matrix.
 int mgs_orthonormalize(float* G, int r, int c, cudaStream_t s);
-// w -= le * o + (decay * lr) * w ; then (if zero_m) m = 0
+// w -= le * o + (decay * lr) * w ; then (if zero_m) m = 0; w16 (optional)
+// receives the updated weights in bf16 (a flat working copy)
 int muon_apply(float* w, const float* o, float* m, long long n, float le, float decay_lr, int zero_m,
-               cudaStream_t s);
+               cudaStream_t s, __nv_bfloat16* w16 = nullptr);
 // X /= (||X||_F + eps) as a two-kernel deterministic reduction; scratch >= 1024 floats.
 // out = x / (||x||_F + eps); out16 (optional) receives the same values in bf16
 int frob_normalize(const float* x, long long n, float eps, float* out, float* scratch, cudaStream_t s,
