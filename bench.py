@@ -1,21 +1,27 @@
 """Benchmark: NeuralScript CUDA-backend hot path on B200.
 
-Default workload (configs[1] of BASELINE.json): the config-2 transformer block
-forward through ns_eval_infer, tokens [64, 256] per GPU, bf16 tensor cores,
-random-init weights N(0, 0.02), synthetic token ids (seeded). With
---config c4 it times the config-4 AOT train step (block + 512->8192 head, CE,
-AdamW, cosine schedule) instead.
+Default workload (configs[3] of BASELINE.json, the train step the metric
+names and the one path with a collective): the config-4 AOT train step
+through ns_runtime_train_step (config-2 block + 512->8192 head,
+cross-entropy, AdamW 0.9/0.95 wd 0.1, cosine warm-up schedule), 64 x 256
+tokens per GPU, bf16 tensor cores, random-init weights N(0, 0.02), synthetic
+token ids and targets (seeded). --config c1|c2|c3|c5 times the other
+configurations, each in its contract precision (c1 and c3 TF32, the rest
+bf16; --precision overrides).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c4] [--impl b200|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1..c5] [--impl b200|reference]
 
-N > 1 runs under torchrun, one process per GPU: inference is replicated
-(each rank its own batch, no collective; "scaling": "weak"); the train step
-all-reduces gradients over NCCL. Timing: per-step CUDA events on the stream
-the engine is driven from, L2 flushed between steps (a 512 MB write outside
-the timed events), max over ranks. `e2e` times the reference-facing C-ABI
-call (ns_eval_infer / ns_runtime_train_step) with host buffers, copies
-included. `--impl reference` times the reference's own CPU code
-(oracle/_ref, emitted by the reference compiler) on this host's cores.
+N > 1 runs under torchrun, one process per GPU: the train step shards the
+batch (each rank 64 x 256 tokens, "scaling": "weak") and all-reduces the
+gradients over NCCL; inference configurations run replicas. Timing: per-step
+CUDA events on the stream the engine is driven from, L2 flushed between
+steps (a 512 MB write outside the timed events), max over ranks. `e2e` times
+the reference-facing call itself, by its reference name in the per-model
+library libns_<config>.so (ns_runtime_train_step with dense one-hot fp32
+labels for c4, ns_eval_infer for c1/c2), host buffers in page-locked
+memory, copies included. `--impl reference` times the reference's own CPU
+code (oracle/_ref: translation units the reference compiler emitted,
+compiled with -O3 -march=native on the measuring host) on all host cores.
 """
 import argparse
 import json
@@ -32,6 +38,38 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# Contract precision per configuration: the mode whose forward activations
+# stay within the 2e-3 bound (c1, c3: TF32; bf16 rounding alone puts their
+# chained GEMMs above it) or whose losses track the fp32 reference within
+# 1e-3 (c4, c5), and the c2 block output (7.6e-4 from fp32 in bf16).
+DEFAULT_PRECISION = {"c1": "tf32", "c2": "bf16", "c3": "tf32", "c4": "bf16", "c5": "bf16"}
+
+
+def ref_lib(name):
+    """The reference's emitted CPU unit for `name` as a shared library built
+    for this host (-O3 -march=native, into a per-host temp directory), or the
+    prebuilt portable one (-O3 -march=x86-64-v3) when no compiler is found.
+    Returns (path, build description) or (None, None)."""
+    import shutil
+    import tempfile
+    src = os.path.join(ROOT, "oracle", "_ref", f"{name}.cpp")
+    pre = os.path.join(ROOT, "oracle", "_ref", f"libref_{name}.so")
+    if os.path.exists(src) and shutil.which("g++"):
+        d = os.path.join(tempfile.gettempdir(), "nsb_ref_native")
+        os.makedirs(d, exist_ok=True)
+        out = os.path.join(d, f"libref_{name}.so")
+        if not os.path.exists(out) or os.path.getmtime(out) < os.path.getmtime(src):
+            tmp = out + f".{os.getpid()}"
+            r = subprocess.run(["g++", "-std=c++17", "-O3", "-march=native", "-fPIC", "-shared", src, "-o", tmp],
+                               capture_output=True, text=True)
+            if r.returncode == 0:
+                os.replace(tmp, out)
+        if os.path.exists(out):
+            return out, "g++ -O3 -march=native (reference emit compiled on this host)"
+    if os.path.exists(pre):
+        return pre, "g++ -O3 -march=x86-64-v3 (prebuilt reference emit)"
+    return None, None
 
 
 def peaks():
@@ -143,41 +181,58 @@ def dist_env():
 _REF = {}
 
 
-def _ref_init(lib_path):
-    """Worker initialiser: load the reference library and build one model."""
+def _ref_init(lib_path, kind):
+    """Worker initialiser: load the reference library and build one model
+    (c2: the config-2 block; c4: the config-4 block without residuals, the
+    form the reference can train) with N(0, 0.02) weights."""
     import ctypes as C
     L = C.CDLL(lib_path)
     L.ns_runtime_init.restype = C.c_void_p
     L.ns_runtime_init.argtypes = [C.c_void_p, C.c_size_t]
     L.ns_eval_infer.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]
+    L.ns_weight_count_static.restype = C.c_size_t
     from neuralscript_b200 import synth
-    from neuralscript_b200.spec import C2, parse
-    s = parse(C2)
-    w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
-    _REF.update(L=L, m=L.ns_runtime_init(w.ctypes.data, w.size), w=w, out=np.empty(256 * 512, np.float32))
+    n = L.ns_weight_count_static()
+    w = synth.normal(n, 311, 0.0, 0.02)
+    _REF.update(L=L, kind=kind, m=L.ns_runtime_init(w.ctypes.data, w.size), w=w)
+    if kind == "c2":
+        _REF["out"] = np.empty(256 * 512, np.float32)
+    else:
+        L.ns_runtime_train_step.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_float),
+                                            C.c_float]
+        L.ns_objective_loss.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_float)]
+        _REF["loss"] = C.c_float(0)
 
 
-def _ref_run(seed):
-    """One 256-token sequence through the reference ns_eval_infer."""
+def _ref_run(job):
+    """One 256-token sequence through the reference: its ns_eval_infer (c2),
+    its ns_runtime_train_step (c4 step) or its ns_objective_loss (c4 warm-up:
+    the forward only). Returns the call's wall time."""
+    import ctypes as C
     from neuralscript_b200 import synth
+    seed, what = job
     tok = synth.tokens(256, seed, 8192)
+    L, m = _REF["L"], _REF["m"]
+    if _REF["kind"] == "c2":
+        t0 = time.perf_counter()
+        L.ns_eval_infer(m, tok.ctypes.data, _REF["out"].ctypes.data, 256)
+        return time.perf_counter() - t0
+    y = synth.one_hot(synth.tokens(256, seed + 1, 8192), 8192)
     t0 = time.perf_counter()
-    _REF["L"].ns_eval_infer(_REF["m"], tok.ctypes.data, _REF["out"].ctypes.data, 256)
+    if what == "train":
+        L.ns_runtime_train_step(m, tok.ctypes.data, y.ctypes.data, 256, C.byref(_REF["loss"]), C.c_float(3e-4))
+    else:
+        L.ns_objective_loss(m, tok.ctypes.data, y.ctypes.data, 256, C.byref(_REF["loss"]))
     return time.perf_counter() - t0
 
 
-def ref_lib_path():
-    p = os.path.join(ROOT, "oracle", "_ref", "libref_c2.so")
-    return p if os.path.exists(p) else None
-
-
 def ref_abi_rows_per_s(name, w, rows, in_cols, out_cols):
-    """Reference CPU emit (oracle/_ref/libref_<name>.so) through its own
-    ns_eval_infer on `rows` rows, one core: rows/s."""
+    """Reference CPU emit (libref_<name>.so) through its own ns_eval_infer on
+    `rows` rows, one core: rows/s."""
     import ctypes as C
     from neuralscript_b200 import synth
-    p = os.path.join(ROOT, "oracle", "_ref", f"libref_{name}.so")
-    if not os.path.exists(p):
+    p, build = ref_lib(name)
+    if p is None:
         return None
     L = C.CDLL(p)
     L.ns_runtime_init.restype = C.c_void_p
@@ -193,7 +248,8 @@ def ref_abi_rows_per_s(name, w, rows, in_cols, out_cols):
     dt = time.perf_counter() - t0
     L.ns_free(m)
     return {"value": rows / dt, "unit": "rows/s", "cores": 1, "kind": "reference",
-            "sample": f"{rows} rows through the reference CPU emit's ns_eval_infer (libref_{name}.so), 1 core"}
+            "sample": f"{rows} rows through the reference CPU emit's ns_eval_infer (libref_{name}.so, {build}), "
+                      "1 core"}
 
 
 def _oracle():
@@ -247,33 +303,31 @@ def oracle_mlp_rows_per_s(rows_step):
 
 
 class RefPool:
-    """Reference CPU emit for config 2 on `workers` processes (the emitted
-    code is single-threaded and keeps file-scope buffers, so parallelism is
-    one process per core, each on whole 256-token sequences: the reference
-    attends over one call, so one call per sequence is the per-sequence
-    semantics)."""
+    """The reference's CPU emit on `workers` processes, one per core (the
+    emitted code is single-threaded): each worker holds one model and runs
+    whole 256-token sequences, one call per sequence (the reference attends
+    over one call, so one call per sequence is the per-sequence semantics)."""
 
-    def __init__(self, workers):
+    def __init__(self, workers, path, kind):
         import multiprocessing as mp
         self.workers = workers
-        path = ref_lib_path()
         if workers == 1:
-            _ref_init(path)
+            _ref_init(path, kind)
             self.pool = None
         else:
-            self.pool = mp.get_context("spawn").Pool(workers, initializer=_ref_init, initargs=(path,))
-            self.pool.map(_ref_run, range(workers))  # warm every worker
+            self.pool = mp.get_context("spawn").Pool(workers, initializer=_ref_init, initargs=(path, kind))
 
-    def step(self, seqs_per_worker=1, seed=9001):
-        n = self.workers * seqs_per_worker
+    def step(self, seed, what="run"):
+        """Every worker runs one sequence; returns (tokens/s, wall seconds)."""
+        jobs = [(seed + q, what) for q in range(self.workers)]
         t0 = time.perf_counter()
         if self.pool is None:
-            for q in range(n):
-                _ref_run(seed + q)
+            for j in jobs:
+                _ref_run(j)
         else:
-            self.pool.map(_ref_run, range(seed, seed + n))
+            self.pool.map(_ref_run, jobs, chunksize=1)
         dt = time.perf_counter() - t0
-        return 256 * n / dt, dt
+        return 256 * self.workers / dt, dt
 
     def close(self):
         if self.pool is not None:
@@ -291,10 +345,6 @@ def run_reference_other(args):
     from neuralscript_b200 import synth
     from neuralscript_b200.spec import CONFIGS, parse
     cfg = args.config
-    if cfg == "c4":
-        print(json.dumps({"impl": "reference", "unavailable": "the reference CPU emit cannot train the config-4 "
-                          "residual block (its + has no backward); config 2 is the reference arm"}))
-        return 0
     s = parse(CONFIGS[cfg])
     if cfg == "c1":
         w = np.concatenate([synth.normal(c, 311 + i, 0.0, float(r) ** -0.5)
@@ -317,36 +367,62 @@ def run_reference_other(args):
     return 0
 
 
+# One reference train call on a 256-token sequence takes about a minute on
+# one core (its Gram-Schmidt optimizer alone is ~12 GFLOP per call), so the
+# config-4 reference arm runs at most this many timed steps, every core on
+# its own sequence in each.
+REF_C4_MAX_STEPS = 2
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    if args.config != "c2":
+    if args.config not in ("c2", "c4"):
         return run_reference_other(args)
-    metric, unit = "tokens_per_s_ns_eval_infer_c2", "tokens/s"
-    if ref_lib_path() is None:
+    cfg = args.config
+    name = "c2" if cfg == "c2" else "c4ref"
+    path, build = ref_lib(name)
+    if path is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (reference sources absent)"}))
         return 0
     cores = os.cpu_count() or 1
-    pool = RefPool(cores)
-    for w in range(min(args.warmup, 1)):
-        pool.step(1, 5000 + w)
+    pool = RefPool(cores, path, cfg)
+    if cfg == "c2":
+        metric = "tokens_per_s_ns_eval_infer_c2"
+        warm, steps = args.warmup, args.steps
+        for w in range(warm):
+            pool.step(5000 + w * cores)
+        what = "run"
+        workload = ("config 2 transformer block forward, the reference CPU emit (nsc --cpp --runtime, " + build +
+                    "), one ns_eval_infer call per 256-token sequence")
+    else:
+        metric = "tokens_per_s_ns_runtime_train_step_c4"
+        # warm-up: the forward only (pages in code and buffers; a train call
+        # would take a minute per step)
+        warm, steps = min(args.warmup, 1), min(args.steps, REF_C4_MAX_STEPS)
+        for w in range(warm):
+            pool.step(5000 + w * cores, "objective")
+        what = "train"
+        workload = ("config 4 block without its residual adds (the reference cannot backpropagate through +) "
+                    "+ 512->8192 head + cross-entropy, the reference CPU emit's ns_runtime_train_step (" + build +
+                    ", its optimizer: Gram-Schmidt Muon on every matrix), one call per 256-token sequence; "
+                    "tokens/s of one 64-sequence step = 256 tokens / call time")
     vals, tot = [], 0.0
-    for i in range(args.steps):
-        v, dt = pool.step(1, 9001 + i * cores)
+    for i in range(steps):
+        v, dt = pool.step(9001 + i * cores, what)
         vals.append(v)
         tot += dt
     pool.close()
     v = float(np.median(vals))
-    line = {"impl": "reference", "metric": metric, "value": v, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * tot / max(args.steps, 1), "higher_is_better": True,
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": warm, "ms_per_step": 1000.0 * tot / max(steps, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config 2 transformer block forward, reference CPU emit (nsc --cpp --runtime, "
-                                   "g++ -O3 -march=x86-64-v3), one ns_eval_infer call per 256-token sequence",
-                       "seq_len": 256, "tokens_per_step": 256 * cores},
-            "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": "reference",
+            "config": {"workload": workload, "seq_len": 256, "tokens_per_step": 256 * cores,
+                       "steps_requested": args.steps, "warmup_requested": args.warmup},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference",
                              "sample": f"{cores} sequences of 256 tokens per step, one process per core"},
-            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
 
@@ -401,8 +477,9 @@ def region_work(spec, label, M, train, world=1):
         return None, 0
     k = l.kind
     bwd = phase == "bwd"
-    # a layer reading the network input computes no input gradient
-    first = any(o.fn == lname and o.args and o.args[0] == "x" for o in s.ops)
+    # a layer reading the network input computes no input gradient, unless
+    # the spec asks for it (`grad input`)
+    first = not s.input_grad and any(o.fn == lname and o.args and o.args[0] == "x" for o in s.ops)
     if k == "dense":
         f = 2.0 * M * l.i("in") * l.i("out")
         return "flops", (f if first else 2 * f) if bwd else f
@@ -447,6 +524,7 @@ def _randn(n, seed, sd):
 def setup_workload(args, rank, world, dist):
     """Model, device inputs, the timed step and the end-to-end call of one
     benchmark configuration (synthetic, seeded)."""
+    import ctypes as C
     import torch
     import neuralscript_b200 as nsb
     from neuralscript_b200 import synth
@@ -455,34 +533,64 @@ def setup_workload(args, rank, world, dist):
 
     cfg = args.config
     spec = CONFIGS[cfg]
-    W = NS(cfg=cfg, seq_len=None, labels_kind=None, cpu=None)
+    W = NS(cfg=cfg, seq_len=None, labels_kind=None, cpu=None, e2e_extra=None)
+    s = parse(spec)
     if cfg in ("c2", "c4"):
-        s = parse(spec)
         w = np.concatenate([synth.normal(c, 311 + i, 0.0, 0.02) for i, (_, _, c, _) in enumerate(s.layout())])
     elif cfg == "c1":
         # N(0, 1/fan_in) weights (sd = fan_in^-1/2), no biases, dropout off
-        s = parse(spec)
         w = np.concatenate([synth.normal(c, 311 + i, 0.0, float(r) ** -0.5)
                             for i, (_, _, c, (r, _)) in enumerate(s.layout())])
     elif cfg == "c3":
-        # the MoE layer trained on MSE against N(0,1) targets: forward, dWg,
-        # dWe1, dWe2 (the input gradient of the network input is not formed)
-        spec = spec + "loss mse\noptimizer adamw\n"
-        s = parse(spec)
+        # the MoE layer trained on MSE against N(0,1) targets: forward, dX,
+        # dWg, dWe1, dWe2 (the spec's `grad input` forms dX) and AdamW
         w = np.concatenate([_randn(c, 311 + i, 0.02 if i == 0 else 1.0 / 32)
                             for i, (_, _, c, _) in enumerate(s.layout())])
     else:  # c5: fp32 master weights N(0, (1/64)^2), Muon NS-5, MSE
-        s = parse(spec)
         w = np.concatenate([_randn(c, 311 + i, 1.0 / 64) for i, (_, _, c, _) in enumerate(s.layout())])
     model = nsb.Model(spec, w, precision=args.precision)
     W.spec, W.model = spec, model
     train = cfg in ("c3", "c4", "c5")
     W.train = train
-    if train and world > 1:
+
+    def join(handle):
         uid = nsb.dist_unique_id() if rank == 0 else bytes(128)
         obj = [uid]
         dist.broadcast_object_list(obj, src=0)
-        model.dist_init(rank, world, obj[0], 120000)
+        buf = C.create_string_buffer(obj[0], 128)
+        if nsb.lib().nsb_dist_init(handle, rank, world, buf, 120000) != 0:
+            raise RuntimeError("dist_init failed: " + nsb.last_error())
+
+    if train and world > 1:
+        join(model.handle)
+
+    # The reference-facing call for e2e: the per-model library's own
+    # ns_runtime_init / ns_eval_infer / ns_runtime_train_step, on a second
+    # model with the same weights and precision.
+    RL = nsb.RuntimeLib(cfg)
+    h = RL.ns_runtime_init(w.ctypes.data, w.size)
+    if not h:
+        raise RuntimeError("ns_runtime_init failed: " + nsb.last_error())
+    if nsb.lib().nsb_set_precision(h, nsb.PRECISION[args.precision]) != 0:
+        raise RuntimeError("set_precision failed: " + nsb.last_error())
+    if train and world > 1:
+        join(h)
+    W.e2e_handle, W.e2e_lib = h, RL
+    e2e_loss = C.c_float(0)
+
+    def abi_train(x_h, y_h, lr):
+        def f():
+            if RL.ns_runtime_train_step(h, C.c_void_p(x_h.ctypes.data), C.c_void_p(y_h.ctypes.data), x_h.size,
+                                        C.byref(e2e_loss), C.c_float(lr)) != 0:
+                raise RuntimeError("ns_runtime_train_step failed: " + nsb.last_error())
+        return f
+
+    def abi_infer(x_h, out_h):
+        def f():
+            if RL.ns_eval_infer(h, C.c_void_p(x_h.ctypes.data), C.c_void_p(out_h.ctypes.data), x_h.size) != 0:
+                raise RuntimeError("ns_eval_infer failed: " + nsb.last_error())
+        return f
+
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
@@ -498,37 +606,53 @@ def setup_workload(args, rank, world, dist):
             if args.one_hot:
                 labels = torch.zeros(M, 8192, device="cuda")
                 labels[torch.arange(M), tgt.long()] = 1.0
-            W.labels_kind = "one-hot" if args.one_hot else "int32 targets"
+            W.labels_kind = "one-hot fp32 on the device" if args.one_hot else "int32 targets on the device"
             W.step = lambda: model.train_step_device(tok, labels=labels, targets=None if labels is not None else tgt,
                                                      lr=3e-4, stream=sp, want_loss=False)
             tgt_h = tgt.cpu().pin_memory().numpy()
-            y1h = None
-            if args.e2e_one_hot:
-                y1h = torch.zeros(M, 8192).pin_memory().numpy()
-                y1h[np.arange(M), tgt_h] = 1.0
-            W.e2e_fn = (lambda: model.train_step(tok_h, y1h, 3e-4)) if y1h is not None else \
-                (lambda: model.train_step_idx(tok_h, tgt_h, 3e-4))
-            W.h2d = tok_h.nbytes + (y1h.nbytes if y1h is not None else tgt_h.nbytes)
+            # e2e: the reference ABI takes dense one-hot fp32 labels [M, 8192]
+            y1h = torch.zeros(M, 8192).pin_memory().numpy()
+            y1h[np.arange(M), tgt_h] = 1.0
+            W.e2e_fn = abi_train(tok_h, y1h, 3e-4)
+            W.h2d = tok_h.nbytes + y1h.nbytes
             W.d2h = 4
+            W.e2e_kind = "libns_c4.so ns_runtime_train_step, one-hot fp32 labels"
+            # the index-label extension (int32 targets instead of the one-hot blob)
+            W.e2e_extra = ("e2e_index_labels", lambda: model.train_step_idx(tok_h, tgt_h, 3e-4),
+                           tok_h.nbytes + tgt_h.nbytes, 4)
             W.metric = "tokens_per_s_ns_runtime_train_step_c4"
             W.workload = "config 4 AOT train step (c2 block + 512->8192 head, CE, AdamW, cosine)"
             W.flops_per_row = c4_flops_per_token()
+            if args.cpu_baseline and rank == 0:
+                def cpu():
+                    path, build = ref_lib("c4ref")
+                    if path is None:
+                        return None
+                    pool = RefPool(1, path, "c4")
+                    v, dt = pool.step(9001, "train")
+                    return {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                            "sample": "one 256-token sequence through the reference CPU emit's ns_runtime_train_step "
+                                      f"(config 4 without residual adds, {build}), 1 core, {dt:.1f} s"}
+                W.cpu = cpu
         else:
             out = torch.empty(M, 512, device="cuda")
             W.step = lambda: model.infer_device(tok, out, stream=sp)
             out_h = torch.empty(M * 512, dtype=torch.float32).pin_memory().numpy()
-            W.e2e_fn = lambda: model.infer(tok_h, out_h)
+            W.e2e_fn = abi_infer(tok_h, out_h)
+            W.e2e_kind = "libns_c2.so ns_eval_infer"
             W.h2d, W.d2h = tok_h.nbytes, M * 512 * 4
             W.metric = "tokens_per_s_ns_eval_infer_c2"
             W.workload = "config 2 transformer block forward (ns_eval_infer)"
             W.flops_per_row = c2_flops_per_token()
-            if args.cpu_baseline and rank == 0 and ref_lib_path():
+            if args.cpu_baseline and rank == 0:
                 def cpu():
-                    pool = RefPool(1)
-                    v, _ = pool.step(8, 9001)
-                    return None if v is None else {
-                        "value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
-                        "sample": "8 sequences x 256 tokens through the reference CPU emit (libref_c2.so), 1 core"}
+                    path, build = ref_lib("c2")
+                    if path is None:
+                        return None
+                    pool = RefPool(1, path, "c2")
+                    tot = sum(pool.step(9001 + q)[1] for q in range(8))
+                    return {"value": 8 * 256 / tot, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                            "sample": f"8 sequences x 256 tokens through the reference CPU emit ({build}), 1 core"}
                 W.cpu = cpu
         W.M, W.global_batch = M, B * world
         return W
@@ -540,7 +664,8 @@ def setup_workload(args, rank, world, dist):
         W.step = lambda: model.infer_device(x, out, stream=sp)
         x_h = x.cpu().pin_memory().numpy()
         out_h = torch.empty(M * outc, dtype=torch.float32).pin_memory().numpy()
-        W.e2e_fn = lambda: model.infer(x_h, out_h)
+        W.e2e_fn = abi_infer(x_h, out_h)
+        W.e2e_kind = "libns_c1.so ns_eval_infer"
         W.h2d, W.d2h = x_h.nbytes, M * outc * 4
         W.metric = "rows_per_s_ns_eval_infer_c1"
         W.workload = "config 1 MLP 784-1024-1024-10 ReLU forward (ns_eval_infer), batch 4096"
@@ -554,15 +679,16 @@ def setup_workload(args, rank, world, dist):
         y = torch.randn(M, cols, device="cuda", generator=g)
         W.step = lambda: model.train_step_device(x, labels=y, lr=1e-4, stream=sp, want_loss=False)
         x_h, y_h = x.cpu().pin_memory().numpy(), y.cpu().pin_memory().numpy()
-        W.e2e_fn = lambda: model.train_step(x_h, y_h, 1e-4)
+        W.e2e_fn = abi_train(x_h, y_h, 1e-4)
+        W.e2e_kind = f"libns_{cfg}.so ns_runtime_train_step, fp32 MSE targets"
         W.h2d, W.d2h = x_h.nbytes + y_h.nbytes, 4
         W.labels_kind = "fp32 N(0,1) targets (MSE)"
         if cfg == "c3":
             D, E, F = 1024, 8, 1024
             W.metric = "tokens_per_s_moe_train_step_c3"
             W.workload = ("config 3 top-1 MoE layer (D 1024, 8 experts, FFN 1024) forward + backward "
-                          "(dWg, dWe1, dWe2) + AdamW, MSE against N(0,1) targets")
-            W.flops_per_row = 2 * D * E * 2 + 10 * D * F
+                          "(dX, dWg, dWe1, dWe2) + AdamW, MSE against N(0,1) targets")
+            W.flops_per_row = 2 * D * E * 2 + 12 * D * F
             if args.cpu_baseline and rank == 0:
                 W.cpu = lambda: oracle_moe_tokens_per_s(w, 64)
         else:
@@ -637,7 +763,24 @@ def run_b200(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e = {"value": tokens_step / e2e_s, "unit": unit, "h2d_bytes_per_step": int(W.h2d),
-           "d2h_bytes_per_step": int(W.d2h)}
+           "d2h_bytes_per_step": int(W.d2h), "call": W.e2e_kind}
+    e2e_extra = None
+    if W.e2e_extra:
+        key, fn, bi, bo = W.e2e_extra
+        for _ in range(2):
+            fn()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            fn()
+        es = (time.perf_counter() - t0) / n_e2e
+        if world > 1:
+            t = torch.tensor([es], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            es = float(t.item())
+        e2e_extra = (key, {"value": tokens_step / es, "unit": unit, "h2d_bytes_per_step": int(bi),
+                           "d2h_bytes_per_step": int(bo)})
 
     # per-region device time inside the engine (CUDA events on the engine
     # stream) over the same number of steps; the dominant region's kernel is
@@ -705,10 +848,14 @@ def run_b200(args):
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": int(launches) * args.steps,
         }
+        if e2e_extra:
+            result[e2e_extra[0]] = e2e_extra[1]
         print(json.dumps(result))
     if world > 1:
         dist.barrier()
-        model.close()
+    W.e2e_lib.ns_free(W.e2e_handle)
+    model.close()
+    if world > 1:
         dist.destroy_process_group()
     return 0
 
@@ -719,13 +866,15 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
-    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--precision", default=None, choices=["bf16", "tf32", "fp32"],
+                    help="default: the configuration's contract precision")
     ap.add_argument("--one-hot", action="store_true", help="c4: dense one-hot labels on the device path")
-    ap.add_argument("--e2e-one-hot", action="store_true", help="c4: e2e through the one-hot ABI")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.precision is None:
+        args.precision = DEFAULT_PRECISION[args.config]
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)

@@ -85,6 +85,13 @@ int nsb_train_step_device(ns_model* m, const float* d_input, const float* d_labe
  * over ranks when data-parallel), copied to host `out` of n floats. */
 int nsb_model_get_gradients(const ns_model* m, float* out, size_t n);
 
+/* Gradient of the loss with respect to the network input of the last train
+ * step (rows x input width floats, this rank's rows), for specs with a
+ * `grad input` statement. The reference forms it inside ns_moe_grad_x /
+ * ns_matmul_grad_a (src/codegen/codegen.cpp:1318-1326, 1388-1443) but keeps
+ * it internal; here it can be read back, e.g. by a caller chaining layers. */
+int nsb_model_get_input_gradient(const ns_model* m, float* out, size_t n);
+
 /* Per-region timing: CUDA events recorded on the model's stream around every
  * forward op (attention split into qkv / core / out), every backward op,
  * the loss, the all-reduce and the optimizer. enable != 0 switches it on and

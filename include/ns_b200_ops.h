@@ -65,7 +65,9 @@ int nsb_op_embedding_bwd(const float* dout, const float* ids, int M, int V, int 
  * Its sort scratch is a fixed array in the library's device memory, so it
  * calls no cudaMalloc, cudaFree or allocating library routine.
  * Limits: M <= 262144 rows and V <= 65536 vocabulary rows; larger sizes
- * return -2 without launching anything. Every GPU that loads the library
+ * return -2 without launching anything. The work runs on the current device:
+ * a non-NULL `stream` must belong to it (otherwise -4, nothing launched).
+ * Every GPU that loads the library
  * holds the 1.75 MB array until the process exits. The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, once per
  * device, with that device current); make that first call before any CUDA
@@ -124,6 +126,44 @@ int nsb_op_moe_route(const float* x, const float* Wg, const unsigned char* activ
  * ns_act_grad_kernel (cuda_backend.cpp:80-84, 468-472). */
 int nsb_op_act_fwd(const float* x, size_t n, int act, float* out32, void* out16, void* stream);
 int nsb_op_act_bwd(const float* dy, const float* z, int act, size_t n, float* out32, void* stream);
+
+/* Row softmax (max-subtracted, exp, normalised). Replaces ns_softmax_kernel
+ * (cuda_backend.cpp:432-441) / ns_softmax (codegen.cpp CPU helper). */
+int nsb_op_softmax(const float* x, int M, int C, float* out32, void* out16, void* stream);
+
+/* out = a (op) b over n elements, code 0 + 1 - 2 * 3 /, full-size b.
+ * Replaces ns_binop_kernel (cuda_backend.cpp:408-419) / ns_binop
+ * (codegen.cpp:1267-1278). The backward (no reference counterpart: the
+ * reference has no binop gradient) writes da and/or db (either may be NULL). */
+int nsb_op_binop(const float* a, const float* b, size_t n, int code, float* out32, void* out16, void* stream);
+int nsb_op_binop_bwd(const float* dout, const float* a, const float* b, size_t n, int code, float* da, float* db,
+                     void* stream);
+
+/* Inverted dropout with a counter-based mask: element i keeps its value with
+ * probability 1 - rate (scaled by 1/(1 - rate)), decided by Philox4x32-10 of
+ * (i, step, site) under key (key0, key1); the backward regenerates the same
+ * mask. Replaces ns_dropout_fwd_kernel / ns_dropout_mul_kernel
+ * (cuda_backend.cpp:778-793), whose curand mask (and the CPU emit's
+ * std::mt19937 mask, codegen.cpp:2874-2893) it does not reproduce. */
+int nsb_op_dropout_fwd(const float* x, size_t n, float rate, unsigned key0, unsigned key1, unsigned step,
+                       unsigned site, float* out32, void* out16, void* stream);
+int nsb_op_dropout_bwd(const float* dy, size_t n, float rate, unsigned key0, unsigned key1, unsigned step,
+                       unsigned site, float* dx, void* stream);
+
+/* Data movement on row-major fp32 tensors. axis 1: column forms on [rows,
+ * cols]; axis 0: row forms. Indices are int64. A scatter keeps the last
+ * update of a repeated index (the reference CPU helpers' order); an index
+ * outside the source reads 0. Replace ns_transpose2d_kernel,
+ * ns_concat2/0_kernel, ns_slice2/slicerows_kernel, ns_index/indexrows_kernel
+ * and ns_scatter/scatterrows_kernel (cuda_backend.cpp:93-171). */
+int nsb_op_transpose(const float* in, int R, int C, float* out, void* stream);
+int nsb_op_concat(const float* a, const float* b, int axis, int rows_a, int rows_b, int ca, int cb, float* out,
+                  void* stream);
+int nsb_op_slice(const float* in, int axis, int rows, int cols, int start, int end, float* out, void* stream);
+int nsb_op_index(const float* in, int axis, int rows, int cols, const long long* idx, int L, float* out,
+                 void* stream);
+int nsb_op_scatter(const float* in, int axis, int rows, int cols, const long long* idx, int L, const float* upd,
+                   float* out, void* stream);
 
 #ifdef __cplusplus
 }

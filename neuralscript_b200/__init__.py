@@ -79,6 +79,7 @@ def lib() -> C.CDLL:
                                             C.c_float, C.c_void_p]),
         "nsb_last_launch_count": (C.c_longlong, [C.c_void_p]),
         "nsb_model_get_gradients": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+        "nsb_model_get_input_gradient": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
         "nsb_region_timing": (C.c_int, [C.c_void_p, C.c_int]),
         "nsb_region_count": (C.c_int, [C.c_void_p]),
         "nsb_region_get": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_double),
@@ -126,6 +127,7 @@ class Model:
         self.spec_text = spec_text
         self.spec = parse(spec_text)
         w = np.ascontiguousarray(weights, dtype=np.float32).reshape(-1)
+        self._last_rows = 0
         self._h = lib().nsb_runtime_init(spec_text.encode(), _ptr(w), w.size)
         if not self._h:
             raise RuntimeError(f"ns_runtime_init failed: {last_error()}")
@@ -182,6 +184,7 @@ class Model:
         loss = C.c_float(0)
         _check(lib().nsb_runtime_train_step(self._h, _ptr(x), _ptr(y), x.size, C.byref(loss), lr),
                "ns_runtime_train_step")
+        self._last_rows = x.size // self.spec.in_cols
         return loss.value
 
     def train_step_idx(self, x: np.ndarray, targets: np.ndarray, lr: float) -> float:
@@ -190,6 +193,7 @@ class Model:
         loss = C.c_float(0)
         _check(lib().nsb_runtime_train_step_idx(self._h, _ptr(x), _ptr(t), x.size, C.byref(loss), lr),
                "train_step_idx")
+        self._last_rows = x.size // self.spec.in_cols
         return loss.value
 
     def objective(self, x: np.ndarray, labels: np.ndarray) -> float:
@@ -209,6 +213,14 @@ class Model:
         out = np.empty(self.weight_count(), np.float32)
         _check(lib().nsb_model_get_gradients(self._h, _ptr(out), out.size), "get_gradients")
         return out
+
+    def get_input_gradient(self) -> np.ndarray:
+        """dLoss/dx of the last train step, [rows, input width] (specs with a
+        `grad input` statement)."""
+        rows = self._last_rows
+        out = np.empty(rows * self.spec.in_cols, np.float32)
+        _check(lib().nsb_model_get_input_gradient(self._h, _ptr(out), out.size), "get_input_gradient")
+        return out.reshape(rows, self.spec.in_cols)
 
     def layout(self):
         return spec_layout(self.spec_text)
@@ -244,6 +256,7 @@ class Model:
         _check(lib().nsb_train_step_device(self._h, C.c_void_p(x.data_ptr()), lp, tp, x.numel(),
                                            C.byref(loss) if want_loss else None, lr, C.c_void_p(stream)),
                "train_step_device")
+        self._last_rows = x.numel() // self.spec.in_cols
         return loss.value
 
     def region_timing(self, enable: bool = True) -> None:

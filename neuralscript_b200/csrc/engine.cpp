@@ -29,6 +29,7 @@
 
 #include "../../include/ns_b200.h"
 #include "attention.h"
+#include "elementwise.h"
 #include "engine.h"
 #include "gemm.h"
 #include "kernels.h"
@@ -129,6 +130,11 @@ static bool build_graph(ns_model* m, std::string& err) {
         if (so.fn == "add") op.kind = OP_ADD;
         else if (so.fn == "sub") op.kind = OP_SUB;
         else if (so.fn == "mul") op.kind = OP_MUL;
+        else if (so.fn == "div") op.kind = OP_DIV;
+        else if (so.fn == "concat") op.kind = OP_CONCAT;
+        else if (so.fn == "slice") op.kind = OP_SLICE;
+        else if (so.fn == "index") op.kind = OP_INDEX;
+        else if (so.fn == "scatter") op.kind = OP_SCATTER;
         else if (so.fn == "softmax") op.kind = OP_SOFTMAX;
         else if (act_code(so.fn) >= 0) {
             op.kind = OP_ACT;
@@ -143,13 +149,20 @@ static bool build_graph(ns_model* m, std::string& err) {
             else if (l.kind == "attention") op.kind = OP_ATTN;
             else if (l.kind == "layernorm") op.kind = OP_LN;
             else if (l.kind == "moe") op.kind = OP_MOE;
-            else if (l.kind == "dropout") op.kind = OP_DROPOUT;
+            else if (l.kind == "dropout") {
+                op.kind = OP_DROPOUT;
+                op.drop_rate = (float)std::stod(l.gets("rate", "0"));
+                int site = 0;
+                for (const Op& o : m->ops) site += o.kind == OP_DROPOUT ? 1 : 0;
+                op.drop_site = site;
+            }
             for (size_t wi = 0; wi < s.weights.size(); wi++)
                 if (s.weights[wi].layer == op.layer) {
                     op.widx = (int)wi;
                     break;
                 }
         }
+        op.ints = so.ints;
         op.in = find_val(m, so.args[0]);
         if (so.args.size() > 1) op.in2 = find_val(m, so.args[1]);
         if (find_val(m, so.out) >= 0) {
@@ -190,10 +203,11 @@ static bool build_graph(ns_model* m, std::string& err) {
             break;
         }
     }
-    // Dropout shares its input's storage (identity: no training-time mask
-    // in this backend; see DESIGN notes on dropout).
+    // A dropout of rate 0 is the identity in training too: its value shares
+    // its input's storage. Others keep their own buffer (masked in training,
+    // a copy in inference).
     for (auto& op : m->ops)
-        if (op.kind == OP_DROPOUT) m->vals[op.out].alias_of = op.in;
+        if (op.kind == OP_DROPOUT && op.drop_rate == 0.f) m->vals[op.out].alias_of = op.in;
     return true;
 }
 
@@ -428,6 +442,8 @@ static int plan(ns_model* m, int M, bool train) {
             Val& v = m->vals[vi];
             v.gbuf = PA(float, R * v.cols);
         }
+        // `grad input`: the network input's gradient is formed too
+        if (s.input_grad) m->vals[0].gbuf = PA(float, R * s.in_cols);
         for (auto& op : m->ops)
             if (op.kind == OP_EMB) {
                 const LayerSpec& l = s.layers[op.layer];
@@ -658,8 +674,30 @@ static int forward(ns_model* m, int M, bool train) {
                 rc = layernorm_fwd(in.f32, M, in.cols, out.f32, out.h16, m->stream);
                 break;
             case OP_ADD:
+            case OP_SUB:
+            case OP_MUL:
+            case OP_DIV:
                 launch_counter() += 1;
-                rc = add_f32(in.f32, m->vals[op.in2].f32, (size_t)M * in.cols, out.f32, out.h16, m->stream);
+                rc = binop_fwd(in.f32, m->vals[op.in2].f32, (size_t)M * in.cols, op.kind - OP_ADD, out.f32, out.h16,
+                               m->stream);
+                break;
+            case OP_CONCAT:
+                launch_counter() += 1;
+                rc = concat_cols(in.f32, in.cols, m->vals[op.in2].f32, m->vals[op.in2].cols, M, out.f32, out.h16,
+                                 m->stream);
+                break;
+            case OP_SLICE:
+                launch_counter() += 1;
+                rc = slice_cols(in.f32, M, in.cols, (int)op.ints[0], (int)op.ints[1], out.f32, out.h16, m->stream);
+                break;
+            case OP_INDEX:
+                launch_counter() += 1;
+                rc = index_cols(in.f32, M, in.cols, op.d_idx, (int)op.ints.size(), out.f32, out.h16, m->stream);
+                break;
+            case OP_SCATTER:
+                launch_counter() += 1;
+                rc = scatter_cols(in.f32, M, in.cols, op.d_idx, (int)op.ints.size(), m->vals[op.in2].f32, out.f32,
+                                  out.h16, m->stream);
                 break;
             case OP_ACT:
                 launch_counter() += 1;
@@ -669,8 +707,18 @@ static int forward(ns_model* m, int M, bool train) {
                 launch_counter() += 1;
                 rc = softmax_rows(in.f32, M, in.cols, out.f32, out.h16, m->stream);
                 break;
-            case OP_DROPOUT:
+            case OP_DROPOUT: {
+                if (op.drop_rate == 0.f) break;  // identity, storage shared with the input
+                DropoutSite d;
+                d.rate = train ? op.drop_rate : 0.f;  // inference: a copy
+                d.key0 = m->drop_key0;
+                d.key1 = m->drop_key1;
+                d.step = m->drop_step;
+                d.site = (uint32_t)op.drop_site;
+                launch_counter() += 1;
+                rc = dropout_fwd(in.f32, (size_t)M * in.cols, d, out.f32, out.h16, m->stream);
                 break;
+            }
             case OP_MOE:
                 rc = moe_forward(m, op, M, train);
                 break;
@@ -1050,8 +1098,89 @@ static int backward(ns_model* m, int M) {
                 rc = act_bwd(dv, in.f32, kF32, op.act, in.gcur, (size_t)M * in.cols, in.gbuf, nullptr, m->stream);
                 in.gcur = in.gbuf;
                 break;
-            case OP_SOFTMAX:  // the reference's softmax gradient is a pass-through (code 0)
+            case OP_SUB:
+            case OP_MUL:
+            case OP_DIV: {
+                // two passes (a then b) so that op(x, x) accumulates correctly
+                Val& b = m->vals[op.in2];
+                const size_t n = (size_t)M * in.cols;
+                const int code = op.kind - OP_ADD;
+                if (in.gbuf) {
+                    launch_counter() += 1;
+                    if ((rc = binop_bwd(dv, in.f32, b.f32, n, code, in.gcur, in.gbuf, nullptr, nullptr, m->stream))) break;
+                    in.gcur = in.gbuf;
+                }
+                if (b.gbuf) {
+                    launch_counter() += 1;
+                    if ((rc = binop_bwd(dv, in.f32, b.f32, n, code, nullptr, nullptr, b.gcur, b.gbuf, m->stream))) break;
+                    b.gcur = b.gbuf;
+                }
+                break;
+            }
+            case OP_CONCAT: {
+                Val& b = m->vals[op.in2];
+                if (in.gbuf) {
+                    launch_counter() += 1;
+                    if ((rc = concat_cols_bwd(dv, in.cols, b.cols, M, in.gcur, in.gbuf, nullptr, nullptr, m->stream)))
+                        break;
+                    in.gcur = in.gbuf;
+                }
+                if (b.gbuf) {
+                    launch_counter() += 1;
+                    if ((rc = concat_cols_bwd(dv, in.cols, b.cols, M, nullptr, nullptr, b.gcur, b.gbuf, m->stream)))
+                        break;
+                    b.gcur = b.gbuf;
+                }
+                break;
+            }
+            case OP_SLICE:
+                if (!in.gbuf) break;
+                launch_counter() += 1;
+                rc = slice_cols_bwd(dv, M, in.cols, (int)op.ints[0], (int)op.ints[1], in.gcur, in.gbuf, m->stream);
+                in.gcur = in.gbuf;
+                break;
+            case OP_INDEX:
+                if (!in.gbuf) break;
+                launch_counter() += 1;
+                rc = index_cols_bwd(dv, M, in.cols, op.d_idx, (int)op.ints.size(), in.gcur, in.gbuf, m->stream);
+                in.gcur = in.gbuf;
+                break;
+            case OP_SCATTER: {
+                Val& u = m->vals[op.in2];
+                const int L = (int)op.ints.size();
+                if (in.gbuf) {
+                    launch_counter() += 1;
+                    if ((rc = scatter_cols_bwd(dv, M, in.cols, op.d_idx, L, in.gcur, in.gbuf, nullptr, nullptr,
+                                               m->stream)))
+                        break;
+                    in.gcur = in.gbuf;
+                }
+                if (u.gbuf) {
+                    launch_counter() += 2;
+                    if ((rc = scatter_cols_bwd(dv, M, in.cols, op.d_idx, L, nullptr, nullptr, u.gcur, u.gbuf,
+                                               m->stream)))
+                        break;
+                    u.gcur = u.gbuf;
+                }
+                break;
+            }
             case OP_DROPOUT:
+                if (op.drop_rate > 0.f) {
+                    if (!in.gbuf) break;
+                    DropoutSite d;
+                    d.rate = op.drop_rate;
+                    d.key0 = m->drop_key0;
+                    d.key1 = m->drop_key1;
+                    d.step = m->drop_step;
+                    d.site = (uint32_t)op.drop_site;
+                    launch_counter() += 1;
+                    rc = dropout_bwd(dv, (size_t)M * in.cols, d, in.gcur, in.gbuf, m->stream);
+                    in.gcur = in.gbuf;
+                    break;
+                }
+                rc = contribute_alias(m, in, dv, M);
+                break;
+            case OP_SOFTMAX:  // the reference's softmax gradient is a pass-through (code 0)
                 rc = contribute_alias(m, in, dv, M);
                 break;
             case OP_MOE:
@@ -1511,6 +1640,14 @@ ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_fl
             ok = ok && (m->d_active = (uint8_t*)persist_alloc(E));
             break;
         }
+    // column indices of index / scatter ops, int64 on the device
+    for (auto& op : m->ops)
+        if (ok && (op.kind == OP_INDEX || op.kind == OP_SCATTER)) {
+            std::vector<int64_t> h(op.ints.begin(), op.ints.end());
+            op.d_idx = (int64_t*)persist_alloc(sizeof(int64_t) * h.size());
+            ok = op.d_idx && cudaMemcpy(op.d_idx, h.data(), sizeof(int64_t) * h.size(), cudaMemcpyHostToDevice) ==
+                                 cudaSuccess;
+        }
     ok = ok && alloc_working(m) == 0;
     if (!ok || upload_weights(m)) {
         std::string e = g_err.empty() ? "device allocation failed" : g_err;
@@ -1529,6 +1666,8 @@ void nsb_free(ns_model* m) {
     for (void* p : {(void*)m->d_err, (void*)m->d_w, (void*)m->d_g, (void*)m->d_m, (void*)m->d_v, (void*)m->d_o,
                     (void*)m->d_ns, (void*)m->d_active})
         if (p) cudaFree(p);
+    for (auto& op : m->ops)
+        if (op.d_idx) cudaFree(op.d_idx);
     for (auto& r : m->regions) {
         for (auto& ev : r.pending) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
         for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
@@ -1609,6 +1748,16 @@ int nsb_model_get_gradients(const ns_model* m, float* out, size_t n) {
     if (!m || !out || n != m->spec.total) return -1;
     cudaStreamSynchronize(m->stream);
     return cudaMemcpy(out, m->d_g, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
+}
+
+int nsb_model_get_input_gradient(const ns_model* m, float* out, size_t n) {
+    if (!m || !out) return -1;
+    if (!m->spec.input_grad) return fail("the spec has no 'grad input' statement");
+    const Val& x = m->vals[0];
+    if (!m->last_rows || !x.gcur) return fail("no train step has formed an input gradient yet");
+    if (n != (size_t)m->last_rows * m->spec.in_cols) return fail("size mismatch");
+    cudaStreamSynchronize(m->stream);
+    return cudaMemcpy(out, x.gcur, n * sizeof(float), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : -1;
 }
 
 static int rows_of(const ns_model* m, size_t input_numel) {
@@ -1808,6 +1957,10 @@ static int train_entry(ns_model* m, const float* input, const float* labels, con
     }
     const auto h0 = std::chrono::steady_clock::now();
     int rc = train_core(m, M, dl, dt, loss_out, lr_eff, train);
+    if (train) {
+        m->drop_step++;  // the next step draws fresh dropout masks
+        m->last_rows = M;
+    }
     m->launches = launch_counter() - l0;
     const auto h1 = std::chrono::steady_clock::now();
     if (device_ptrs && !loss_out && !rc) {

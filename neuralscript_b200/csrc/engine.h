@@ -18,7 +18,10 @@ namespace nsb {
 // Kernel launches issued by the calling thread (each launcher adds its own).
 long long& launch_counter();
 
-enum OpKind { OP_DENSE, OP_EMB, OP_ATTN, OP_LN, OP_MOE, OP_ADD, OP_SUB, OP_MUL, OP_ACT, OP_SOFTMAX, OP_DROPOUT };
+enum OpKind {
+    OP_DENSE, OP_EMB, OP_ATTN, OP_LN, OP_MOE, OP_ADD, OP_SUB, OP_MUL, OP_DIV, OP_ACT, OP_SOFTMAX, OP_DROPOUT,
+    OP_CONCAT, OP_SLICE, OP_INDEX, OP_SCATTER
+};
 
 struct Val {
     std::string name;
@@ -66,6 +69,12 @@ struct Op {
     float* lse = nullptr;
     float* dvec = nullptr;
     MoeScratch* moe = nullptr;
+    // data movement: integer operands (slice bounds / column indices), the
+    // indices also on the device (int64, as the reference's kernels take them)
+    std::vector<long long> ints;
+    int64_t* d_idx = nullptr;
+    float drop_rate = 0.f;  // dropout layers
+    int drop_site = 0;      // dropout: index among the network's dropout ops
     bool dz_ready = false;  // backward: dz already holds act'(z) * dout (written by the consumer's GEMM)
     bool g16_ready = false;  // backward: dz / dout_w already holds the bf16 output gradient
 };
@@ -100,6 +109,9 @@ struct ns_model {
     uint8_t* d_active = nullptr;
     std::mt19937 rng{0x9E3779B9u};
     long long lr_step = 0;
+    uint32_t drop_key0 = 0x243F6A88u, drop_key1 = 0x85A308D3u;  // dropout Philox key
+    uint32_t drop_step = 0;  // advances every training step (fresh masks per step)
+    int last_rows = 0;       // rows of the last train step (input gradient export)
     bool seed16 = false;  // last loss seed went to the output Dense layer's bf16 dz
     // graph
     std::vector<nsb::Val> vals;

@@ -181,9 +181,9 @@ __global__ void emb_fill_kernel(const float* __restrict__ ids, int M, int V, con
 }
 
 // Sum of the listed dOut rows (ascending row order) into dst for D = 128*CH:
-// each lane owns CH float4 columns; two rows are loaded before either is
-// added, so a warp keeps 2*CH independent loads in flight while the sums
-// stay in row order (bit-identical to a one-row-at-a-time loop).
+// each lane owns CH float4 columns; four rows are loaded before any is
+// added, so a warp keeps 4*CH independent 16-byte loads in flight while the
+// sums stay in row order (bit-identical to a one-row-at-a-time loop).
 template <int CH>
 __device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int D, const int* rows_sorted, int n,
                                              float* __restrict__ dst, int lane) {
@@ -191,22 +191,22 @@ __device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int
 #pragma unroll
     for (int c = 0; c < CH; c++) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
     int q = 0;
-    for (; q + 1 < n; q += 2) {
-        const float4* r0 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q] * D) + lane;
-        const float4* r1 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q + 1] * D) + lane;
-        float4 t0[CH], t1[CH];
+    for (; q + 3 < n; q += 4) {
+        float4 t[4][CH];
 #pragma unroll
-        for (int c = 0; c < CH; c++) {
-            t0[c] = __ldcs(r0 + 32 * c);
-            t1[c] = __ldcs(r1 + 32 * c);
+        for (int u = 0; u < 4; u++) {
+            const float4* r = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q + u] * D) + lane;
+#pragma unroll
+            for (int c = 0; c < CH; c++) t[u][c] = __ldcs(r + 32 * c);
         }
 #pragma unroll
-        for (int c = 0; c < CH; c++) {
-            acc[c].x += t0[c].x; acc[c].y += t0[c].y; acc[c].z += t0[c].z; acc[c].w += t0[c].w;
-            acc[c].x += t1[c].x; acc[c].y += t1[c].y; acc[c].z += t1[c].z; acc[c].w += t1[c].w;
-        }
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                acc[c].x += t[u][c].x; acc[c].y += t[u][c].y; acc[c].z += t[u][c].z; acc[c].w += t[u][c].w;
+            }
     }
-    if (q < n) {
+    for (; q < n; q++) {
         const float4* r0 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q] * D) + lane;
 #pragma unroll
         for (int c = 0; c < CH; c++) {
@@ -219,10 +219,13 @@ __device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int
     for (int c = 0; c < CH; c++) d4[32 * c] = acc[c];
 }
 
-// One warp per vocabulary row: gather the rows that hit it, order them by
-// row index, and sum their gradients in that order. The sorted row ids are
+// Buckets of at most kEmbWarpRows rows: one warp per vocabulary row gathers
+// the rows that hit it, orders them by row index (bitonic sort across the
+// warp) and sums their gradients in that order. The sorted row ids are
 // staged in shared memory so the column loops (where only some lanes may be
-// active for narrow rows) never shuffle across inactive lanes.
+// active for narrow rows) never shuffle across inactive lanes. Larger
+// buckets are left to emb_big_kernel.
+constexpr int kEmbWarpRows = 32;
 __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, const int* __restrict__ count,
                                   const int* __restrict__ offset, const int* __restrict__ rows,
                                   float* __restrict__ dW, int vec) {
@@ -231,69 +234,135 @@ __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, 
     const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
     for (int v = blockIdx.x * warps + wi; v < V; v += gridDim.x * warps) {
         const int n = count[v];
+        if (n > kEmbWarpRows) continue;
         const int* rv = rows + offset[v];
         float* dst = dW + (size_t)v * D;
         if (n == 0) {
             for (int c = lane; c < D; c += 32) dst[c] = 0.f;
             continue;
         }
-        if (n <= 32) {
-            int key = lane < n ? rv[lane] : 0x7fffffff;
-            // warp bitonic sort, ascending (all 32 lanes participate)
+        int key = lane < n ? rv[lane] : 0x7fffffff;
+        // warp bitonic sort, ascending (all 32 lanes participate)
 #pragma unroll
-            for (int k = 2; k <= 32; k <<= 1) {
+        for (int k = 2; k <= 32; k <<= 1) {
 #pragma unroll
-                for (int j = k >> 1; j > 0; j >>= 1) {
-                    int other = __shfl_xor_sync(kFull, key, j);
-                    bool up = (lane & k) == 0;
-                    bool lower = (lane & j) == 0;
-                    int mn = min(key, other), mx = max(key, other);
-                    key = (lower == up) ? mn : mx;
-                }
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                int other = __shfl_xor_sync(kFull, key, j);
+                bool up = (lane & k) == 0;
+                bool lower = (lane & j) == 0;
+                int mn = min(key, other), mx = max(key, other);
+                key = (lower == up) ? mn : mx;
             }
-            sorted[wi][lane] = key;
-            __syncwarp();
-            if (vec && D == 512) {
-                emb_sum_rows<4>(dout, D, sorted[wi], n, dst, lane);
-            } else if (vec && D == 256) {
-                emb_sum_rows<2>(dout, D, sorted[wi], n, dst, lane);
-            } else if (vec && D == 128) {
-                emb_sum_rows<1>(dout, D, sorted[wi], n, dst, lane);
-            } else if (vec && D == 1024) {
-                emb_sum_rows<8>(dout, D, sorted[wi], n, dst, lane);
-            } else if (vec) {
-                for (int c = lane * 4; c < D; c += 128) {
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int q = 0; q < n; q++) {
-                        float4 t = *reinterpret_cast<const float4*>(dout + (size_t)sorted[wi][q] * D + c);
-                        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
-                    }
-                    *reinterpret_cast<float4*>(dst + c) = acc;
+        }
+        sorted[wi][lane] = key;
+        __syncwarp();
+        if (vec && D == 512) {
+            emb_sum_rows<4>(dout, D, sorted[wi], n, dst, lane);
+        } else if (vec && D == 256) {
+            emb_sum_rows<2>(dout, D, sorted[wi], n, dst, lane);
+        } else if (vec && D == 128) {
+            emb_sum_rows<1>(dout, D, sorted[wi], n, dst, lane);
+        } else if (vec && D == 1024) {
+            emb_sum_rows<8>(dout, D, sorted[wi], n, dst, lane);
+        } else if (vec) {
+            for (int c = lane * 4; c < D; c += 128) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int q = 0; q < n; q++) {
+                    float4 t = *reinterpret_cast<const float4*>(dout + (size_t)sorted[wi][q] * D + c);
+                    acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
                 }
-            } else {
-                for (int c = lane; c < D; c += 32) {
-                    float acc = 0.f;
-                    for (int q = 0; q < n; q++) acc += dout[(size_t)sorted[wi][q] * D + c];
-                    dst[c] = acc;
-                }
+                *reinterpret_cast<float4*>(dst + c) = acc;
             }
-            __syncwarp();
         } else {
-            // large bucket: repeatedly take the next-smallest row index
-            for (int c = lane; c < D; c += 32) dst[c] = 0.f;
-            __syncwarp();
-            int last = -1;
-            for (int q = 0; q < n; q++) {
-                int cand = 0x7fffffff;
-                for (int i = lane; i < n; i += 32) {
-                    int r = rv[i];
-                    if (r > last && r < cand) cand = r;
+            for (int c = lane; c < D; c += 32) {
+                float acc = 0.f;
+                for (int q = 0; q < n; q++) acc += dout[(size_t)sorted[wi][q] * D + c];
+                dst[c] = acc;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// Buckets of more than kEmbWarpRows rows (frequent ids), one CTA per bucket
+// at a time. The bucket's row list (filled in arbitrary order) is ordered in
+// linear time through a bitmap of row indices in shared memory, one window
+// of kEmbBitmapRows rows at a time: every row of the bucket that falls in the
+// window sets its bit (atomicOr: order-independent), then every thread walks
+// the set bits in ascending order and adds those rows into its own column
+// slice. Each column is thus a sequential sum over ascending rows, as in the
+// reference's loop, for any bucket size (work O(n + M/32) per bucket).
+constexpr int kEmbBitmapRows = 262144;  // 32 KB bitmap
+constexpr int kEmbBigThreads = 256;
+__global__ void __launch_bounds__(kEmbBigThreads) emb_big_kernel(const float* __restrict__ dout, int M, int D, int V,
+                                                               const int* __restrict__ count,
+                                                               const int* __restrict__ offset,
+                                                               const int* __restrict__ rows, float* __restrict__ dW,
+                                                               int vec) {
+    __shared__ unsigned bits[kEmbBitmapRows / 32];
+    const int tid = threadIdx.x;
+    const int slots = vec ? D / 4 : D;  // float4 or scalar columns
+    for (int v = blockIdx.x; v < V; v += gridDim.x) {
+        const int n = count[v];
+        if (n <= kEmbWarpRows) continue;  // uniform across the CTA
+        const int* rv = rows + offset[v];
+        float* dst = dW + (size_t)v * D;
+        for (int s0 = 0; s0 < slots; s0 += kEmbBigThreads) {  // column chunks of one slot per thread
+            const int slot = s0 + tid;
+            const bool mine = slot < slots;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int w0 = 0; w0 < M; w0 += kEmbBitmapRows) {
+                const int wrows = min(kEmbBitmapRows, M - w0), words = (wrows + 31) / 32;
+                for (int i = tid; i < words; i += kEmbBigThreads) bits[i] = 0u;
+                __syncthreads();
+                for (int i = tid; i < n; i += kEmbBigThreads) {
+                    const int r = rv[i] - w0;
+                    if (r >= 0 && r < wrows) atomicOr(&bits[r >> 5], 1u << (r & 31));
                 }
+                __syncthreads();
+                if (mine) {
+                    int pend[4];
+                    int np = 0;
+                    for (int q = 0; q < words; q++) {
+                        unsigned b = bits[q];
+                        while (b) {
+                            pend[np++] = w0 + q * 32 + __ffs(b) - 1;
+                            b &= b - 1;
+                            if (np == 4) {
+                                if (vec) {
+                                    float4 t[4];
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(kFull, cand, o));
-                last = cand;
-                for (int c = lane; c < D; c += 32) dst[c] += dout[(size_t)cand * D + c];
-                __syncwarp();
+                                    for (int u = 0; u < 4; u++)
+                                        t[u] = __ldcs(reinterpret_cast<const float4*>(dout + (size_t)pend[u] * D) + slot);
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) {
+                                        acc.x += t[u].x; acc.y += t[u].y; acc.z += t[u].z; acc.w += t[u].w;
+                                    }
+                                } else {
+                                    float t[4];
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) t[u] = dout[(size_t)pend[u] * D + slot];
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) acc.x += t[u];
+                                }
+                                np = 0;
+                            }
+                        }
+                    }
+                    for (int u = 0; u < np; u++) {
+                        if (vec) {
+                            const float4 t = __ldcs(reinterpret_cast<const float4*>(dout + (size_t)pend[u] * D) + slot);
+                            acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+                        } else {
+                            acc.x += dout[(size_t)pend[u] * D + slot];
+                        }
+                    }
+                }
+                __syncthreads();  // before the next window clears the bitmap
+            }
+            if (mine) {
+                if (vec) reinterpret_cast<float4*>(dst)[slot] = acc;
+                else dst[slot] = acc.x;
             }
         }
     }
@@ -311,6 +380,12 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
     int vec = (D % 4 == 0) && aligned16(dout) && aligned16(dW);
     emb_reduce_kernel<<<grid_for((size_t)V, 8), 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    if (M > kEmbWarpRows) {
+        // a few CTAs per SM walk the vocabulary; buckets of <= 32 rows are
+        // skipped after one read of their count
+        const unsigned big = (unsigned)(V < 148 * 4 ? V : 148 * 4);
+        emb_big_kernel<<<big, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec);
+    }
     return launch_ok();
 }
 
@@ -353,6 +428,13 @@ extern "C" int nsb_op_embedding_bwd_noalloc(const float* dout, const float* ids,
                                             void* stream) {
     if (M < 0 || V <= 0 || D <= 0 || !dout || !ids || !dW) return -1;
     if (M > nsb::kNoAllocMaxRows || V > nsb::kNoAllocMaxVocab) return -2;  // beyond the fixed scratch
+    if (stream) {
+        // the scratch address is the current device's: the stream must be on it
+        int sdev = -1, cur = -1;
+        if (cudaStreamGetDevice((cudaStream_t)stream, &sdev) != cudaSuccess || cudaGetDevice(&cur) != cudaSuccess ||
+            sdev != cur)
+            return -4;
+    }
     void* scratch = nsb::noalloc_scratch_ptr();
     if (!scratch) return -3;
     // embedding_bwd zeroes the counters it needs at the start of every call

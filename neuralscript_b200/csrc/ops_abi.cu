@@ -5,6 +5,7 @@
 
 #include "../../include/ns_b200_ops.h"
 #include "attention.h"
+#include "elementwise.h"
 #include "engine.h"
 #include "gemm.h"
 #include "kernels.h"
@@ -168,6 +169,88 @@ int nsb_op_act_fwd(const float* x, size_t n, int act, float* out32, void* out16,
 
 int nsb_op_act_bwd(const float* dy, const float* z, int act, size_t n, float* out32, void* stream) {
     return act_bwd(dy, z, kF32, act, nullptr, n, out32, nullptr, (cudaStream_t)stream);
+}
+
+
+int nsb_op_softmax(const float* x, int M, int C, float* out32, void* out16, void* stream) {
+    if (!x || M < 0 || C <= 0) return -1;
+    launch_counter() += 1;
+    return softmax_rows(x, M, C, out32, reinterpret_cast<__nv_bfloat16*>(out16), (cudaStream_t)stream);
+}
+
+int nsb_op_binop(const float* a, const float* b, size_t n, int code, float* out32, void* out16, void* stream) {
+    launch_counter() += 1;
+    return binop_fwd(a, b, n, code, out32, reinterpret_cast<__nv_bfloat16*>(out16), (cudaStream_t)stream);
+}
+
+int nsb_op_binop_bwd(const float* dout, const float* a, const float* b, size_t n, int code, float* da, float* db,
+                     void* stream) {
+    launch_counter() += 1;
+    return binop_bwd(dout, a, b, n, code, nullptr, da, nullptr, db, (cudaStream_t)stream);
+}
+
+static DropoutSite site_of(float rate, unsigned key0, unsigned key1, unsigned step, unsigned site) {
+    DropoutSite d;
+    d.rate = rate;
+    d.key0 = key0;
+    d.key1 = key1;
+    d.step = step;
+    d.site = site;
+    return d;
+}
+
+int nsb_op_dropout_fwd(const float* x, size_t n, float rate, unsigned key0, unsigned key1, unsigned step,
+                       unsigned site, float* out32, void* out16, void* stream) {
+    launch_counter() += 1;
+    return dropout_fwd(x, n, site_of(rate, key0, key1, step, site), out32, reinterpret_cast<__nv_bfloat16*>(out16),
+                       (cudaStream_t)stream);
+}
+
+int nsb_op_dropout_bwd(const float* dy, size_t n, float rate, unsigned key0, unsigned key1, unsigned step,
+                       unsigned site, float* dx, void* stream) {
+    launch_counter() += 1;
+    return dropout_bwd(dy, n, site_of(rate, key0, key1, step, site), nullptr, dx, (cudaStream_t)stream);
+}
+
+int nsb_op_transpose(const float* in, int R, int C, float* out, void* stream) {
+    launch_counter() += 1;
+    return transpose2d(in, R, C, out, (cudaStream_t)stream);
+}
+
+int nsb_op_concat(const float* a, const float* b, int axis, int rows_a, int rows_b, int ca, int cb, float* out,
+                  void* stream) {
+    launch_counter() += 1;
+    if (axis == 0) {
+        if (ca != cb) return -1;
+        return concat_rows(a, rows_a, b, rows_b, ca, out, (cudaStream_t)stream);
+    }
+    if (rows_a != rows_b) return -1;
+    return concat_cols(a, ca, b, cb, rows_a, out, nullptr, (cudaStream_t)stream);
+}
+
+int nsb_op_slice(const float* in, int axis, int rows, int cols, int start, int end, float* out, void* stream) {
+    launch_counter() += 1;
+    if (axis == 0) {
+        if (start < 0 || end > rows) return -1;
+        return slice_rows(in, cols, start, end, out, (cudaStream_t)stream);
+    }
+    return slice_cols(in, rows, cols, start, end, out, nullptr, (cudaStream_t)stream);
+}
+
+int nsb_op_index(const float* in, int axis, int rows, int cols, const long long* idx, int L, float* out,
+                 void* stream) {
+    launch_counter() += 1;
+    const int64_t* ix = reinterpret_cast<const int64_t*>(idx);
+    if (axis == 0) return index_rows(in, rows, cols, ix, L, out, (cudaStream_t)stream);
+    return index_cols(in, rows, cols, ix, L, out, nullptr, (cudaStream_t)stream);
+}
+
+int nsb_op_scatter(const float* in, int axis, int rows, int cols, const long long* idx, int L, const float* upd,
+                   float* out, void* stream) {
+    launch_counter() += 1;
+    const int64_t* ix = reinterpret_cast<const int64_t*>(idx);
+    if (axis == 0) return scatter_rows(in, rows, cols, ix, L, upd, out, (cudaStream_t)stream);
+    return scatter_cols(in, rows, cols, ix, L, upd, out, nullptr, (cudaStream_t)stream);
 }
 
 }  // extern "C"

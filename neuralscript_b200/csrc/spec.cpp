@@ -19,6 +19,14 @@ int act_code(const std::string& n0) {
     return -1;
 }
 
+int data_fn_values(const std::string& fn) {
+    if (fn == "concat") return 2;
+    if (fn == "slice") return 1;
+    if (fn == "index") return 1;
+    if (fn == "scatter") return 2;
+    return -1;
+}
+
 static std::string trim(const std::string& s) {
     size_t a = s.find_first_not_of(" \t\r\n");
     if (a == std::string::npos) return "";
@@ -79,6 +87,18 @@ bool parse_spec(const std::string& text, Spec& s, std::string& err) {
                     a = trim(a);
                     if (!a.empty()) op.args.push_back(a);
                 }
+                const int nv = data_fn_values(op.fn);
+                if (nv >= 0) {
+                    // value operands first, then integers
+                    if ((int)op.args.size() < nv) { err = "line " + std::to_string(lineno) + ": " + op.fn + " needs " + std::to_string(nv) + " values"; return false; }
+                    for (size_t i = nv; i < op.args.size(); i++) {
+                        size_t used = 0;
+                        long long v = std::stoll(op.args[i], &used);
+                        if (used != op.args[i].size()) { err = "line " + std::to_string(lineno) + ": expected an integer, got '" + op.args[i] + "'"; return false; }
+                        op.ints.push_back(v);
+                    }
+                    op.args.resize(nv);
+                }
                 s.ops.push_back(op);
                 continue;
             }
@@ -115,6 +135,9 @@ bool parse_spec(const std::string& text, Spec& s, std::string& err) {
                 std::map<std::string, std::string> m;
                 if (!kv(tok, 2, m, err)) return false;
                 for (auto& e : m) s.sched[e.first] = std::stod(e.second);
+            } else if (kw == "grad") {
+                if (tok.size() != 2 || tok[1] != "input") { err = "line " + std::to_string(lineno) + ": expected 'grad input'"; return false; }
+                s.input_grad = true;
             } else if (kw == "precision") {
                 if (tok.size() > 1) {
                     if (tok[1] == "fp32") s.precision = 0;
@@ -132,6 +155,7 @@ bool parse_spec(const std::string& text, Spec& s, std::string& err) {
         return false;
     }
     if (s.ops.empty()) { err = "spec has no operations"; return false; }
+    if (s.input_grad && s.tokens) { err = "grad input needs a real-valued input (token ids have no gradient)"; return false; }
     if (s.output.empty()) s.output = s.ops.back().out;
 
     // weights in layer-declaration order
@@ -172,7 +196,11 @@ bool parse_spec(const std::string& text, Spec& s, std::string& err) {
                 add(l.name + "_e1_w", e, d * f);
                 add(l.name + "_e2_w", e, f * d);
             }
-        } else if (l.kind == "layernorm" || l.kind == "dropout") {
+        } else if (l.kind == "dropout") {
+            double r = 0.0;
+            try { r = std::stod(l.gets("rate", "0")); } catch (...) { r = -1.0; }
+            if (!(r >= 0.0 && r < 1.0)) { err = "dropout " + l.name + ": rate must be in [0, 1)"; return false; }
+        } else if (l.kind == "layernorm") {
         } else {
             err = "unknown layer kind " + l.kind;
             return false;
@@ -187,12 +215,29 @@ bool parse_spec(const std::string& text, Spec& s, std::string& err) {
         for (auto& a : op.args)
             if (!s.width.count(a)) { err = "op " + op.out + ": unknown value " + a; return false; }
         int w0 = s.width[op.args[0]];
-        if (op.fn == "add" || op.fn == "sub" || op.fn == "mul") {
+        if (op.fn == "add" || op.fn == "sub" || op.fn == "mul" || op.fn == "div") {
             if (op.args.size() != 2) { err = op.fn + " takes two values"; return false; }
             if (s.width[op.args[1]] != w0) { err = op.out + ": width mismatch"; return false; }
             s.width[op.out] = w0;
         } else if (act_code(op.fn) >= 0 || op.fn == "softmax") {
             s.width[op.out] = w0;
+        } else if (op.fn == "concat") {
+            s.width[op.out] = w0 + s.width[op.args[1]];
+        } else if (op.fn == "slice") {
+            if (op.ints.size() != 2 || op.ints[0] < 0 || op.ints[1] > w0 || op.ints[1] <= op.ints[0]) {
+                err = op.out + ": slice(u, cs, ce) needs 0 <= cs < ce <= width";
+                return false;
+            }
+            s.width[op.out] = (int)(op.ints[1] - op.ints[0]);
+        } else if (op.fn == "index" || op.fn == "scatter") {
+            if (op.ints.empty()) { err = op.out + ": " + op.fn + " needs at least one column index"; return false; }
+            for (long long c : op.ints)
+                if (c < 0 || c >= w0) { err = op.out + ": column index out of range"; return false; }
+            if (op.fn == "scatter" && s.width[op.args[1]] != (int)op.ints.size()) {
+                err = op.out + ": scatter update width must equal the number of indices";
+                return false;
+            }
+            s.width[op.out] = op.fn == "index" ? (int)op.ints.size() : w0;
         } else {
             int li = s.layer_index(op.fn);
             if (li < 0) { err = "unknown layer or function " + op.fn; return false; }

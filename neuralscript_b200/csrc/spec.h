@@ -26,8 +26,14 @@ struct LayerSpec {
 
 struct SpecOp {
     std::string out, fn;
-    std::vector<std::string> args;
+    std::vector<std::string> args;  // value operands
+    std::vector<long long> ints;    // integer operands (slice bounds, column indices)
 };
+
+// Data-movement functions and how many value operands they take before the
+// integer operands: concat(a, b), slice(u, cs, ce), index(u, i0, ...),
+// scatter(u, upd, i0, ...).
+int data_fn_values(const std::string& fn);
 
 struct WeightInfo {
     std::string name;
@@ -50,6 +56,7 @@ struct Spec {
     std::string schedule = "constant";
     std::map<std::string, double> sched;
     int precision = 2;  // 0 fp32, 1 tf32, 2 bf16
+    bool input_grad = false;  // `grad input`: train steps also form dLoss/dx
     std::vector<WeightInfo> weights;
     size_t total = 0;
     std::map<std::string, int> width;  // value name -> columns

@@ -20,13 +20,16 @@ Grammar (one statement per line, ``#`` comments)::
     layer <name> moe dim=<D> experts=<E> ffn=<F> [initial=<K0>] [expert=ffn|linear]
     layer <name> dropout rate=<p>
     <v> = <layer>(<u>)
-    <v> = add(<a>, <b>) | sub(..) | mul(..)
+    <v> = add(<a>, <b>) | sub(..) | mul(..) | div(..)
     <v> = <act>(<u>) | softmax(<u>)
+    <v> = concat(<a>, <b>) | slice(<u>, <cs>, <ce>) | index(<u>, <c0>, <c1>, ..)
+        | scatter(<u>, <upd>, <c0>, <c1>, ..)               # column data movement
     output <v>
     loss cross_entropy | mse
     optimizer reference | adamw [beta1= beta2= eps= decay=] | muon [momentum= steps= decay= ...]
     schedule constant | cosine [warmup= total= min=]
     precision bf16 | tf32 | fp32
+    grad input                                              # train steps also form dLoss/dx
 """
 from __future__ import annotations
 
@@ -73,11 +76,16 @@ class Layer:
         return []
 
 
+# data-movement functions: value operands first, then integers
+DATA_FNS = {"concat": 2, "slice": 1, "index": 1, "scatter": 2}
+
+
 @dataclass
 class Op:
     out: str
     fn: str
     args: List[str]
+    ints: List[int] = field(default_factory=list)
 
 
 @dataclass
@@ -94,6 +102,7 @@ class Spec:
     schedule: str = "constant"
     sched: Dict[str, float] = field(default_factory=dict)
     precision: str = "bf16"
+    input_grad: bool = False
     text: str = ""
 
     def layer(self, name: str) -> Layer:
@@ -137,8 +146,13 @@ def parse(text: str) -> Spec:
             lhs, rhs = line.split("=", 1)
             rhs = rhs.strip()
             fn, rest = rhs.split("(", 1)
+            fn = fn.strip()
             args = [a.strip() for a in rest.rstrip(")").split(",") if a.strip()]
-            s.ops.append(Op(lhs.strip(), fn.strip(), args))
+            ints: List[int] = []
+            if fn in DATA_FNS:
+                ints = [int(a) for a in args[DATA_FNS[fn]:]]
+                args = args[:DATA_FNS[fn]]
+            s.ops.append(Op(lhs.strip(), fn, args, ints))
             continue
         tok = line.split()
         kw = tok[0]
@@ -163,6 +177,10 @@ def parse(text: str) -> Spec:
             s.sched = {k: float(v) for k, v in _kv(tok[2:]).items()}
         elif kw == "precision":
             s.precision = tok[1]
+        elif kw == "grad":
+            if tok[1:] != ["input"]:
+                raise ValueError(f"expected 'grad input': {line}")
+            s.input_grad = True
         else:
             raise ValueError(f"unknown statement: {line}")
     if not s.output and s.ops:
@@ -174,8 +192,17 @@ def out_cols(s: Spec) -> int:
     """Width of the output value (propagated through the graph)."""
     width = {"x": s.in_cols}
     for op in s.ops:
-        if op.fn in ACT_CODES or op.fn in ("softmax", "add", "sub", "mul"):
+        if op.fn in ACT_CODES or op.fn in ("softmax", "add", "sub", "mul", "div", "scatter"):
             width[op.out] = width[op.args[0]]
+            continue
+        if op.fn == "concat":
+            width[op.out] = width[op.args[0]] + width[op.args[1]]
+            continue
+        if op.fn == "slice":
+            width[op.out] = op.ints[1] - op.ints[0]
+            continue
+        if op.fn == "index":
+            width[op.out] = len(op.ints)
             continue
         l = s.layer(op.fn)
         if l.kind == "dense":
@@ -226,6 +253,9 @@ input 1024
 layer moe moe dim=1024 experts=8 ffn=1024
 y = moe(x)
 output y
+loss mse
+optimizer adamw
+grad input
 """
 
 C4 = """network C4

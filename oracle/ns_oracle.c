@@ -697,3 +697,84 @@ float orc_mse(const float* p, const float* y, size_t n) {
 void orc_mse_grad(const float* p, const float* y, float* d, size_t n, float denom) {
     for (size_t i = 0; i < n; i++) d[i] = 2.0f * (p[i] - y[i]) / denom;
 }
+
+/* ---- data movement: the reference's CPU helpers (emitted into every CPU
+ * unit by src/codegen/codegen.cpp; CUDA forms cuda_backend.cpp:93-171).
+ * Scatters write updates in increasing k, so a repeated index keeps its
+ * last update. Index reads outside the source (undefined in the reference)
+ * read 0 here, as the device kernels do. */
+void orc_transpose2d(const float* in, float* out, int64_t rows, int64_t cols) {
+    for (int64_t i = 0; i < rows; i++)
+        for (int64_t j = 0; j < cols; j++) out[j * rows + i] = in[i * cols + j];
+}
+void orc_concat2(const float* a, const float* b, float* out, int64_t rows, int64_t ca, int64_t cb) {
+    for (int64_t r = 0; r < rows; r++) {
+        memcpy(out + r * (ca + cb), a + r * ca, (size_t)ca * sizeof(float));
+        memcpy(out + r * (ca + cb) + ca, b + r * cb, (size_t)cb * sizeof(float));
+    }
+}
+void orc_concat0(const float* a, const float* b, float* out, int64_t ba, int64_t bb, int64_t d) {
+    memcpy(out, a, (size_t)(ba * d) * sizeof(float));
+    memcpy(out + ba * d, b, (size_t)(bb * d) * sizeof(float));
+}
+void orc_slice2(const float* in, float* out, int64_t M, int64_t C, int64_t cs, int64_t ce) {
+    for (int64_t r = 0; r < M; r++) memcpy(out + r * (ce - cs), in + r * C + cs, (size_t)(ce - cs) * sizeof(float));
+}
+void orc_slicerows(const float* in, float* out, int64_t C, int64_t rs, int64_t re) {
+    memcpy(out, in + rs * C, (size_t)((re - rs) * C) * sizeof(float));
+}
+void orc_index2(const float* in, const int64_t* idx, float* out, int64_t M, int64_t C, int64_t L) {
+    for (int64_t r = 0; r < M; r++)
+        for (int64_t k = 0; k < L; k++) out[r * L + k] = (idx[k] >= 0 && idx[k] < C) ? in[r * C + idx[k]] : 0.f;
+}
+void orc_indexrows(const float* in, int64_t R, const int64_t* idx, float* out, int64_t L, int64_t C) {
+    for (int64_t k = 0; k < L; k++)
+        for (int64_t c = 0; c < C; c++) out[k * C + c] = (idx[k] >= 0 && idx[k] < R) ? in[idx[k] * C + c] : 0.f;
+}
+void orc_scatter2(const float* in, const int64_t* idx, const float* upd, float* out, int64_t M, int64_t C, int64_t L) {
+    memcpy(out, in, (size_t)(M * C) * sizeof(float));
+    for (int64_t r = 0; r < M; r++)
+        for (int64_t k = 0; k < L; k++)
+            if (idx[k] >= 0 && idx[k] < C) out[r * C + idx[k]] = upd[r * L + k];
+}
+void orc_scatterrows(const float* in, const int64_t* idx, const float* upd, float* out, int64_t R, int64_t C,
+                     int64_t L) {
+    memcpy(out, in, (size_t)(R * C) * sizeof(float));
+    for (int64_t k = 0; k < L; k++)
+        if (idx[k] >= 0 && idx[k] < R) memcpy(out + idx[k] * C, upd + k * C, (size_t)C * sizeof(float));
+}
+
+/* ---- dropout mask (no reference counterpart for the values: the reference
+ * draws its CPU mask from std::mt19937 via bernoulli_distribution,
+ * codegen.cpp:2874-2893, and its CUDA mask from curand). Counter-based
+ * Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC 2011), restated here
+ * independently of the device code: element i keeps its value when the top
+ * 24 bits of word i % 4 of Philox(counter = {i/4 lo, i/4 hi, step, site},
+ * key = {k0, k1}) / 2^24 >= rate; kept elements are scaled by 1/(1 - rate). */
+static uint32_t orc_mulhilo(uint32_t a, uint32_t b, uint32_t* hi) {
+    uint64_t p = (uint64_t)a * (uint64_t)b;
+    *hi = (uint32_t)(p >> 32);
+    return (uint32_t)p;
+}
+void orc_dropout_mask(float* mask, size_t n, float rate, uint32_t k0, uint32_t k1, uint32_t step, uint32_t site) {
+    const float scale = 1.0f / (1.0f - rate);
+    for (size_t q = 0; 4 * q < n; q++) {
+        uint32_t c0 = (uint32_t)q, c1 = (uint32_t)((uint64_t)q >> 32), c2 = step, c3 = site;
+        uint32_t a = k0, b = k1;
+        for (int r = 0; r < 10; r++) {
+            uint32_t hi0, hi1;
+            uint32_t lo0 = orc_mulhilo(0xD2511F53u, c0, &hi0);
+            uint32_t lo1 = orc_mulhilo(0xCD9E8D57u, c2, &hi1);
+            uint32_t n0 = hi1 ^ c1 ^ a, n2 = hi0 ^ c3 ^ b;
+            c0 = n0;
+            c1 = lo1;
+            c2 = n2;
+            c3 = lo0;
+            a += 0x9E3779B9u;
+            b += 0xBB67AE85u;
+        }
+        const uint32_t w[4] = {c0, c1, c2, c3};
+        for (int j = 0; j < 4 && 4 * q + j < n; j++)
+            mask[4 * q + j] = (float)(w[j] >> 8) * (1.0f / 16777216.0f) >= rate ? scale : 0.f;
+    }
+}

@@ -178,6 +178,45 @@ static void kernels() {
         ns_orthonom(G.data(), 12, 9); ns_orthonom(G2.data(), 5, 11);
         savef("mgs_a", G, {12, 9}); savef("mgs_b", G2, {5, 11});
     }
+    {   // elementwise binops (all four codes, full-size right operand)
+        auto A = U(7 * 13, 190, -2, 2), B = U(7 * 13, 191, 0.5, 2);
+        for (int code = 0; code < 4; code++) {
+            std::vector<float> C(7 * 13);
+            ns_binop(A.data(), A.size(), B.data(), B.size(), C.data(), code);
+            savef("binop_" + std::to_string(code), C, {7, 13});
+        }
+        savef("binop_a", A, {7, 13}); savef("binop_b", B, {7, 13});
+    }
+    {   // data movement: the reference's CPU helpers on a [9, 11] tensor; the
+        // scatters repeat an index so the write order is pinned
+        const int64_t R = 9, C = 11;
+        auto X = U(R * C, 195, -1, 1), Y = U(R * 5, 196, -1, 1), Z = U(4 * C, 197, -1, 1);
+        std::vector<float> t(R * C), c2(R * (C + 5)), c0((R + 4) * C), s2(R * 6), sr(3 * C), i2(R * 4), ir(3 * C),
+            sc(R * C), scr(R * C);
+        const int64_t idx_c[4] = {7, 2, 7, 0};   // columns (7 repeated)
+        const int64_t idx_r[3] = {5, 1, 5};      // rows (5 repeated)
+        const int64_t upd_c[5] = {3, 9, 3, 1, 10};
+        const int64_t upd_r[4] = {2, 6, 2, 8};
+        ns_transpose2d(X.data(), t.data(), R, C);
+        ns_concat2(X.data(), Y.data(), c2.data(), R, C, 5);
+        ns_concat0(X.data(), Z.data(), c0.data(), R, 4, C);
+        ns_slice2(X.data(), s2.data(), R, C, 3, 9);
+        ns_slicerows(X.data(), sr.data(), C, 2, 5);
+        ns_index2(X.data(), idx_c, i2.data(), R, C, 4);
+        ns_indexrows(X.data(), idx_r, ir.data(), 3, C);
+        ns_scatter2(X.data(), upd_c, Y.data(), sc.data(), R, C, 5);
+        ns_scatterrows(X.data(), upd_r, Z.data(), scr.data(), R, C, 4);
+        savef("dm_x", X, {(size_t)R, (size_t)C}); savef("dm_y", Y, {(size_t)R, 5}); savef("dm_z", Z, {4, (size_t)C});
+        savef("dm_transpose", t, {(size_t)C, (size_t)R});
+        savef("dm_concat2", c2, {(size_t)R, (size_t)C + 5});
+        savef("dm_concat0", c0, {(size_t)R + 4, (size_t)C});
+        savef("dm_slice2", s2, {(size_t)R, 6});
+        savef("dm_slicerows", sr, {3, (size_t)C});
+        savef("dm_index2", i2, {(size_t)R, 4});
+        savef("dm_indexrows", ir, {3, (size_t)C});
+        savef("dm_scatter2", sc, {(size_t)R, (size_t)C});
+        savef("dm_scatterrows", scr, {(size_t)R, (size_t)C});
+    }
 }
 
 // ---- ABI level -------------------------------------------------------------
@@ -310,22 +349,22 @@ static void abi() {
         infer(m, tok.data(), out.data(), 256);
         infer(m, tok.data() + 256, out.data() + 256 * 512, 256);
         saved("c2_rowsum", row_sums(out, 512, 512), {512});
-        std::vector<float> head(out.begin(), out.begin() + 4 * 512);
-        head.insert(head.end(), out.begin() + 256 * 512, out.begin() + 260 * 512);
-        savef("c2_head", head, {8, 512});
+        // rows 0..127 of each sequence (256 rows)
+        std::vector<float> rows(out.begin(), out.begin() + 128 * 512);
+        rows.insert(rows.end(), out.begin() + 256 * 512, out.begin() + 384 * 512);
+        savef("c2_rows", rows, {256, 512});
     }
-    {   // config 3 forward (FFN experts), 32 tokens
+    {   // config 3 forward (FFN experts), 64 tokens
         RefLib L = load("c3");
         auto init = L.sym<init_t>("ns_runtime_init");
         auto infer = L.sym<infer_t>("ns_eval_infer");
         auto w = make_blob({1024 * 8, 8 * 1024 * 1024, 8 * 1024 * 1024}, {0.02, 1 / 32.0, 1 / 32.0}, 411);
-        auto x = N(32 * 1024, 401, 0, 1);
+        auto x = N(64 * 1024, 401, 0, 1);
         void* m = init(w.data(), w.size());
-        std::vector<float> out(32 * 1024);
+        std::vector<float> out(64 * 1024);
         infer(m, x.data(), out.data(), x.size());
-        saved("c3_rowsum", row_sums(out, 32, 1024), {32});
-        std::vector<float> head(out.begin(), out.begin() + 2 * 1024);
-        savef("c3_head", head, {2, 1024});
+        saved("c3_rowsum", row_sums(out, 64, 1024), {64});
+        savef("c3_rows", out, {64, 1024});
     }
     // small training runs through ns_runtime_train_step (reference optimizer)
     train_case("tmlp", {6 * 16, 16 * 8, 8 * 4}, {0.41, 0.25, 0.35}, 501, U(16 * 6, 502, -1, 1), 6, 4,

@@ -4,8 +4,8 @@ Builds the reference compiler from its sources (oracle/Makefile.ref, outputs
 in oracle/_ref/), emits the reference CPU units for oracle/models/*.ns,
 compiles tests/golden/gen_golden.cpp against one emitted unit plus the
 shared input generator, runs it, and packs every array it writes into one
-compressed archive. Needs the reference sources (default /root/reference,
-override with NS_REFERENCE); it runs here, never on the GPU box.
+compressed archive. Needs the reference sources: set NS_REFERENCE to the reference
+checkout. It runs on a build host, never on the GPU box.
 
     python tests/golden/gen_golden.py
 """
@@ -18,7 +18,7 @@ import tempfile
 import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-REF = os.environ.get("NS_REFERENCE", "/root/reference")
+REF = os.environ.get("NS_REFERENCE")
 FLAGS = ["-O3", "-march=x86-64-v3"]
 
 
@@ -28,6 +28,8 @@ def run(cmd, **kw):
 
 
 def main():
+    if not REF or not os.path.isdir(os.path.join(REF, "src")):
+        sys.exit("set NS_REFERENCE to the reference source tree")
     run(["make", "-s", "-f", "oracle/Makefile.ref", f"REF={REF}", "-j8"])
     ref_dir = os.path.join(ROOT, "oracle", "_ref")
     with tempfile.TemporaryDirectory() as tmp:

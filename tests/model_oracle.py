@@ -20,6 +20,11 @@ import numpy as np
 import oracle_lib as O
 from neuralscript_b200.spec import ACT_CODES, Spec, parse
 
+# Dropout key of every model (the engine's default Philox key); the step
+# counter advances once per training step and the site is the dropout op's
+# index among the network's dropout ops.
+DROP_KEY = (0x243F6A88, 0x85A308D3)
+
 # include/ns/optim/optim_params.hpp:20-32
 REF_OPT = dict(momentum=0.95, muon_decay=0.01, beta1=0.9, beta2=0.999, eps=1e-8, decay=0.01,
                omb1=0.1, omb2=0.001)
@@ -35,6 +40,8 @@ class OracleModel:
         self.w = np.array(weights, dtype=np.float32, copy=True)
         assert self.w.size == self.s.weight_count
         self.lr_step = 0
+        self.drop_step = 0
+        self.input_grad = None  # dLoss/dx of the last train step (`grad input` specs)
         self.state: Dict[str, dict] = {}
         self.active = None
         for l in self.s.layers:
@@ -54,16 +61,29 @@ class OracleModel:
         raise KeyError(name)
 
     # -- forward ---------------------------------------------------------------
-    def forward(self, x: np.ndarray, keep: bool = False):
+    def forward(self, x: np.ndarray, keep: bool = False, train: bool = False):
         s = self.s
         x = np.asarray(x, np.float32).reshape(-1)
         rows = x.size // s.in_cols
         vals = {"x": x.reshape(rows, s.in_cols) if not s.tokens else x[:rows]}
         cache = {}
+        site = 0
         for op in s.ops:
             a = [vals[t] for t in op.args]
-            if op.fn in ("add", "sub", "mul"):
-                code = {"add": 0, "sub": 1, "mul": 2}[op.fn]
+            if op.fn == "concat":
+                vals[op.out] = O.concat_cols(a[0], a[1])
+                continue
+            if op.fn == "slice":
+                vals[op.out] = O.slice_cols(a[0], op.ints[0], op.ints[1])
+                continue
+            if op.fn == "index":
+                vals[op.out] = O.index_cols(a[0], op.ints)
+                continue
+            if op.fn == "scatter":
+                vals[op.out] = O.scatter_cols(a[0], op.ints, a[1])
+                continue
+            if op.fn in ("add", "sub", "mul", "div"):
+                code = {"add": 0, "sub": 1, "mul": 2, "div": 3}[op.fn]
                 out = np.empty_like(a[0])
                 O.lib.orc_binop(a[0].reshape(-1), a[0].size, np.ascontiguousarray(a[1]).reshape(-1),
                                 a[1].size, out.reshape(-1), code)
@@ -92,7 +112,14 @@ class OracleModel:
             elif l.kind == "moe":
                 vals[op.out] = self._moe_fwd(l, u)
             elif l.kind == "dropout":
-                vals[op.out] = u.copy()
+                rate = float(l.p.get("rate", "0"))
+                if train and rate > 0:
+                    mask = O.dropout_mask(u.size, rate, DROP_KEY[0], DROP_KEY[1], self.drop_step, site)
+                    cache[op.out] = mask.reshape(u.shape)
+                    vals[op.out] = (u * cache[op.out]).astype(np.float32)
+                else:
+                    vals[op.out] = u.copy()
+                site += 1
             else:
                 raise ValueError(l.kind)
         out = vals[s.output]
@@ -137,6 +164,40 @@ class OracleModel:
                 add(op.args[0], dv)
                 add(op.args[1], (-dv).astype(np.float32))
                 continue
+            if op.fn == "mul":
+                add(op.args[0], (dv * a[1]).astype(np.float32))
+                add(op.args[1], (dv * a[0]).astype(np.float32))
+                continue
+            if op.fn == "div":
+                add(op.args[0], (dv / a[1]).astype(np.float32))
+                add(op.args[1], (-dv * a[0] / (a[1] * a[1])).astype(np.float32))
+                continue
+            if op.fn == "concat":
+                ca = a[0].shape[1]
+                add(op.args[0], np.ascontiguousarray(dv[:, :ca]))
+                add(op.args[1], np.ascontiguousarray(dv[:, ca:]))
+                continue
+            if op.fn == "slice":
+                d = np.zeros_like(a[0])
+                d[:, op.ints[0]:op.ints[1]] = dv
+                add(op.args[0], d)
+                continue
+            if op.fn == "index":
+                d = np.zeros_like(a[0])
+                for k, c in enumerate(op.ints):  # duplicates add in increasing k
+                    d[:, c] = (d[:, c] + dv[:, k]).astype(np.float32)
+                add(op.args[0], d)
+                continue
+            if op.fn == "scatter":
+                last = {c: k for k, c in enumerate(op.ints)}  # the update each column keeps
+                d_in = dv.copy()
+                d_upd = np.zeros_like(a[1])
+                for c, k in last.items():
+                    d_in[:, c] = 0.0
+                    d_upd[:, k] = dv[:, c]
+                add(op.args[0], d_in)
+                add(op.args[1], d_upd)
+                continue
             if op.fn in ACT_CODES:
                 add(op.args[0], O.act_grad(dv, a[0], ACT_CODES[op.fn]))
                 continue
@@ -175,7 +236,10 @@ class OracleModel:
                 grads.update({f"{l.name}_g_w": dwg, f"{l.name}_e1_w": dwe1, f"{l.name}_e2_w": dwe2})
                 add(op.args[0], dx)
             elif l.kind == "dropout":
-                add(op.args[0], dv)
+                mask = cache.get(op.out)
+                add(op.args[0], dv if mask is None else (dv * mask).astype(np.float32))
+        if s.input_grad:
+            grads["__input__"] = g.get("x")
         return grads
 
     # -- loss ------------------------------------------------------------------
@@ -209,10 +273,12 @@ class OracleModel:
         st = self.lr_step
         self.lr_step += 1
         lr_eff = _f(_f(lr) * _f(self.schedule(st)))
-        out, vals, cache = self.forward(x, keep=True)
+        out, vals, cache = self.forward(x, keep=True, train=True)
         loss, seed = self._loss_and_seed(out, labels)
         grads = self.backward(vals, cache, seed)
+        self.input_grad = grads.pop("__input__", None)
         self.apply(grads, lr_eff)
+        self.drop_step += 1
         return float(loss)
 
     def apply(self, grads, lr_eff):

@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(ROOT, "oracle", "libns_oracle.so")
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
 _i64 = C.c_int64
 
 
@@ -50,6 +51,16 @@ def _load():
         "orc_newton_schulz5": (None, [_f32p, _i64, _i64, C.c_int]),
         "orc_mse": (C.c_float, [_f32p, _f32p, C.c_size_t]),
         "orc_mse_grad": (None, [_f32p, _f32p, _f32p, C.c_size_t, C.c_float]),
+        "orc_transpose2d": (None, [_f32p, _f32p, _i64, _i64]),
+        "orc_concat2": (None, [_f32p, _f32p, _f32p, _i64, _i64, _i64]),
+        "orc_concat0": (None, [_f32p, _f32p, _f32p, _i64, _i64, _i64]),
+        "orc_slice2": (None, [_f32p, _f32p, _i64, _i64, _i64, _i64]),
+        "orc_slicerows": (None, [_f32p, _f32p, _i64, _i64, _i64]),
+        "orc_index2": (None, [_f32p, _i64p, _f32p, _i64, _i64, _i64]),
+        "orc_indexrows": (None, [_f32p, _i64, _i64p, _f32p, _i64, _i64]),
+        "orc_scatter2": (None, [_f32p, _i64p, _f32p, _f32p, _i64, _i64, _i64]),
+        "orc_scatterrows": (None, [_f32p, _i64p, _f32p, _f32p, _i64, _i64, _i64]),
+        "orc_dropout_mask": (None, [_f32p, C.c_size_t, C.c_float, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
         "orc_fill_uniform": (None, [_f32p, C.c_size_t, C.c_uint64, C.c_double, C.c_double]),
         "orc_fill_normal": (None, [_f32p, C.c_size_t, C.c_uint64, C.c_double, C.c_double]),
         "orc_fill_tokens": (None, [_f32p, C.c_size_t, C.c_uint64, _i64]),
@@ -264,4 +275,78 @@ def fill_normal(n, seed, mu, sd):
 def fill_tokens(n, seed, vocab):
     out = np.empty(n, np.float32)
     lib.orc_fill_tokens(out, n, seed, vocab)
+    return out
+
+
+# ---- data movement and dropout (restated reference CPU helpers) -------------
+def _i64a(v):
+    return np.ascontiguousarray(v, dtype=np.int64)
+
+
+def transpose2d(x):
+    x = f32(x)
+    out = np.empty((x.shape[1], x.shape[0]), np.float32)
+    lib.orc_transpose2d(x, out, x.shape[0], x.shape[1])
+    return out
+
+
+def concat_cols(a, b):
+    a, b = f32(a), f32(b)
+    out = np.empty((a.shape[0], a.shape[1] + b.shape[1]), np.float32)
+    lib.orc_concat2(a, b, out, a.shape[0], a.shape[1], b.shape[1])
+    return out
+
+
+def concat_rows(a, b):
+    a, b = f32(a), f32(b)
+    out = np.empty((a.shape[0] + b.shape[0], a.shape[1]), np.float32)
+    lib.orc_concat0(a, b, out, a.shape[0], b.shape[0], a.shape[1])
+    return out
+
+
+def slice_cols(x, cs, ce):
+    x = f32(x)
+    out = np.empty((x.shape[0], ce - cs), np.float32)
+    lib.orc_slice2(x, out, x.shape[0], x.shape[1], cs, ce)
+    return out
+
+
+def slice_rows(x, rs, re):
+    x = f32(x)
+    out = np.empty((re - rs, x.shape[1]), np.float32)
+    lib.orc_slicerows(x, out, x.shape[1], rs, re)
+    return out
+
+
+def index_cols(x, idx):
+    x, idx = f32(x), _i64a(idx)
+    out = np.empty((x.shape[0], idx.size), np.float32)
+    lib.orc_index2(x, idx, out, x.shape[0], x.shape[1], idx.size)
+    return out
+
+
+def index_rows(x, idx):
+    x, idx = f32(x), _i64a(idx)
+    out = np.empty((idx.size, x.shape[1]), np.float32)
+    lib.orc_indexrows(x, x.shape[0], idx, out, idx.size, x.shape[1])
+    return out
+
+
+def scatter_cols(x, idx, upd):
+    x, idx, upd = f32(x), _i64a(idx), f32(upd)
+    out = np.empty_like(x)
+    lib.orc_scatter2(x, idx, upd, out, x.shape[0], x.shape[1], idx.size)
+    return out
+
+
+def scatter_rows(x, idx, upd):
+    x, idx, upd = f32(x), _i64a(idx), f32(upd)
+    out = np.empty_like(x)
+    lib.orc_scatterrows(x, idx, upd, out, x.shape[0], x.shape[1], idx.size)
+    return out
+
+
+def dropout_mask(n, rate, k0, k1, step, site):
+    out = np.empty(n, np.float32)
+    lib.orc_dropout_mask(out, n, rate, k0, k1, step, site)
     return out

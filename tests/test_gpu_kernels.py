@@ -193,6 +193,28 @@ def test_embedding_fwd_bwd_deterministic_and_exact(V, D, M):
     assert torch.equal(dW1, dW2)
 
 
+@pytest.mark.parametrize("M,V,D,hot", [(16384, 8192, 512, 0.25), (131072, 8192, 512, 0.05), (5000, 300, 96, 0.6)])
+def test_embedding_grad_skewed_ids_exact(M, V, D, hot):
+    """Frequent ids (one id takes `hot` of the rows, a few more take 1-2 %
+    each, the rest uniform): buckets far larger than a warp are summed in
+    ascending row order through the bitmap path, bit-exact against the
+    oracle (the reference's sequential loop)."""
+    rng = np.random.default_rng(7)
+    ids = rng.integers(0, V, M).astype(np.float32)
+    pick = rng.random(M)
+    ids[pick < hot] = 11
+    for k, v in enumerate([5, 99, V - 1]):
+        lo = hot + 0.015 * k
+        ids[(pick >= lo) & (pick < lo + 0.012)] = v
+    ids[:3] = [-1, V, 11.9]
+    dout = rng.normal(0, 1, (M, D)).astype(np.float32)
+    idd, dd = torch.from_numpy(ids).to(DEV), torch.from_numpy(dout).to(DEV)
+    dW = torch.empty(V, D, device=DEV)
+    O.embedding_bwd(dd, idd, V, dW)
+    torch.cuda.synchronize()
+    assert np.array_equal(dW.cpu().numpy(), R.embedding_grad_w(dout, ids, V))
+
+
 def attn_reference(qkv, B, S, H, D, dctx=None):
     dh = D // H
     q = qkv[:, :D].reshape(B, S, H, dh).transpose(0, 2, 1, 3)

@@ -3,9 +3,13 @@ libraries against the reference's own outputs (tests/golden), and the
 engine against the model-level oracle for what the reference cannot run
 (per-sequence attention with residuals, AdamW/cosine configuration modes).
 
-Tolerances: pure-fp32 SIMT mode 1e-5 relative; TF32 / bf16 tensor-core
-modes 2e-3 / 1e-2 relative (Frobenius norm) on forward activations; losses
-after training as stated per test.
+Tolerances (relative Frobenius norm) on forward activations: pure-fp32
+SIMT mode 1e-5; the tensor-core modes 2e-3 (the contract's bound) in each
+configuration's contract mode: bf16 for the config-2 block, TF32 for the
+config-1 MLP. bf16 on config 1 is held to 6e-3 and documented as outside
+the contract: three chained GEMMs over bf16-rounded operands put its output
+about 4.6e-3 from fp32 by rounding alone. Losses after training as stated
+per test (1e-3 relative over 100 steps in the tensor-core modes).
 """
 import os
 import struct
@@ -23,7 +27,8 @@ from neuralscript_b200.spec import C1, C2, parse  # noqa: E402
 from specs import SMALL, TMLP, TTFM  # noqa: E402
 
 G = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
-TOL = {"fp32": 1e-5, "tf32": 2e-3, "bf16": 1e-2}
+TOL = {"fp32": 1e-5, "tf32": 2e-3, "bf16": 2e-3}
+C1_TOL = {"fp32": 1e-5, "tf32": 2e-3, "bf16": 6e-3}
 
 
 def relerr(a, b):
@@ -56,34 +61,56 @@ def test_c1_dropin_abi_matches_reference(mode, precision_env):
     assert L.ns_model_output_numel(m, x.size) == 640
     e = relerr(out.reshape(64, 10), G["c1_out"])
     L.ns_free(m)
-    assert e < TOL[mode], e
+    assert e < C1_TOL[mode], e
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32"])
+def test_c1_full_batch_matches_oracle(mode, precision_env):
+    """The config-1 batch (4096 rows) in its contract modes through the
+    drop-in ABI, against the oracle on every 16th row (rows are independent)."""
+    os.environ["NS_B200_PRECISION"] = mode
+    L = nsb.RuntimeLib("c1")
+    w = make_weights(C1, 212, sds=[1 / 28.0, 1 / 32.0, 1 / 32.0])
+    x = synth.uniform(4096 * 784, 202, -1, 1)
+    m = L.ns_runtime_init(w.ctypes.data, w.size)
+    out = np.empty(4096 * 10, np.float32)
+    assert L.ns_eval_infer(m, x.ctypes.data, out.ctypes.data, x.size) == 0
+    L.ns_free(m)
+    sample = x.reshape(4096, 784)[::16]
+    exp = OracleModel(C1, w).forward(sample)
+    assert relerr(out.reshape(4096, 10)[::16], exp) < TOL[mode]
 
 
 @pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
 def test_c2_forward_matches_reference(mode):
     """Config-2 block on two 256-token sequences vs the reference CPU emit
-    called once per sequence."""
+    called once per sequence: 256 rows (the first 128 of each sequence)."""
     w = make_weights(C2, 311, default_sd=0.02)
     tok = synth.tokens(512, 301, 8192)
     m = nsb.Model(C2, w, precision=mode)
     out = m.infer(tok)
-    head = np.concatenate([out[:4], out[256:260]])
-    assert relerr(head, G["c2_head"]) < TOL[mode]
+    rows = np.concatenate([out[:128], out[256:384]])
+    assert relerr(rows, G["c2_rows"]) < TOL[mode]
+    for r in range(0, 256, 8):  # and row by row on a sample
+        assert relerr(rows[r], G["c2_rows"][r]) < 2 * TOL[mode], r
     rs = out.astype(np.float64).sum(axis=1)
     # LayerNorm outputs have ~zero row sums; compare them absolutely
     assert np.max(np.abs(rs - G["c2_rowsum"])) < (1e-3 if mode == "fp32" else 0.05)
 
 
-def test_c2_forward_full_batch_matches_oracle_tf32():
-    """64 x 256 tokens (the config-2 batch) against the oracle on 4 of the
-    sequences (the oracle is too slow for all 64); rows are independent
-    across sequences, so a sample pins the whole batch."""
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+def test_c2_forward_full_batch_matches_oracle(mode):
+    """64 x 256 tokens (the config-2 batch) against the oracle on 4
+    sequences spread over the batch (the oracle is too slow for all 64);
+    rows are independent across sequences, so a sample pins the batch."""
     w = make_weights(C2, 311, default_sd=0.02)
     tok = synth.tokens(64 * 256, 302, 8192)
-    m = nsb.Model(C2, w, precision="tf32")
+    m = nsb.Model(C2, w, precision=mode)
     out = m.infer(tok)
-    ref = OracleModel(C2, w).forward(tok[:4 * 256])
-    assert relerr(out[:1024], ref) < 2e-3
+    seqs = [0, 21, 42, 63]
+    sel = np.concatenate([np.arange(q * 256, (q + 1) * 256) for q in seqs])
+    ref = OracleModel(C2, w).forward(tok[sel])
+    assert relerr(out[sel], ref) < TOL[mode]
     assert np.all(np.isfinite(out))
 
 
@@ -317,3 +344,46 @@ def test_config5_structure_muon_matches_oracle(mode):
     # Muon's large normalised steps (each one moves a weight by a sizeable
     # fraction of itself) the weights drift apart by several percent within
     # a few steps (7.5 % after 8 in TF32) while the losses stay together.
+
+
+# The config-2 block at small size with the loss taken on the block output
+# itself (no head layer): the smoke network. Its forward output is a config
+# block output, so the contract's 2e-3 applies in bf16.
+SMOKE = RESID.replace("layer head dense in=32 out=48\n", "").replace("logits = head(y)\noutput logits",
+                                                                       "output y")
+
+
+def test_smoke_block_bf16_forward_and_step():
+    w = make_weights(SMOKE, 901, default_sd=0.1)
+    tok = synth.tokens(64, 902, 64)
+    y = synth.one_hot(synth.tokens(64, 903, 32), 32)
+    m = nsb.Model(SMOKE, w, precision="bf16")
+    ref = OracleModel(SMOKE, w)
+    assert relerr(m.infer(tok), ref.forward(tok)) < TOL["bf16"]
+    l_gpu, l_ref = m.train_step(tok, y, 0.01), ref.train_step(tok, y, 0.01)
+    assert abs(l_gpu - l_ref) < 1e-3 * abs(l_ref), (l_gpu, l_ref)
+
+
+def test_config4_full_size_step_matches_reference():
+    """One config-4 train step at its full per-GPU size (64 x 256 tokens,
+    512 -> 8192 head, bf16) against the float64 restatement
+    (tests/torch_ref.py, pinned to the oracle on CPU): the loss within 1e-3
+    and every weight gradient within 2e-2 (relative Frobenius). The cosine
+    schedule's first step has a zero learning rate, so the weights stay put
+    and a second step must reproduce the loss."""
+    import torch_ref
+    from neuralscript_b200.spec import C4
+    w = make_weights(C4, 1301, default_sd=0.02)
+    tok = synth.tokens(64 * 256, 1302, 8192)
+    tgt = synth.tokens(64 * 256, 1303, 8192).astype(np.int32)
+    m = nsb.Model(C4, w, precision="bf16")
+    l1 = m.train_step_idx(tok, tgt, 3e-4)
+    g = m.get_gradients()
+    l_ref, g_ref, _ = torch_ref.forward_backward(C4, w, tok, tgt, device="cuda")
+    assert abs(l1 - l_ref) < 1e-3 * abs(l_ref), (l1, l_ref)
+    for name, off, cnt, shp in parse(C4).layout():
+        e = relerr(g[off:off + cnt], g_ref[name].reshape(-1))
+        assert e < 2e-2, (name, e)
+    assert np.array_equal(m.get_weights(), w)  # lr factor 0 at step 0
+    l2 = m.train_step_idx(tok, tgt, 3e-4)
+    assert abs(l2 - l1) < 1e-6 * abs(l1)

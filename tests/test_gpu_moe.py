@@ -47,15 +47,24 @@ def test_routing_bit_exact_at_config3_router_scale(M, active):
     assert relerr(probs.cpu(), p_ref) < 1e-6
 
 
+# Forward-activation tolerances against the reference. TF32 is config 3's
+# contract mode (2e-3). bf16 is not: two chained GEMMs over bf16-rounded
+# operands put the expert output about 3.4e-3 (relative Frobenius) from the
+# fp32 result by rounding alone, so bf16 is held to 5e-3 here.
+C3_TOL = {"fp32": 1e-5, "tf32": 2e-3, "bf16": 5e-3}
+
+
 @pytest.mark.parametrize("mode", ["fp32", "tf32", "bf16"])
 def test_c3_ffn_forward_matches_reference(mode):
+    """64 tokens of the config-3 layer against the reference CPU emit."""
     w = make_weights(C3, 411, sds=[0.02, 1 / 32.0, 1 / 32.0])
-    x = synth.normal(32 * 1024, 401, 0, 1)
+    x = synth.normal(64 * 1024, 401, 0, 1)
     m = nsb.Model(C3, w, precision=mode)
     out = m.infer(x)
-    tol = {"fp32": 1e-5, "tf32": 2e-3, "bf16": 1e-2}[mode]
-    assert relerr(out[:2], G["c3_head"]) < tol
-    assert relerr(out.astype(np.float64).sum(axis=1), G["c3_rowsum"]) < tol * 10
+    tol = C3_TOL[mode]
+    assert relerr(out, G["c3_rows"]) < tol
+    for r in range(64):  # and row by row
+        assert relerr(out[r], G["c3_rows"][r]) < 2 * tol, r
 
 
 def test_tmoe_training_and_lifecycle_match_reference_runtime(tmp_path):
@@ -138,10 +147,12 @@ def test_c3_ffn_gradients_match_oracle(mode):
     """Config-3 dimensions (D 1024, 8 experts, FFN 1024) on the tensor-core
     paths: expert GEMMs grouped by routed token (forward with the per-expert
     weights stacked along K, weight gradients grouped over each expert's
-    tokens) and the two-pass gate-weight gradient, against the oracle's
-    restatement of the reference MoE gradient helpers."""
-    spec = C3 + "loss mse\noptimizer adamw\n"
-    D, E, H, M = 1024, 8, 1024, 160
+    tokens), the input gradient dX (ns_moe_grad_x: grouped dH We1^T GEMM
+    scattered back to tokens, plus the gate term) and the two-pass gate-weight
+    gradient, against the oracle's restatement of the reference MoE gradient
+    helpers (src/codegen/codegen.cpp:1388-1579)."""
+    spec = C3  # MSE, AdamW, `grad input` (dX formed)
+    D, E, H, M = 1024, 8, 1024, 256
     w = make_weights(spec, 411, sds=[0.02, 1 / 32.0, 1 / 32.0])
     x = synth.normal(M * D, 431, 0, 1).reshape(M, D)
     t = synth.normal(M * D, 432, 0, 1).reshape(M, D)
@@ -150,12 +161,15 @@ def test_c3_ffn_gradients_match_oracle(mode):
     We2 = w[D * E + E * D * H:].reshape(E, H * D)
     out = R.moe_fwd(x, Wg, We1, We2, H)
     dy = 2.0 * (out.astype(np.float64) - t) / out.size
-    _, dWg, dWe1, dWe2 = R.moe_grads(dy.astype(np.float32), x, Wg, We1, We2, H)
+    dX, dWg, dWe1, dWe2 = R.moe_grads(dy.astype(np.float32), x, Wg, We1, We2, H)
     m = nsb.Model(spec, w, precision=mode)
     tol = {"tf32": 3e-3, "bf16": 1.5e-2}[mode]
-    assert relerr(m.infer(x.reshape(-1)), out) < tol
+    assert relerr(m.infer(x.reshape(-1)), out) < C3_TOL[mode]
     m.train_step(x.reshape(-1), t.reshape(-1), 0.0)
     g = m.get_gradients()
+    gx = m.get_input_gradient()
+    assert gx.shape == (M, D)
+    assert relerr(gx, dX) < 3 * tol
     assert relerr(g[:D * E], dWg.reshape(-1)) < 3 * tol
     assert relerr(g[D * E:D * E + E * D * H], dWe1.reshape(-1)) < 3 * tol
     assert relerr(g[D * E + E * D * H:], dWe2.reshape(-1)) < 3 * tol

@@ -57,6 +57,36 @@ def test_noalloc_matches_regular_entry_point_twice():
         assert torch.equal(got, ref)  # deterministic: identical bits
 
 
+def test_noalloc_at_its_limits_after_larger_and_smaller_calls():
+    """The whole scratch in use (M = 262144 rows, V = 65536 vocabulary rows),
+    then a small call, then the full size again: each bit-for-bit equal to
+    the regular entry point, so no counter survives from an earlier call
+    anywhere in the shared array."""
+    L = _lib()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for seed, (M, V, D) in enumerate([(262144, 65536, 32), (700, 50, 16), (262144, 65536, 32)]):
+        ids, dout = _case(10 + seed, M, V, D)
+        ids[M // 2:M // 2 + 5000] = 7.0  # a bucket far larger than a warp
+        scratch = torch.empty(L.nsb_op_embedding_bwd_scratch_bytes(M, V), dtype=torch.uint8, device="cuda")
+        ref = torch.empty(V, D, device="cuda")
+        assert L.nsb_op_embedding_bwd(_ptr(dout), _ptr(ids), M, V, D, _ptr(ref), _ptr(scratch), stream) == 0
+        got = torch.full((V, D), float("nan"), device="cuda")
+        assert L.nsb_op_embedding_bwd_noalloc(_ptr(dout), _ptr(ids), M, V, D, _ptr(got), stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), (M, V)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_noalloc_rejects_a_stream_of_another_device():
+    L = _lib()
+    with torch.cuda.device(1):
+        other = torch.cuda.Stream()
+    d = torch.zeros(4, 8, device="cuda:0")
+    ids = torch.zeros(4, device="cuda:0")
+    out = torch.zeros(16, 8, device="cuda:0")
+    assert L.nsb_op_embedding_bwd_noalloc(_ptr(d), _ptr(ids), 4, 16, 8, _ptr(out), C.c_void_p(other.cuda_stream)) == -4
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch():
     L = _lib()
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
