@@ -20,6 +20,8 @@
 #include <string.h>
 
 #include <chrono>
+#include <condition_variable>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -64,6 +66,10 @@ struct Nccl {
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*Reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, int, ncclComm_t,
+                           cudaStream_t) = nullptr;
+    ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*CommInitAll)(ncclComm_t*, int, const int*) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
     bool ok = false;
 };
@@ -81,9 +87,12 @@ static const Nccl& nccl() {
         n.CommAbort = (decltype(n.CommAbort))dlsym(h, "ncclCommAbort");
         n.CommDestroy = (decltype(n.CommDestroy))dlsym(h, "ncclCommDestroy");
         n.AllReduce = (decltype(n.AllReduce))dlsym(h, "ncclAllReduce");
+        n.Reduce = (decltype(n.Reduce))dlsym(h, "ncclReduce");
+        n.Broadcast = (decltype(n.Broadcast))dlsym(h, "ncclBroadcast");
+        n.CommInitAll = (decltype(n.CommInitAll))dlsym(h, "ncclCommInitAll");
         n.GetErrorString = (decltype(n.GetErrorString))dlsym(h, "ncclGetErrorString");
         n.ok = n.GetUniqueId && n.CommInitRankConfig && n.CommGetAsyncError && n.CommAbort && n.CommDestroy &&
-               n.AllReduce && n.GetErrorString;
+               n.AllReduce && n.Reduce && n.Broadcast && n.CommInitAll && n.GetErrorString;
     });
     return n;
 }
@@ -335,7 +344,7 @@ static WkTarget working_target(const ns_model* m, int wi) {
 
 // Refresh the working copies from the fp32 master blob (all of them, or
 // those not marked in `done`).
-static int refresh_working(ns_model* m, const std::vector<char>* done = nullptr) {
+static int refresh_working(ns_model* m, const std::vector<char>* done) {
     const Spec& s = m->spec;
     for (size_t wi = 0; wi < s.weights.size(); wi++) {
         if (done && (*done)[wi]) continue;
@@ -763,6 +772,8 @@ static const void* grad_operand(ns_model* m, const float* g, void* tmp16, size_t
 // ---------------------------------------------------------------------------
 static int nccl_settle(ns_model* m);
 static int optimizer_step(ns_model* m, float lr, const std::vector<char>* sel = nullptr);
+static int refresh_working(ns_model* m, const std::vector<char>* done);
+void assign_owners(ns_model* m);
 static bool dist_active(const ns_model* m) { return m->comm && m->world > 1; }
 
 static cudaEvent_t dist_event(ns_model* m) {
@@ -774,15 +785,24 @@ static cudaEvent_t dist_event(ns_model* m) {
     return m->dist_events[m->ev_next++];
 }
 
-static int dist_reduce_range(ns_model* m, size_t off, size_t count) {
+// One collective on the communication stream, ordered after the work so
+// far on the engine stream: all-reduce (root < 0) or reduce to `root` of the
+// gradient range, or (bcast) broadcast of the weight range from `root`.
+static int dist_collective(ns_model* m, size_t off, size_t count, int root, bool bcast) {
     if (!count) return 0;
     cudaEvent_t ev = dist_event(m);
     if (!ev) return fail("event creation failed");
     cudaEventRecord(ev, m->stream);
     cudaStreamWaitEvent(m->comm_stream, ev, 0);
     launch_counter() += 1;
-    ncclResult_t r = nccl().AllReduce(m->d_g + off, m->d_g + off, count, ncclFloat, ncclSum, m->comm, m->comm_stream);
-    if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("allreduce: ") + nccl().GetErrorString(r));
+    ncclResult_t r;
+    if (bcast)
+        r = nccl().Broadcast(m->d_w + off, m->d_w + off, count, ncclFloat, root, m->comm, m->comm_stream);
+    else if (root >= 0)
+        r = nccl().Reduce(m->d_g + off, m->d_g + off, count, ncclFloat, ncclSum, root, m->comm, m->comm_stream);
+    else
+        r = nccl().AllReduce(m->d_g + off, m->d_g + off, count, ncclFloat, ncclSum, m->comm, m->comm_stream);
+    if (r != ncclSuccess && r != ncclInProgress) return fail(std::string("collective: ") + nccl().GetErrorString(r));
     // a non-blocking communicator may still be enqueueing: wait until the
     // collective sits on its stream before the next NCCL call
     if (r == ncclInProgress && nccl_settle(m)) return -1;
@@ -793,18 +813,36 @@ static int dist_reduce_range(ns_model* m, size_t off, size_t count) {
     return 0;
 }
 
-// All-reduce weights [w0, w1) once their gradients are final (the range that
-// ends the blob also carries the loss sum stored after it).
+static int dist_reduce_range(ns_model* m, size_t off, size_t count) { return dist_collective(m, off, count, -1, false); }
+
+// Reduce the gradients of weights [w0, w1) once they are final: matrices
+// with an owner rank (sharded Muon) are reduced to their owner only, the
+// rest all-reduced in contiguous runs; the loss sum stored after the blob
+// rides with an all-reduce that ends the blob, or alone.
 static int dist_reduce_weights(ns_model* m, int w0, int w1) {
     const Spec& s = m->spec;
     for (int w = w0; w < w1; w++)
         if (m->reduced[w]) return 0;
     for (int w = w0; w < w1; w++) m->reduced[w] = 1;
     m->bucket_w.push_back(std::make_pair(w0, w1));
-    const size_t off = s.weights[w0].off;
-    size_t end = s.weights[w1 - 1].off + s.weights[w1 - 1].count;
-    if (end == s.total) end += 1;
-    return dist_reduce_range(m, off, end - off);
+    int w = w0;
+    while (w < w1) {
+        const int own = m->owner.empty() ? -1 : m->owner[w];
+        if (own >= 0) {
+            if (dist_collective(m, s.weights[w].off, s.weights[w].count, own, false)) return -1;
+            if (s.weights[w].off + s.weights[w].count == s.total && dist_reduce_range(m, s.total, 1)) return -1;
+            w++;
+            continue;
+        }
+        int e = w;
+        while (e < w1 && (m->owner.empty() || m->owner[e] < 0)) e++;
+        const size_t off = s.weights[w].off;
+        size_t end = s.weights[e - 1].off + s.weights[e - 1].count;
+        if (end == s.total) end += 1;
+        if (dist_reduce_range(m, off, end - off)) return -1;
+        w = e;
+    }
+    return 0;
 }
 
 // Reduce what is left (weights of layers without a gradient op in this
@@ -838,6 +876,34 @@ static int dist_reduce_finish(ns_model* m) {
 static int dist_optimizer(ns_model* m, float lr) {
     const size_t nb = m->bucket_w.size();
     const size_t nw = m->spec.weights.size();
+    bool sharded = false;
+    for (int o : m->owner) sharded = sharded || o >= 0;
+    if (sharded) {
+        // Sharded Muon: every reduction done; update the replicated (AdamW)
+        // weights and the matrices this rank owns; broadcast each owned
+        // matrix from its owner (weight order, the same on every rank); then
+        // refresh the working copies of the matrices received.
+        int ra = region_begin(m, "allreduce");
+        if (nb) cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 1], 0);
+        region_end(m, ra);
+        std::vector<char> mine(nw, 0), received(nw, 1);
+        for (size_t w = 0; w < nw; w++) {
+            mine[w] = m->owner[w] < 0 || m->owner[w] == m->rank;
+            if (m->owner[w] >= 0 && m->owner[w] != m->rank) received[w] = 0;
+        }
+        int ro = region_begin(m, "optimizer");
+        if (optimizer_step(m, lr, &mine)) return -1;
+        region_end(m, ro);
+        int rb = region_begin(m, "broadcast");
+        const size_t before = m->bucket_done.size();
+        for (size_t w = 0; w < nw; w++)
+            if (m->owner[w] >= 0 &&
+                dist_collective(m, m->spec.weights[w].off, m->spec.weights[w].count, m->owner[w], true))
+                return -1;
+        if (m->bucket_done.size() > before) cudaStreamWaitEvent(m->stream, m->bucket_done.back(), 0);
+        region_end(m, rb);
+        return refresh_working(m, &received);
+    }
     if (nb >= 2) {
         std::vector<char> early(nw, 0);
         for (size_t b = 0; b + 1 < nb; b++)
@@ -1524,7 +1590,7 @@ static int upload_weights(ns_model* m) {
         return fail("weight upload failed");
     if (m->d_active && !m->moe_active.empty())
         cudaMemcpy(m->d_active, m->moe_active.data(), m->moe_active.size(), cudaMemcpyHostToDevice);
-    if (refresh_working(m)) return -1;
+    if (refresh_working(m, nullptr)) return -1;
     return finish(m);
 }
 
@@ -1709,7 +1775,7 @@ int nsb_set_precision(ns_model* m, int mode) {
     free_plan(m);
     m->precision = mode;
     m->wdt = mode == 2 ? kBF16 : kF32;
-    if (alloc_working(m) || refresh_working(m)) return -1;
+    if (alloc_working(m) || refresh_working(m, nullptr)) return -1;
     return finish(m);
 }
 
@@ -1767,6 +1833,7 @@ static int rows_of(const ns_model* m, size_t input_numel) {
 int nsb_eval_infer_device(ns_model* m, const float* d_input, float* d_output, size_t input_numel, void* stream) {
     if (!m) return -1;
     g_err.clear();
+    if (!m->reps.empty()) return fail("device-pointer entries take single-GPU models (NS_B200_GPUS unset)");
     const long long l0 = launch_counter();
     const int M = rows_of(m, input_numel);
     if (M <= 0) return 0;
@@ -1852,7 +1919,7 @@ static int eval_pipelined(ns_model* m, const float* input, float* output, int M,
     return 0;
 }
 
-int nsb_eval_infer(ns_model* m, const float* input, float* output, size_t input_numel) {
+static int eval_infer_one(ns_model* m, const float* input, float* output, size_t input_numel) {
     if (!m) return -1;
     g_err.clear();
     const long long l0 = launch_counter();
@@ -1982,22 +2049,35 @@ static int train_entry(ns_model* m, const float* input, const float* labels, con
     return 0;
 }
 
+static int multi_train(ns_model* m, const float* input, const float* labels, const int* targets, size_t input_numel,
+                       float* loss_out, float lr, bool train);
+static int multi_infer(ns_model* m, const float* input, float* output, size_t input_numel);
+
+int nsb_eval_infer(ns_model* m, const float* input, float* output, size_t input_numel) {
+    if (m && !m->reps.empty()) return multi_infer(m, input, output, input_numel);
+    return eval_infer_one(m, input, output, input_numel);
+}
+
 int nsb_runtime_train_step(ns_model* m, const float* input, const float* labels, size_t input_numel, float* loss_out,
                            float lr) {
+    if (m && !m->reps.empty()) return multi_train(m, input, labels, nullptr, input_numel, loss_out, lr, true);
     return train_entry(m, input, labels, nullptr, input_numel, loss_out, lr, true, false, nullptr);
 }
 
 int nsb_runtime_train_step_idx(ns_model* m, const float* input, const int* targets, size_t input_numel,
                                float* loss_out, float lr) {
+    if (m && !m->reps.empty()) return multi_train(m, input, nullptr, targets, input_numel, loss_out, lr, true);
     return train_entry(m, input, nullptr, targets, input_numel, loss_out, lr, true, false, nullptr);
 }
 
 int nsb_train_step_device(ns_model* m, const float* d_input, const float* d_labels, const int* d_targets,
                           size_t input_numel, float* loss_out, float lr, void* stream) {
+    if (m && !m->reps.empty()) return fail("device-pointer entries take single-GPU models (NS_B200_GPUS unset)");
     return train_entry(m, d_input, d_labels, d_targets, input_numel, loss_out, lr, true, true, stream);
 }
 
 int nsb_objective_loss(ns_model* m, const float* input, const float* labels, size_t input_numel, float* loss_out) {
+    if (m && !m->reps.empty()) return multi_train(m, input, labels, nullptr, input_numel, loss_out, 0.f, false);
     return train_entry(m, input, labels, nullptr, input_numel, loss_out, 0.f, false, false, nullptr);
 }
 
@@ -2139,6 +2219,29 @@ size_t nsb_expert_birth(ns_model* m, int n) {
 }
 
 // ---- data parallel ----------------------------------------------------------
+}  // extern "C"
+
+// Muon matrices are sharded over the ranks: matrix k (in weight order) is
+// updated by rank k % world only. NS_B200_SHARD_MUON=0 keeps every update
+// replicated.
+static bool takes_muon(const ns_model* m, const WeightInfo& w) {
+    const std::string& mode = m->spec.optimizer;
+    const int mn = w.rows < w.cols ? w.rows : w.cols;
+    return (mode == "reference" || mode == "muon") && w.rows > 1 && w.cols > 1 && mn >= 8;
+}
+
+void assign_owners(ns_model* m) {
+    const char* e = getenv("NS_B200_SHARD_MUON");
+    const bool on = !(e && e[0] == '0');
+    m->owner.assign(m->spec.weights.size(), -1);
+    if (!on || m->world <= 1) return;
+    int k = 0;
+    for (size_t w = 0; w < m->spec.weights.size(); w++)
+        if (takes_muon(m, m->spec.weights[w])) m->owner[w] = k++ % m->world;
+}
+
+extern "C" {
+
 int nsb_dist_unique_id(void* id128) {
     if (!id128) return -1;
     if (!nccl().ok) return fail("libnccl.so.2 not loadable");
@@ -2198,6 +2301,7 @@ int nsb_dist_init(ns_model* m, int rank, int world, const void* id128, int timeo
     m->comm = comm;
     m->rank = rank;
     m->world = world;
+    assign_owners(m);
     return 0;
 }
 

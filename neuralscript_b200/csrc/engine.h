@@ -81,8 +81,17 @@ struct Op {
 
 }  // namespace nsb
 
+namespace nsb {
+struct ReplicaPool;
+}
+
 struct ns_model {
     nsb::Spec spec;
+    // In-call multi-GPU (NS_B200_GPUS=N at init): the model on the first
+    // device holds replicas on the others, joined by NCCL, and one worker
+    // thread per replica; every ABI call splits its rows over all of them.
+    std::vector<ns_model*> reps;
+    nsb::ReplicaPool* pool = nullptr;
     int device = 0;
     cudaStream_t stream = nullptr;
     int* d_err = nullptr;
@@ -147,6 +156,7 @@ struct ns_model {
     std::vector<char> reduced;             // per weight: its all-reduce was issued this step
     std::vector<std::pair<int, int>> bucket_w;  // weight ranges in all-reduce issue order
     std::vector<cudaEvent_t> bucket_done;       // recorded on the comm stream after each range
+    std::vector<int> owner;  // per weight: rank that updates it (sharded Muon) or -1 (replicated update)
     int timeout_ms = 60000;
     long long launches = 0;
     // per-region CUDA-event timing on the engine stream (opt-in)

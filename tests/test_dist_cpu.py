@@ -125,3 +125,75 @@ def test_peer_failure_is_detected_by_the_survivor():
     for p in ps:
         p.join(timeout=120)
     assert q.get(timeout=5) != "no-error"
+
+
+MUON_SPEC = """network MU
+input 32
+layer fc1 dense in=32 out=32 act=relu
+layer fc2 dense in=32 out=32 act=relu
+layer fc3 dense in=32 out=32
+h1 = fc1(x)
+h2 = fc2(h1)
+y = fc3(h2)
+output y
+loss mse
+optimizer muon momentum=0.95 steps=5 decay=0.01
+"""
+
+
+def _muon_worker(rank, world, port, q):
+    """The sharded Muon step the engine runs under data parallelism: each
+    rank's gradient (global-row seed) is SUM-reduced to the matrix's owner
+    (matrix k owned by rank k % world), the owner alone applies momentum,
+    Newton-Schulz-5 and the update, then broadcasts the new matrix."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        w = make_weights(MUON_SPEC, 711, default_sd=0.18)
+        x = synth.normal(64 * 32, 712, 0.0, 1.0)
+        t = synth.normal(64 * 32, 713, 0.0, 1.0)
+        rows = 64 // world
+        sl = slice(rank * rows * 32, (rank + 1) * rows * 32)
+        m = OracleModel(MUON_SPEC, w)
+        layout = m.s.layout()
+        for step in range(3):
+            out, vals, cache = m.forward(x[sl], keep=True)
+            _, seed = m._loss_and_seed(out, t[sl].reshape(out.shape), 64 * 32)
+            g = m.backward(vals, cache, seed)
+            upd = {}
+            for k, (name, off, cnt, _) in enumerate(layout):
+                owner = k % world
+                gk = torch.from_numpy(np.ascontiguousarray(g[name], np.float32).reshape(-1))
+                dist.reduce(gk, dst=owner)
+                if rank == owner:
+                    upd[name] = gk.numpy()
+            m.apply(upd, 0.02)  # the owner updates only its matrices
+            for k, (name, off, cnt, _) in enumerate(layout):
+                wk = torch.from_numpy(m.w[off:off + cnt].copy())
+                dist.broadcast(wk, src=k % world)
+                m.w[off:off + cnt] = wk.numpy()
+        if rank == 0:
+            ref = OracleModel(MUON_SPEC, w)
+            for step in range(3):
+                ref.train_step(x, t, 0.02)
+            err = float(np.linalg.norm(m.w - ref.w) / np.linalg.norm(ref.w))
+            q.put(("ok", err))
+        else:
+            q.put(("done", 0.0))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_muon_decomposition_equals_full_batch_step():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_muon_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    res = [q.get(timeout=5) for _ in range(2)]
+    ok = [r for r in res if r[0] == "ok"][0]
+    assert ok[1] < 1e-4, ok

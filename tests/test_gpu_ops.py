@@ -138,11 +138,13 @@ def test_data_movement_kernels_match_reference_helpers():
     assert np.array_equal(run("nsb_op_scatter", (R_, C_), P(X), 0, R_, C_, P(i4), 4, P(Z), None),
                           G["dm_scatterrows"])
     # an index outside the source reads 0 (the reference reads out of bounds)
-    oob = run("nsb_op_index", (R_, 2), P(X), 1, R_, C_, P(ix([1, 11])), 2, None)
+    i5 = ix([1, 11])  # held: the kernel reads it after the output is allocated
+    oob = run("nsb_op_index", (R_, 2), P(X), 1, R_, C_, P(i5), 2, None)
     assert np.array_equal(oob[:, 0], G["dm_x"][:, 1]) and np.all(oob[:, 1] == 0)
     # a large transpose (several 32 x 32 tiles, ragged edges)
     big = synth.normal(1000 * 777, 41, 0, 1).reshape(1000, 777)
-    assert np.array_equal(run("nsb_op_transpose", (777, 1000), P(dev(big)), 1000, 777, None), big.T)
+    bigd = dev(big)
+    assert np.array_equal(run("nsb_op_transpose", (777, 1000), P(bigd), 1000, 777, None), big.T)
 
 
 OPS_NET = """network OPS
