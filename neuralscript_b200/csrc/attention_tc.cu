@@ -660,10 +660,13 @@ bool attention_tc_supported(const AttnArgs& a) {
 int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
     CUtensorMap m;
     if (!bf16_tmap(&m, a.qkv, 3LL * a.D, (long long)a.B * a.S, a.ld_qkv)) return -2;
-    static bool attr = false;
-    if (!attr) {
+    static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to the current one
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) return -1;
+    if (!attr[dev]) {
         cudaFuncSetAttribute(attn_tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-        attr = true;
+        attr[dev] = true;
     }
     const int items = a.B * a.H * ((a.S + kQ - 1) / kQ);
     const int grid = items < num_sms() ? items : num_sms();
@@ -684,10 +687,13 @@ int attention_tc_bwd(const AttnArgs& a, cudaStream_t s, int* err) {
     if (!bf16_tmap(&mq, a.qkv, 3LL * a.D, rows, a.ld_qkv) || !bf16_tmap(&mo, a.dctx, a.D, rows, a.ld_dctx) ||
         !bf16_tmap(&mc, a.ctx, a.D, rows, a.ld_ctx) || !bf16_tmap(&md, a.dqkv, 3LL * a.D, rows, a.ld_dqkv))
         return -2;
-    static bool attr = false;
-    if (!attr) {
+    static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to the current one
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) return -1;
+    if (!attr[dev]) {
         cudaFuncSetAttribute(attn_tc_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
-        attr = true;
+        attr[dev] = true;
     }
     dim3 grid(a.H, a.B);
     attn_tc_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(

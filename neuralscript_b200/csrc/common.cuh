@@ -8,6 +8,9 @@
 
 namespace nsb {
 
+// Upper bound on device ordinals for per-device caches (kernel attributes).
+constexpr int kMaxDevices = 64;
+
 // Device error codes written into the per-context error word.
 enum DevErr : int {
     kErrNone = 0,

@@ -89,12 +89,28 @@ __global__ void binop_bwd_kernel(const float* __restrict__ d, const float* __res
     }
 }
 
+// Multipliers of the local elements 4 q .. 4 q + 3 (batch elements base +
+// 4 q ..): one Philox block when base is a multiple of 4, else two.
+__device__ __forceinline__ void local_mask4(const DropoutSite& d, size_t q, float m[4]) {
+    const unsigned long long g0 = d.base + 4ull * q;
+    if ((g0 & 3ull) == 0) {
+        dropout_mask4(d, g0 >> 2, m);
+        return;
+    }
+    float a[4], b[4];
+    dropout_mask4(d, g0 >> 2, a);
+    dropout_mask4(d, (g0 >> 2) + 1, b);
+    const int sh = (int)(g0 & 3ull);
+#pragma unroll
+    for (int j = 0; j < 4; j++) m[j] = j + sh < 4 ? a[j + sh] : b[j + sh - 4];
+}
+
 __global__ void dropout_fwd_kernel(const float* __restrict__ x, size_t n, DropoutSite d, float* __restrict__ o32,
                                    __nv_bfloat16* __restrict__ o16, int vec) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x; 4 * q < n; q += stride) {
         float m[4];
-        dropout_mask4(d, q, m);
+        local_mask4(d, q, m);
         if (vec) {
             const float4 v = reinterpret_cast<const float4*>(x)[q];
             store4(o32, o16, 4 * q, make_float4(v.x * m[0], v.y * m[1], v.z * m[2], v.w * m[3]));
@@ -113,7 +129,7 @@ __global__ void dropout_bwd_kernel(const float* __restrict__ dy, size_t n, Dropo
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x; 4 * q < n; q += stride) {
         float m[4];
-        dropout_mask4(d, q, m);
+        local_mask4(d, q, m);
         for (int j = 0; j < 4 && 4 * q + j < n; j++) {
             const size_t i = 4 * q + j;
             const float g = dy[i] * m[j];

@@ -25,14 +25,18 @@ int binop_bwd(const float* dout, const float* a, const float* b, size_t n, int c
 // ---- counter-based dropout (Philox4x32-10) ---------------------------------
 // Element i of a dropout site keeps its value with probability 1 - rate and
 // is then scaled by 1 / (1 - rate). The keep decision is a pure function of
-// (key, site, step, i): uniform(i) = top 24 bits of word (i % 4) of
-// Philox4x32-10(counter = {i / 4 low, i / 4 high, step, site}, key) / 2^24,
-// kept when uniform >= rate. The backward regenerates the same mask.
+// (key, site, step, g) with g = base + i the element's index in the whole
+// batch: uniform(g) = top 24 bits of word (g % 4) of
+// Philox4x32-10(counter = {g / 4 low, g / 4 high, step, site}, key) / 2^24,
+// kept when uniform >= rate. The backward regenerates the same mask, and a
+// batch split over data-parallel ranks (base = the rank's first row times
+// the width) draws exactly the masks of the unsplit batch.
 struct DropoutSite {
     float rate = 0.f;
     uint32_t key0 = 0, key1 = 0;  // model seed
     uint32_t step = 0;            // training step (advances every train call)
     uint32_t site = 0;            // which dropout op of the network
+    unsigned long long base = 0;  // index of element 0 in the whole batch
 };
 
 __host__ __device__ __forceinline__ void philox_round(uint32_t c[4], uint32_t k0, uint32_t k1) {
@@ -59,7 +63,7 @@ __host__ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k
     }
 }
 
-// Keep multipliers (0 or 1 / (1 - rate)) of the four elements 4 q .. 4 q + 3.
+// Keep multipliers (0 or 1 / (1 - rate)) of the four batch elements 4 q .. 4 q + 3.
 __host__ __device__ __forceinline__ void dropout_mask4(const DropoutSite& d, unsigned long long q, float m[4]) {
     uint32_t c[4] = {(uint32_t)q, (uint32_t)(q >> 32), d.step, d.site};
     philox4x32_10(c, d.key0, d.key1);

@@ -724,6 +724,8 @@ static int forward(ns_model* m, int M, bool train) {
                 d.key1 = m->drop_key1;
                 d.step = m->drop_step;
                 d.site = (uint32_t)op.drop_site;
+                // data parallel: this rank's rows follow rank x M rows of the batch
+                d.base = (unsigned long long)m->rank * (unsigned long long)M * (unsigned long long)in.cols;
                 launch_counter() += 1;
                 rc = dropout_fwd(in.f32, (size_t)M * in.cols, d, out.f32, out.h16, m->stream);
                 break;
@@ -825,6 +827,7 @@ static int dist_reduce_weights(ns_model* m, int w0, int w1) {
         if (m->reduced[w]) return 0;
     for (int w = w0; w < w1; w++) m->reduced[w] = 1;
     m->bucket_w.push_back(std::make_pair(w0, w1));
+    const size_t ev0 = m->bucket_done.size();
     int w = w0;
     while (w < w1) {
         const int own = m->owner.empty() ? -1 : m->owner[w];
@@ -842,6 +845,8 @@ static int dist_reduce_weights(ns_model* m, int w0, int w1) {
         if (dist_reduce_range(m, off, end - off)) return -1;
         w = e;
     }
+    // completion of the bucket = completion of its last collective
+    m->bucket_evt.push_back(m->bucket_done.size() > ev0 ? m->bucket_done.back() : nullptr);
     return 0;
 }
 
@@ -865,6 +870,7 @@ static int dist_reduce_finish(ns_model* m) {
     if (nw == 0) {
         m->bucket_w.push_back(std::make_pair(0, 0));
         if (dist_reduce_range(m, s.total, 1)) return -1;
+        m->bucket_evt.push_back(m->bucket_done.back());
     }
     return 0;
 }
@@ -884,7 +890,7 @@ static int dist_optimizer(ns_model* m, float lr) {
         // matrix from its owner (weight order, the same on every rank); then
         // refresh the working copies of the matrices received.
         int ra = region_begin(m, "allreduce");
-        if (nb) cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 1], 0);
+        if (!m->bucket_done.empty()) cudaStreamWaitEvent(m->stream, m->bucket_done.back(), 0);
         region_end(m, ra);
         std::vector<char> mine(nw, 0), received(nw, 1);
         for (size_t w = 0; w < nw; w++) {
@@ -908,12 +914,13 @@ static int dist_optimizer(ns_model* m, float lr) {
         std::vector<char> early(nw, 0);
         for (size_t b = 0; b + 1 < nb; b++)
             for (int w = m->bucket_w[b].first; w < m->bucket_w[b].second; w++) early[w] = 1;
-        cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 2], 0);
+        // (collectives complete in issue order on the one communication stream)
+        if (m->bucket_evt[nb - 2]) cudaStreamWaitEvent(m->stream, m->bucket_evt[nb - 2], 0);
         int ro = region_begin(m, "optimizer");
         if (optimizer_step(m, lr, &early)) return -1;
         region_end(m, ro);
         int ra = region_begin(m, "allreduce");  // what is left to wait for
-        cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 1], 0);
+        cudaStreamWaitEvent(m->stream, m->bucket_done.back(), 0);
         region_end(m, ra);
         std::vector<char> late(nw, 0);
         for (size_t w = 0; w < nw; w++) late[w] = !early[w];
@@ -923,7 +930,7 @@ static int dist_optimizer(ns_model* m, float lr) {
         return 0;
     }
     int ra = region_begin(m, "allreduce");
-    if (nb) cudaStreamWaitEvent(m->stream, m->bucket_done[nb - 1], 0);
+    if (!m->bucket_done.empty()) cudaStreamWaitEvent(m->stream, m->bucket_done.back(), 0);
     region_end(m, ra);
     int ro = region_begin(m, "optimizer");
     if (optimizer_step(m, lr)) return -1;
@@ -1239,6 +1246,7 @@ static int backward(ns_model* m, int M) {
                     d.key1 = m->drop_key1;
                     d.step = m->drop_step;
                     d.site = (uint32_t)op.drop_site;
+                    d.base = (unsigned long long)m->rank * (unsigned long long)M * (unsigned long long)in.cols;
                     launch_counter() += 1;
                     rc = dropout_bwd(dv, (size_t)M * in.cols, d, in.gcur, in.gbuf, m->stream);
                     in.gcur = in.gbuf;
@@ -1648,7 +1656,7 @@ const ns_weight_layout* nsb_spec_layout(const char* spec) {
     return s ? &s->layout : nullptr;
 }
 
-ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_floats) {
+static ns_model* init_one(const char* spec, const float* weights, size_t num_floats) {
     g_err.clear();
     if (!spec || !weights) {
         fail("null spec or weights");
@@ -1724,8 +1732,27 @@ ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_fl
     return m;
 }
 
+static void multi_detach(ns_model* m);
+static int multi_attach(ns_model* m, const char* spec, const float* weights, size_t n, int gpus);
+
+ns_model* nsb_runtime_init(const char* spec, const float* weights, size_t num_floats) {
+    ns_model* m = init_one(spec, weights, num_floats);
+    if (!m) return nullptr;
+    // NS_B200_GPUS=N: this model also drives the next N-1 devices
+    const char* e = getenv("NS_B200_GPUS");
+    const int gpus = e ? atoi(e) : 1;
+    if (gpus > 1 && multi_attach(m, spec, weights, num_floats, gpus)) {
+        const std::string err = g_err;
+        nsb_free(m);
+        fail(err);
+        return nullptr;
+    }
+    return m;
+}
+
 void nsb_free(ns_model* m) {
     if (!m) return;
+    multi_detach(m);
     if (m->stream) cudaStreamSynchronize(m->stream);
     free_plan(m);
     free_working(m);
@@ -1768,8 +1795,11 @@ int nsb_model_get_weights(const ns_model* m, float* out, size_t n) {
     return 0;
 }
 
+static int for_replicas(ns_model* m, const std::function<int(ns_model*)>& fn);
+
 int nsb_set_precision(ns_model* m, int mode) {
     if (!m || mode < 0 || mode > 2) return -1;
+    if (!m->reps.empty() && for_replicas(m, [mode](ns_model* r) { return nsb_set_precision(r, mode); })) return -1;
     if (mode == m->precision) return 0;
     cudaStreamSynchronize(m->stream);
     free_plan(m);
@@ -1781,7 +1811,12 @@ int nsb_set_precision(ns_model* m, int mode) {
 
 int nsb_get_precision(const ns_model* m) { return m ? m->precision : -1; }
 
-long long nsb_last_launch_count(const ns_model* m) { return m ? m->launches : 0; }
+long long nsb_last_launch_count(const ns_model* m) {
+    if (!m) return 0;
+    long long n = m->launches;
+    for (const ns_model* r : m->reps) n += r->launches;
+    return n;
+}
 
 int nsb_region_timing(ns_model* m, int enable) {
     if (!m) return -1;
@@ -1819,6 +1854,25 @@ int nsb_model_get_gradients(const ns_model* m, float* out, size_t n) {
 int nsb_model_get_input_gradient(const ns_model* m, float* out, size_t n) {
     if (!m || !out) return -1;
     if (!m->spec.input_grad) return fail("the spec has no 'grad input' statement");
+    if (!m->reps.empty()) {
+        // the rows of all replicas, in call order
+        size_t total = (size_t)m->last_rows;
+        for (const ns_model* r : m->reps) total += (size_t)r->last_rows;
+        const size_t w = (size_t)m->spec.in_cols;
+        if (n != total * w) return fail("size mismatch");
+        size_t off = 0;
+        for (int i = -1; i < (int)m->reps.size(); i++) {
+            const ns_model* r = i < 0 ? m : m->reps[i];
+            if (!r->last_rows) continue;
+            if (!r->vals[0].gcur) return fail("no train step has formed an input gradient yet");
+            cudaStreamSynchronize(r->stream);
+            if (cudaMemcpy(out + off, r->vals[0].gcur, sizeof(float) * r->last_rows * w, cudaMemcpyDeviceToHost) !=
+                cudaSuccess)
+                return -1;
+            off += (size_t)r->last_rows * w;
+        }
+        return 0;
+    }
     const Val& x = m->vals[0];
     if (!m->last_rows || !x.gcur) return fail("no train step has formed an input gradient yet");
     if (n != (size_t)m->last_rows * m->spec.in_cols) return fail("size mismatch");
@@ -1967,6 +2021,7 @@ static int train_core(ns_model* m, int M, const float* d_labels, const int* d_ta
             m->ev_next = 0;
             m->bucket_w.clear();
             m->bucket_done.clear();
+            m->bucket_evt.clear();
         }
         if (backward(m, M)) return -1;
         if (dist_active(m)) {
@@ -2103,6 +2158,7 @@ int nsb_save_checkpoint(const ns_model* m, const char* path) {
 
 int nsb_load_checkpoint(ns_model* m, const char* path) {
     if (!m || !path) return -1;
+    if (!m->reps.empty() && for_replicas(m, [path](ns_model* r) { return nsb_load_checkpoint(r, path); })) return -1;
     FILE* fp = fopen(path, "rb");
     if (!fp) return -1;
     unsigned magic = 0;
@@ -2160,6 +2216,7 @@ size_t nsb_expert_count(const ns_model* m) { return m ? m->moe_active_count : 0;
 
 size_t nsb_expert_kill(ns_model* m, int k) {
     if (!m || m->moe_layer < 0) return m ? m->moe_active_count : 0;
+    if (!m->reps.empty()) for_replicas(m, [k](ns_model* r) { nsb_expert_kill(r, k); return 0; });
     if (k < 0 || k >= (int)m->moe_active.size() || !m->moe_active[k]) return m->moe_active_count;
     m->moe_active[k] = 0;
     m->moe_active_count--;
@@ -2170,6 +2227,7 @@ size_t nsb_expert_kill(ns_model* m, int k) {
 size_t nsb_expert_merge(ns_model* m, int a, int b) {
     MoeGeom g;
     if (!m || !moe_geom(m, g)) return m ? m->moe_active_count : 0;
+    if (!m->reps.empty()) for_replicas(m, [a, b](ns_model* r) { nsb_expert_merge(r, a, b); return 0; });
     const int cap = (int)g.cap;
     if (a < 0 || b < 0 || a == b || a >= cap || b >= cap || !m->moe_active[a] || !m->moe_active[b])
         return m->moe_active_count;
@@ -2192,6 +2250,8 @@ size_t nsb_expert_merge(ns_model* m, int a, int b) {
 size_t nsb_expert_birth(ns_model* m, int n) {
     MoeGeom g;
     if (!m || !moe_geom(m, g) || n <= 0) return m ? m->moe_active_count : 0;
+    // every replica draws the same sources and noise (same generator state)
+    if (!m->reps.empty()) for_replicas(m, [n](ns_model* r) { nsb_expert_birth(r, n); return 0; });
     if (m->moe_active_count >= g.cap) return m->moe_active_count;
     sync_host(m);
     float* w = m->h_w.data();
@@ -2251,8 +2311,17 @@ int nsb_dist_unique_id(void* id128) {
     return 0;
 }
 
+static int dist_init_one(ns_model* m, int rank, int world, const void* id128, int timeout_ms);
+
 int nsb_dist_init(ns_model* m, int rank, int world, const void* id128, int timeout_ms) {
     if (!m || !id128 || world < 1 || rank < 0 || rank >= world) return -1;
+    if (!m->reps.empty()) return fail("a model driving several GPUs in-call cannot also join a process group");
+    return dist_init_one(m, rank, world, id128, timeout_ms);
+}
+
+}  // extern "C"
+
+static int dist_init_one(ns_model* m, int rank, int world, const void* id128, int timeout_ms) {
     m->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
     if (world == 1) {
         m->world = 1;
@@ -2305,4 +2374,226 @@ int nsb_dist_init(ns_model* m, int rank, int world, const void* id128, int timeo
     return 0;
 }
 
-}  // extern "C"
+// ---------------------------------------------------------------------------
+// In-call multi-GPU: the reference host calls ns_runtime_train_step /
+// ns_eval_infer once with the whole batch; with NS_B200_GPUS=N set at
+// ns_runtime_init the model holds N-1 replicas on the next devices, joined
+// with it by NCCL (the data-parallel path above: gradients all-reduced,
+// Muon matrices sharded). Each call splits the caller's rows (in whole
+// attention sequences) over the N models, which run at the same time, the
+// lead on the calling thread and each replica on a worker thread of its own;
+// each copies its slice of the host buffers straight in and out.
+// ---------------------------------------------------------------------------
+namespace nsb {
+
+struct ReplicaWorker {
+    std::thread th;
+    std::mutex mu;
+    std::condition_variable cv;
+    std::function<int()> job;
+    bool has_job = false, done = false, quit = false;
+    int rc = 0;
+    std::string err;
+    int device = 0;
+
+    void loop() {
+        cudaSetDevice(device);
+        for (;;) {
+            std::function<int()> j;
+            {
+                std::unique_lock<std::mutex> lk(mu);
+                cv.wait(lk, [&] { return has_job || quit; });
+                if (!has_job) return;
+                j = std::move(job);
+                has_job = false;
+            }
+            g_err.clear();
+            const int r = j();
+            std::lock_guard<std::mutex> g(mu);
+            rc = r;
+            err = g_err;
+            done = true;
+            cv.notify_all();
+        }
+    }
+    void post(std::function<int()> f) {
+        std::lock_guard<std::mutex> g(mu);
+        job = std::move(f);
+        has_job = true;
+        done = false;
+        cv.notify_all();
+    }
+    int wait(std::string& e) {
+        std::unique_lock<std::mutex> lk(mu);
+        cv.wait(lk, [&] { return done; });
+        e = err;
+        return rc;
+    }
+};
+
+struct ReplicaPool {
+    std::vector<std::unique_ptr<ReplicaWorker>> w;
+};
+
+}  // namespace nsb
+
+// fn(model, index) on the lead (index 0, calling thread, lead device
+// current) and on every replica (its worker thread) at the same time.
+static int run_all(ns_model* m, const std::function<int(ns_model*, int)>& fn) {
+    const size_t n = m->reps.size();
+    for (size_t i = 0; i < n; i++) {
+        ns_model* r = m->reps[i];
+        m->pool->w[i]->post([&fn, r, i] { return fn(r, (int)i + 1); });
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->device);
+    int rc = fn(m, 0);
+    std::string err = rc ? g_err : std::string();
+    for (size_t i = 0; i < n; i++) {
+        std::string e;
+        if (m->pool->w[i]->wait(e) && !rc) {
+            rc = -1;
+            err = "GPU " + std::to_string(m->reps[i]->device) + ": " + e;
+        }
+    }
+    cudaSetDevice(prev);
+    if (rc) return fail(err);
+    return 0;
+}
+
+// fn on every replica (not the lead), each on its worker thread.
+static int for_replicas(ns_model* m, const std::function<int(ns_model*)>& fn) {
+    return run_all(m, [&fn](ns_model* r, int i) { return i == 0 ? 0 : fn(r); });
+}
+
+static int multi_attach(ns_model* m, const char* spec, const float* weights, size_t n, int gpus) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || gpus > count)
+        return fail("NS_B200_GPUS=" + std::to_string(gpus) + " but " + std::to_string(count) + " GPUs are visible");
+    if (!nccl().ok) return fail("libnccl.so.2 not loadable");
+    for (const auto& l : m->spec.layers)
+        if (l.kind == "attention" && l.geti("seq", 0) <= 0)
+            return fail("NS_B200_GPUS: attention over the whole call (seq 0) cannot be split across GPUs");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    m->pool = new nsb::ReplicaPool();
+    for (int i = 1; i < gpus; i++) {
+        const int dev = (m->device + i) % count;
+        cudaSetDevice(dev);
+        ns_model* r = init_one(spec, weights, n);
+        if (!r) {
+            cudaSetDevice(prev);
+            return -1;
+        }
+        nsb_set_precision(r, m->precision);
+        m->reps.push_back(r);
+        auto w = std::unique_ptr<nsb::ReplicaWorker>(new nsb::ReplicaWorker());
+        w->device = dev;
+        nsb::ReplicaWorker* wp = w.get();
+        w->th = std::thread([wp] { wp->loop(); });
+        m->pool->w.push_back(std::move(w));
+    }
+    cudaSetDevice(prev);
+    // one communicator per device, all ranks joining at once
+    ncclUniqueId id;
+    if (nccl().GetUniqueId(&id) != ncclSuccess) return fail("ncclGetUniqueId failed");
+    const int timeout = 60000;
+    return run_all(m, [&id, gpus, timeout](ns_model* r, int rank) {
+        return dist_init_one(r, rank, gpus, &id, timeout);
+    });
+}
+
+static void multi_detach(ns_model* m) {
+    if (!m->pool) return;
+    for (auto& w : m->pool->w) {
+        {
+            std::lock_guard<std::mutex> g(w->mu);
+            w->quit = true;
+            w->cv.notify_all();
+        }
+        if (w->th.joinable()) w->th.join();
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    for (ns_model* r : m->reps) {
+        cudaSetDevice(r->device);
+        nsb_free(r);
+    }
+    cudaSetDevice(prev);
+    m->reps.clear();
+    delete m->pool;
+    m->pool = nullptr;
+}
+
+// Rows of one indivisible unit: an attention sequence, else a row.
+static int split_unit(const ns_model* m) {
+    int unit = 1;
+    for (const auto& l : m->spec.layers)
+        if (l.kind == "attention") unit = (int)l.geti("seq", 1);
+    return unit > 0 ? unit : 1;
+}
+
+// [row0, rows) per model: whole units, as even as possible, in call order.
+static std::vector<std::pair<int, int>> split_rows(const ns_model* m, int M) {
+    const int parts = 1 + (int)m->reps.size(), unit = split_unit(m);
+    const int units = M / unit, base = units / parts, extra = units % parts;
+    std::vector<std::pair<int, int>> out;
+    int r0 = 0;
+    for (int i = 0; i < parts; i++) {
+        int rows = (base + (i < extra ? 1 : 0)) * unit;
+        if (i == parts - 1) rows = M - r0;  // a ragged tail (not whole units) stays with the last
+        out.push_back(std::make_pair(r0, rows));
+        r0 += rows;
+    }
+    return out;
+}
+
+static int multi_infer(ns_model* m, const float* input, float* output, size_t input_numel) {
+    g_err.clear();
+    const int M = rows_of(m, input_numel);
+    if (M <= 0) return 0;
+    if (!input || !output) return fail("null input/output");
+    const auto parts = split_rows(m, M);
+    const int in_cols = m->spec.in_cols, out_cols = m->spec.out_cols;
+    return run_all(m, [&](ns_model* r, int i) {
+        const int r0 = parts[i].first, rows = parts[i].second;
+        if (rows <= 0) return 0;
+        return eval_infer_one(r, input + (size_t)r0 * in_cols, output + (size_t)r0 * out_cols,
+                              (size_t)rows * in_cols);
+    });
+}
+
+static int multi_train(ns_model* m, const float* input, const float* labels, const int* targets, size_t input_numel,
+                       float* loss_out, float lr, bool train) {
+    g_err.clear();
+    const int M = rows_of(m, input_numel);
+    const int parts_n = 1 + (int)m->reps.size(), unit = split_unit(m);
+    if (M <= 0) return fail("empty batch");
+    if (!input || (!labels && !targets)) return fail("null input/labels");
+    if (train && M % (parts_n * unit) != 0)
+        return fail("NS_B200_GPUS: a train step's rows must split evenly over the GPUs in whole sequences (" +
+                    std::to_string(M) + " rows, " + std::to_string(parts_n) + " GPUs, unit " + std::to_string(unit) +
+                    ")");
+    const auto parts = split_rows(m, M);
+    const int in_cols = m->spec.in_cols, out_cols = m->spec.out_cols;
+    std::vector<float> losses(parts_n, 0.f);
+    const int rc = run_all(m, [&](ns_model* r, int i) {
+        const int r0 = parts[i].first, rows = parts[i].second;
+        if (rows <= 0) return 0;  // inference-only objective: nothing to do
+        return train_entry(r, input + (size_t)r0 * in_cols, labels ? labels + (size_t)r0 * out_cols : nullptr,
+                           targets ? targets + r0 : nullptr, (size_t)rows * in_cols, loss_out ? &losses[i] : nullptr,
+                           lr, train, false, nullptr);
+    });
+    if (rc) return -1;
+    if (loss_out) {
+        if (train) {
+            *loss_out = losses[0];  // the loss sum rode the all-reduce: every rank holds the global mean
+        } else {
+            double s = 0.0;  // per-model means over their rows, weighted by rows
+            for (int i = 0; i < parts_n; i++) s += (double)losses[i] * parts[i].second;
+            *loss_out = (float)(s / M);
+        }
+    }
+    return 0;
+}

@@ -155,7 +155,8 @@ struct ns_model {
     size_t ev_next = 0;
     std::vector<char> reduced;             // per weight: its all-reduce was issued this step
     std::vector<std::pair<int, int>> bucket_w;  // weight ranges in all-reduce issue order
-    std::vector<cudaEvent_t> bucket_done;       // recorded on the comm stream after each range
+    std::vector<cudaEvent_t> bucket_done;       // recorded on the comm stream after each collective
+    std::vector<cudaEvent_t> bucket_evt;        // per bucket (bucket_w): its last collective's event
     std::vector<int> owner;  // per weight: rank that updates it (sharded Muon) or -1 (replicated update)
     int timeout_ms = 60000;
     long long launches = 0;

@@ -1028,10 +1028,14 @@ static cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const
                              cudaStream_t s) {
     using C = TcCfg<BN, TF32>;
     auto k = gemm_tc_kernel<BN, TF32, A_MN, B_MN>;
-    static bool attr = false;
-    if (!attr) {
+    // the attribute belongs to the current device: set it once per device
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!attr[dev]) {
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        attr = true;
+        attr[dev] = true;
     }
     // one CTA per unit; running CTAs take over the units of CTAs not yet
     // launched (static scheduling: one CTA per SM, units round-robin)
