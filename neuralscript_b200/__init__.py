@@ -110,6 +110,11 @@ def _ptr(a: np.ndarray) -> C.c_void_p:
     return C.c_void_p(a.ctypes.data)
 
 
+def spec_layout_shapes(spec_text: str):
+    """[(name, offset, count, (rows, cols))] of a spec's weight blob."""
+    return parse(spec_text).layout()
+
+
 def spec_layout(spec_text: str) -> List[Tuple[str, int, int]]:
     lay = lib().nsb_spec_layout(spec_text.encode())
     if not lay:

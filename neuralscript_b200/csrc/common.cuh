@@ -137,6 +137,16 @@ struct Epilogue {
     // at c32 + block * col_block_stride, column c % col_block (0 = off)
     int col_block = 0;
     long long col_block_stride = 0;
+    // Softmax cross-entropy statistics of the output rows (head GEMM + loss
+    // fusion, TMA-store path): for every row and every (n tile, epilogue warp
+    // of the row's lane quarter) slot, the maximum m of x * log2(e) over the
+    // slot's columns and the sum of 2^(x log2(e) - m) go to
+    // ce_part[row * ce_parts + slot]; the logit of column ce_tgt[row] goes to
+    // ce_tlogit[row].
+    float2* ce_part = nullptr;
+    int ce_parts = 0;
+    const int* ce_tgt = nullptr;
+    float* ce_tlogit = nullptr;
 };
 
 __device__ __forceinline__ float ld_any(const void* p, int dtype, size_t idx) {

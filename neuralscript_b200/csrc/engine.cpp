@@ -356,6 +356,19 @@ static int refresh_working(ns_model* m, const std::vector<char>* done) {
     return 0;
 }
 
+// The output layer can take the head GEMM + cross-entropy fusion: bf16
+// tensor cores, cross-entropy loss, output straight from a Dense layer
+// without activation or fused residual, at least 256 classes.
+static const Op* ce_fusable_producer(const ns_model* m) {
+    if (m->wdt != kBF16 || m->spec.loss == "mse" || m->out_val < 0) return nullptr;
+    const Val& o = m->vals[m->out_val];
+    if (o.producer < 0) return nullptr;
+    const Op* p = &m->ops[o.producer];
+    if (p->kind != OP_DENSE || p->act || p->fused_res >= 0 || p->skip || p->out != m->out_val) return nullptr;
+    if (o.cols < 256 || o.cols % 8) return nullptr;
+    return p;
+}
+
 // ---------------------------------------------------------------------------
 // planning
 // ---------------------------------------------------------------------------
@@ -381,6 +394,9 @@ static void free_plan(ns_model* m) {
     m->ws_floats = 0;
     m->d_scratch = nullptr;
     m->scratch_bytes = 0;
+    m->d_cepart = nullptr;
+    m->d_tlogit = nullptr;
+    m->ce_parts = 0;
     m->mmax = 0;
     m->train_planned = false;
 }
@@ -460,6 +476,11 @@ static int plan(ns_model* m, int M, bool train) {
                 if (b > m->scratch_bytes) m->scratch_bytes = b;
             }
         if (m->scratch_bytes) m->d_scratch = plan_alloc(m, m->scratch_bytes);
+        if (ce_fusable_producer(m)) {
+            m->ce_parts = gemm_ce_parts(m->vals[m->out_val].cols);
+            m->d_cepart = PA(float2, R * m->ce_parts);
+            m->d_tlogit = PA(float, R);
+        }
         m->train_planned = true;
     }
     for (void* p : m->plan_allocs)
@@ -603,6 +624,16 @@ static int forward(ns_model* m, int M, bool train) {
                 d.ep.ld_c32 = w.cols;
                 d.ep.c16 = out.h16;
                 d.ep.ld_c16 = w.cols;
+                if (train && m->ce_fused && op.out == m->out_val) {
+                    // bf16 logits into the layer's gradient buffer (the loss
+                    // pass turns them into the seed) plus softmax partials
+                    d.ep.c32 = nullptr;
+                    d.ep.c16 = reinterpret_cast<__nv_bfloat16*>(op.dz);
+                    d.ep.ce_part = m->d_cepart;
+                    d.ep.ce_parts = m->ce_parts;
+                    d.ep.ce_tgt = m->ce_targets;
+                    d.ep.ce_tlogit = m->d_tlogit;
+                }
                 rc = run_gemm(m, d);
                 break;
             }
@@ -1307,7 +1338,10 @@ static int loss_and_seed(ns_model* m, int M, const float* labels, const int* tar
     __nv_bfloat16* d16 = m->seed16 ? reinterpret_cast<__nv_bfloat16*>(prod->dz) : nullptr;
     launch_counter() += 1;
     int rc;
-    if (m->spec.loss == "mse") {
+    if (m->ce_fused) {
+        rc = cross_entropy_finish(d16, M, C, m->d_cepart, m->ce_parts, targets, m->d_tlogit, denom, m->d_rowloss,
+                                  m->stream);
+    } else if (m->spec.loss == "mse") {
         if (!labels) return fail("mse loss needs dense targets");
         rc = mse_fwd_bwd(o.f32, labels, M, C, want_grad ? (float)M * C * m->world : 1.f, m->d_rowloss, d32, d16,
                          m->stream);
@@ -2002,8 +2036,11 @@ static int eval_infer_one(ns_model* m, const float* input, float* output, size_t
 
 static int train_core(ns_model* m, int M, const float* d_labels, const int* d_targets, float* loss_out, float lr,
                       bool train) {
+    m->ce_fused = train && d_targets && !d_labels && m->d_cepart && ce_fusable_producer(m) &&
+                  getenv("NS_B200_CE_UNFUSED") == nullptr;
+    m->ce_targets = d_targets;
     if (forward(m, M, train)) return -1;
-    int rl = region_begin(m, "loss");
+    int rl = region_begin(m, m->ce_fused ? "loss.fused" : "loss");
     if (loss_and_seed(m, M, d_labels, d_targets, train)) return -1;
     region_end(m, rl);
     launch_counter() += 1;
@@ -2224,6 +2261,29 @@ size_t nsb_expert_kill(ns_model* m, int k) {
     return m->moe_active_count;
 }
 
+// Re-pack the working copies of the MoE layer's expert weights after the
+// master blob changed on the device (the host mirror is stale from then on).
+static int moe_weights_changed(ns_model* m) {
+    std::vector<char> done(m->spec.weights.size(), 1);
+    for (size_t w = 0; w < m->spec.weights.size(); w++)
+        if (m->spec.weights[w].layer == m->moe_layer) done[w] = 0;
+    m->host_dirty = true;
+    if (refresh_working(m, &done)) return -1;
+    return finish(m);
+}
+
+static nsb::ExpertGeom expert_geom(const MoeGeom& g) {
+    nsb::ExpertGeom e;
+    e.cap = g.cap;
+    e.dim = g.dim;
+    e.n1 = g.dim * g.ffn;
+    e.off_g = g.off_g;
+    e.off_e1 = g.off_e1;
+    e.off_e2 = g.off_e2;
+    e.linear = g.linear;
+    return e;
+}
+
 size_t nsb_expert_merge(ns_model* m, int a, int b) {
     MoeGeom g;
     if (!m || !moe_geom(m, g)) return m ? m->moe_active_count : 0;
@@ -2231,19 +2291,13 @@ size_t nsb_expert_merge(ns_model* m, int a, int b) {
     const int cap = (int)g.cap;
     if (a < 0 || b < 0 || a == b || a >= cap || b >= cap || !m->moe_active[a] || !m->moe_active[b])
         return m->moe_active_count;
-    sync_host(m);
-    float* w = m->h_w.data();
-    for (size_t k = 0; k < g.dim; k++)
-        w[g.off_g + k * g.cap + a] = 0.5f * (w[g.off_g + k * g.cap + a] + w[g.off_g + k * g.cap + b]);
-    const size_t n1 = g.dim * g.ffn;
-    for (size_t q = 0; q < n1; q++)
-        w[g.off_e1 + a * n1 + q] = 0.5f * (w[g.off_e1 + a * n1 + q] + w[g.off_e1 + b * n1 + q]);
-    if (!g.linear)
-        for (size_t q = 0; q < n1; q++)
-            w[g.off_e2 + a * n1 + q] = 0.5f * (w[g.off_e2 + a * n1 + q] + w[g.off_e2 + b * n1 + q]);
+    // on the device blob: expert a := (a + b) / 2, then b leaves the mask
+    launch_counter() += 1;
+    if (expert_merge_device(m->d_w, expert_geom(g), a, b, m->stream)) return m->moe_active_count;
     m->moe_active[b] = 0;
     m->moe_active_count--;
-    upload_weights(m);
+    cudaMemcpyAsync(m->d_active, m->moe_active.data(), m->moe_active.size(), cudaMemcpyHostToDevice, m->stream);
+    moe_weights_changed(m);
     return m->moe_active_count;
 }
 
@@ -2253,28 +2307,35 @@ size_t nsb_expert_birth(ns_model* m, int n) {
     // every replica draws the same sources and noise (same generator state)
     if (!m->reps.empty()) for_replicas(m, [n](ns_model* r) { nsb_expert_birth(r, n); return 0; });
     if (m->moe_active_count >= g.cap) return m->moe_active_count;
-    sync_host(m);
-    float* w = m->h_w.data();
+    // the source and the noise come from the model's generator in the CPU
+    // runtime's order (gate column, e1, e2 per new expert); only the noise
+    // travels to the device, where the new expert is written
     int src = (int)(m->rng() % g.cap);
     size_t tries = 0;
     while (tries++ < g.cap && !m->moe_active[src]) src = (int)(m->rng() % g.cap);
     const size_t n1 = g.dim * g.ffn;
+    const size_t per = g.dim + n1 * (g.linear ? 1 : 2);
+    std::vector<float> noise(per);
+    float* d_noise = nullptr;
+    if (cudaMalloc(&d_noise, per * sizeof(float)) != cudaSuccess) {
+        fail("device allocation failed");
+        return m->moe_active_count;
+    }
+    const nsb::ExpertGeom eg = expert_geom(g);
     for (int e = 0; e < (int)g.cap && n > 0; e++) {
         if (m->moe_active[e]) continue;
-        for (size_t k = 0; k < g.dim; k++)
-            w[g.off_g + k * g.cap + e] =
-                w[g.off_g + k * g.cap + src] + ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
-        for (size_t q = 0; q < n1; q++)
-            w[g.off_e1 + e * n1 + q] = w[g.off_e1 + src * n1 + q] + ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
-        if (!g.linear)
-            for (size_t q = 0; q < n1; q++)
-                w[g.off_e2 + e * n1 + q] =
-                    w[g.off_e2 + src * n1 + q] + ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
+        for (size_t i = 0; i < per; i++) noise[i] = ((float)(m->rng() % 1001) / 1000.f - 0.5f) * 1e-2f;
+        cudaMemcpyAsync(d_noise, noise.data(), per * sizeof(float), cudaMemcpyHostToDevice, m->stream);
+        launch_counter() += 1;
+        expert_birth_device(m->d_w, eg, src, e, d_noise, m->stream);
+        cudaStreamSynchronize(m->stream);  // the host noise buffer is reused by the next expert
         m->moe_active[e] = 1;
         m->moe_active_count++;
         n--;
     }
-    upload_weights(m);
+    cudaFree(d_noise);
+    cudaMemcpyAsync(m->d_active, m->moe_active.data(), m->moe_active.size(), cudaMemcpyHostToDevice, m->stream);
+    moe_weights_changed(m);
     return m->moe_active_count;
 }
 

@@ -43,6 +43,11 @@ int num_sms() {
 // ---------------------------------------------------------------------------
 // Epilogue helpers (shared by all paths)
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ void epi_apply(const Epilogue& ep, int row, int col, float v) {
     v *= ep.alpha;
     if (ep.add) v += ep.add_scale * ep.add[(size_t)row * ep.ld_add + col];
@@ -661,6 +666,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (unit < 0) break;
             tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end);
             const int c_begin = half * HALF_COLS, c_end = (half + 1) * HALF_COLS;
+            // cross-entropy statistics of this thread's row over its columns
+            float ce_m = -INFINITY, ce_s = 0.f;
+            const int ce_t = (p.ep.ce_part && w.m0 + r_in_tile < w.row_end) ? p.ep.ce_tgt[w.m0 + r_in_tile] : -1;
             // the first chunk's operands load while this tile's MMAs run
             bool have = load_ahead(w, w.n0 + c_begin);
             if (!ptx::mbar_wait(&acc_full[acc], acc_phase, p.err, kErrTimeoutEpilogue)) break;
@@ -684,6 +692,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (row < w.row_end)
                         epi_pre32<FAST>(p.ep, row, col0, v, nc, have && ahead_add ? addv : nullptr,
                                         have && ahead_dz ? dzv : nullptr);
+                    if (p.ep.ce_part && row < w.row_end) {
+                        // online max / sum of exponentials in the log2 domain
+                        constexpr float kL2e = 1.4426950408889634f;
+                        float cm = -INFINITY;
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < nc) cm = fmaxf(cm, v[j]);
+                        const float nm = fmaxf(ce_m, cm * kL2e);
+                        float sacc = ce_s * ex2_fast(ce_m - nm);
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (j < nc) sacc += ex2_fast(fmaf(v[j], kL2e, -nm));
+                        ce_m = nm;
+                        ce_s = sacc;
+                        if (ce_t >= col0 && ce_t < col0 + nc) {
+                            float tv = 0.f;
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                if (col0 + j == ce_t) tv = v[j];
+                            p.ep.ce_tlogit[row] = tv;
+                        }
+                    }
                     // the next chunk's operands load while this chunk is stored
                     have = c + 32 < c_end && load_ahead(w, col0 + 32);
                     store_tma(col0, y, v);
@@ -691,6 +721,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     finish(w, col0, v);
                 }
             }
+            if (p.ep.ce_part && w.m0 + r_in_tile < w.row_end)
+                p.ep.ce_part[(size_t)(w.m0 + r_in_tile) * p.ep.ce_parts + (w.n0 / BN) * 2 + half] =
+                    make_float2(ce_m, ce_s);
             ptx::tc_fence_before();
             ptx::mbar_arrive(&acc_empty[acc]);
             acc ^= 1;
@@ -1009,6 +1042,11 @@ static void pick_splits(const GemmDesc& d, int bn, int& splits, int& kb_per_spli
     splits = (k_blocks + kb_per_split - 1) / kb_per_split;
 }
 
+int gemm_ce_parts(int N) {
+    const int bn = N >= 256 ? 256 : 128;
+    return 2 * ((N + bn - 1) / bn);
+}
+
 size_t gemm_workspace_floats(const GemmDesc& d) {
     if (!gemm_uses_tensor_cores(d)) return 0;
     const int bn = pick_bn(d);
@@ -1132,6 +1170,10 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
         if (d.ep.c32) okm = okm && make_out_map(&om.c32, d.ep.c32, kF32, d.N, d.M, d.ep.ld_c32);
         if (d.ep.c16) okm = okm && make_out_map(&om.c16, d.ep.c16, kBF16, d.N, d.M, d.ep.ld_c16);
         p.tma_out = okm ? 1 : 0;
+    }
+    if (d.ep.ce_part) {
+        // the statistics are gathered on the TMA-store path, two slots per n tile
+        if (!p.tma_out || d.ep.ce_parts != 2 * p.n_tiles || !d.ep.ce_tgt || !d.ep.ce_tlogit) return -6;
     }
     cudaError_t e;
     if (bn == 256) {

@@ -747,6 +747,59 @@ __global__ void __launch_bounds__(256) ce_rows_vec_kernel(const float* __restric
     }
 }
 
+// Second half of the head GEMM + cross-entropy fusion: the GEMM epilogue
+// left bf16 logits in g16, per-row (max, sum of exponentials) partials in
+// log2 units and the target logit. One CTA per row: combine the partials
+// into the log-sum-exp, write the row loss lse - logit[target], and
+// overwrite the logits with the seed gradient (softmax - onehot) / denom.
+__global__ void __launch_bounds__(256) ce_finish_kernel(__nv_bfloat16* __restrict__ g16, int M, int C,
+                                                        const float2* __restrict__ part, int parts,
+                                                        const int* __restrict__ targets,
+                                                        const float* __restrict__ tlogit, float denom,
+                                                        float* __restrict__ row_loss) {
+    __shared__ float sh[33];
+    constexpr float kL2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+    for (int r = blockIdx.x; r < M; r += gridDim.x) {
+        float pm = -INFINITY;
+        for (int i = threadIdx.x; i < parts; i += blockDim.x) pm = fmaxf(pm, part[(size_t)r * parts + i].x);
+        const float m2 = block_max(pm, sh);
+        float ps = 0.f;
+        for (int i = threadIdx.x; i < parts; i += blockDim.x) {
+            const float2 q = part[(size_t)r * parts + i];
+            ps += q.y * exp2f(q.x - m2);
+        }
+        const float s = block_sum(ps, sh);
+        const float lse2 = m2 + log2f(s);  // log-sum-exp of the row, log2 units
+        const int t = targets[r];
+        if (threadIdx.x == 0) row_loss[r] = (t >= 0 && t < C) ? (lse2 - tlogit[r] * kL2e) * kLn2 : 0.f;
+        const float inv = 1.f / denom;
+        uint4* row = reinterpret_cast<uint4*>(g16 + (size_t)r * C);
+        for (int q = threadIdx.x; q < C / 8; q += blockDim.x) {
+            uint4 u = row[q];
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 x = __bfloat1622float2(h[e]);
+                const int j = 8 * q + 2 * e;
+                float a = exp2f(fmaf(x.x, kL2e, -lse2)), b = exp2f(fmaf(x.y, kL2e, -lse2));
+                a -= j == t ? 1.f : 0.f;
+                b -= j + 1 == t ? 1.f : 0.f;
+                h[e] = __floats2bfloat162_rn(a * inv, b * inv);
+            }
+            row[q] = u;
+        }
+    }
+}
+
+int cross_entropy_finish(__nv_bfloat16* g16, int M, int C, const float2* part, int parts, const int* targets,
+                         const float* tlogit, float denom, float* row_loss, cudaStream_t s) {
+    if (M <= 0) return 0;
+    if (C % 8 || (reinterpret_cast<uintptr_t>(g16) & 15)) return -1;
+    ce_finish_kernel<<<(unsigned)min(M, num_sms() * 8), 256, 0, s>>>(g16, M, C, part, parts, targets, tlogit, denom,
+                                                                     row_loss);
+    return launch_ok();
+}
+
 int cross_entropy_fwd_bwd(const float* logits, const float* labels, const int* targets, int M, int C, float denom,
                           float* row_loss, float* d32, __nv_bfloat16* d16, cudaStream_t s) {
     if (M <= 0) return 0;

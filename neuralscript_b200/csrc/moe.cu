@@ -880,4 +880,53 @@ int moe_backward(ns_model* m, Op& op, int M) {
     return 0;
 }
 
+// ---------------------------------------------------------------------------
+// Expert lifecycle on the device (merge / birth), grid-stride over the gate
+// column and the expert matrices; the arithmetic is the reference's, element
+// for element: 0.5f * (a + b) and src + noise in fp32.
+// ---------------------------------------------------------------------------
+__global__ void expert_merge_kernel(float* w, ExpertGeom g, int a, int b) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t t0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (size_t k = t0; k < g.dim; k += stride) {
+        float* pa = w + g.off_g + k * g.cap + a;
+        *pa = 0.5f * (*pa + w[g.off_g + k * g.cap + b]);
+    }
+    for (size_t q = t0; q < g.n1; q += stride) {
+        float* pa = w + g.off_e1 + (size_t)a * g.n1 + q;
+        *pa = 0.5f * (*pa + w[g.off_e1 + (size_t)b * g.n1 + q]);
+        if (!g.linear) {
+            float* p2 = w + g.off_e2 + (size_t)a * g.n1 + q;
+            *p2 = 0.5f * (*p2 + w[g.off_e2 + (size_t)b * g.n1 + q]);
+        }
+    }
+}
+
+__global__ void expert_birth_kernel(float* w, ExpertGeom g, int src, int e, const float* __restrict__ noise) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t t0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (size_t k = t0; k < g.dim; k += stride)
+        w[g.off_g + k * g.cap + e] = w[g.off_g + k * g.cap + src] + noise[k];
+    for (size_t q = t0; q < g.n1; q += stride) {
+        w[g.off_e1 + (size_t)e * g.n1 + q] = w[g.off_e1 + (size_t)src * g.n1 + q] + noise[g.dim + q];
+        if (!g.linear) w[g.off_e2 + (size_t)e * g.n1 + q] = w[g.off_e2 + (size_t)src * g.n1 + q] + noise[g.dim + g.n1 + q];
+    }
+}
+
+static unsigned lifecycle_blocks(const ExpertGeom& g) {
+    const size_t n = g.n1 > g.dim ? g.n1 : g.dim;
+    size_t b = (n + 255) / 256;
+    return (unsigned)(b > 148 * 8 ? 148 * 8 : (b ? b : 1));
+}
+
+int expert_merge_device(float* w, const ExpertGeom& g, int a, int b, cudaStream_t s) {
+    expert_merge_kernel<<<lifecycle_blocks(g), 256, 0, s>>>(w, g, a, b);
+    return launch_ok();
+}
+
+int expert_birth_device(float* w, const ExpertGeom& g, int src, int e, const float* noise, cudaStream_t s) {
+    expert_birth_kernel<<<lifecycle_blocks(g), 256, 0, s>>>(w, g, src, e, noise);
+    return launch_ok();
+}
+
 }  // namespace nsb

@@ -320,6 +320,16 @@ static void train_case(const char* tag, const std::vector<size_t>& counts, const
         auto b2 = file_bytes_as_u8(ck);
         remove(ck.c_str());
         savef(t + "_lifecycle_ckpt_bytes", b2, {b2.size()});
+        // birth into the two dead slots: a random live source plus noise,
+        // both from the runtime's generator
+        auto birth = L.sym<ebirth_t>("ns_expert_birth");
+        std::vector<float> bc{(float)birth(m, 2)};
+        std::vector<float> wb(w.size());
+        getw(m, wb.data(), wb.size());
+        infer(m, x.data(), out.data(), x.size());
+        savef(t + "_birth_count", bc, {1});
+        savef(t + "_birth_w", wb, {wb.size()});
+        savef(t + "_birth_out", out, {rows, (size_t)classes});
     }
 }
 

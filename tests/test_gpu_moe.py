@@ -88,6 +88,22 @@ def test_tmoe_training_and_lifecycle_match_reference_runtime(tmp_path):
     m2.load(p)
     assert m2.expert_count() == 1 and np.array_equal(m2.get_weights(), m.get_weights())
     assert np.array_equal(m2.infer(tok), m.infer(tok))
+    # birth on the device into the dead slots 1 and 2: the same source expert
+    # (0, the only live one) and the same noise as the reference runtime, so
+    # each new expert's offset from the source matches the reference's
+    assert m.expert_birth(2) == int(G["tmoe_birth_count"][0]) == 3
+    wb, ref_wb = m.get_weights(), G["tmoe_birth_w"]
+    lay = {n: (off, cnt, shp) for n, off, cnt, shp in nsb.spec_layout_shapes(TMOE)}
+    for name in ("moe_e1_w", "moe_e2_w"):
+        off, cnt, (E, n1) = lay[name]
+        ours, ref = wb[off:off + cnt].reshape(E, n1), ref_wb[off:off + cnt].reshape(E, n1)
+        for e in (1, 2):
+            np.testing.assert_allclose(ours[e] - ours[0], ref[e] - ref[0], rtol=0, atol=1e-6)
+    off, cnt, (D, E) = lay["moe_g_w"]
+    ours, ref = wb[off:off + cnt].reshape(D, E), ref_wb[off:off + cnt].reshape(D, E)
+    for e in (1, 2):
+        np.testing.assert_allclose(ours[:, e] - ours[:, 0], ref[:, e] - ref[:, 0], rtol=0, atol=1e-6)
+    np.testing.assert_allclose(m.infer(tok), G["tmoe_birth_out"], rtol=1e-3, atol=5e-4)
 
 
 def test_moe_forward_backward_matches_oracle_with_dead_expert():
