@@ -464,9 +464,8 @@ def region_work(spec, label, M, train, world=1):
             # fp32 logits read; training also writes the bf16 seed gradient
             return "bytes", M * 8192 * (4 + (2 if train else 0))
         if label == "loss.fused":
-            # head + loss fusion: bf16 logits read and overwritten by the bf16
-            # seed, plus the softmax partials (64 float2 per row)
-            return "bytes", M * 8192 * (2 + 2) + M * 64 * 8
+            # head + loss fusion: bf16 logits read and overwritten by the bf16 seed
+            return "bytes", M * 8192 * (2 + 2)
         if label == "optimizer" and s.optimizer == "muon":
             # Newton-Schulz-5 on every matrix: 5 iterations x 3 GEMMs x 2 n^3
             return "flops", sum(5 * 3 * 2.0 * r * c * min(r, c) for _, _, _, (r, c) in s.layout()

@@ -3,6 +3,7 @@
 // epilogue description shared by the tensor-core and SIMT GEMMs.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -22,7 +23,7 @@ enum DevErr : int {
 };
 
 // Operand element types.
-enum DType : int { kF32 = 0, kBF16 = 1 };
+enum DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };  // kF16: fp16 outputs only (head + loss fusion)
 
 // Activation codes (reference ns_act2, src/codegen/codegen.cpp:1244-1255).
 enum Act : int { kIdentity = 0, kRelu = 1, kLeaky = 2, kSigmoid = 3, kTanh = 4, kSilu = 5, kGelu = 6, kGeluMoe = 7 };
@@ -137,14 +138,11 @@ struct Epilogue {
     // at c32 + block * col_block_stride, column c % col_block (0 = off)
     int col_block = 0;
     long long col_block_stride = 0;
-    // Softmax cross-entropy statistics of the output rows (head GEMM + loss
-    // fusion, TMA-store path): for every row and every (n tile, epilogue warp
-    // of the row's lane quarter) slot, the maximum m of x * log2(e) over the
-    // slot's columns and the sum of 2^(x log2(e) - m) go to
-    // ce_part[row * ce_parts + slot]; the logit of column ce_tgt[row] goes to
-    // ce_tlogit[row].
-    float2* ce_part = nullptr;
-    int ce_parts = 0;
+    // c16 holds IEEE fp16 instead of bf16 (TMA-store path only)
+    bool c16_half = false;
+    // Head GEMM + loss fusion (TMA-store path): the fp32 logit of column
+    // ce_tgt[row] of every row goes to ce_tlogit[row] (the stored logits
+    // are bf16; the loss takes the target's logit at full precision).
     const int* ce_tgt = nullptr;
     float* ce_tlogit = nullptr;
 };

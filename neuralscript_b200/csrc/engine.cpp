@@ -394,9 +394,7 @@ static void free_plan(ns_model* m) {
     m->ws_floats = 0;
     m->d_scratch = nullptr;
     m->scratch_bytes = 0;
-    m->d_cepart = nullptr;
     m->d_tlogit = nullptr;
-    m->ce_parts = 0;
     m->mmax = 0;
     m->train_planned = false;
 }
@@ -476,11 +474,7 @@ static int plan(ns_model* m, int M, bool train) {
                 if (b > m->scratch_bytes) m->scratch_bytes = b;
             }
         if (m->scratch_bytes) m->d_scratch = plan_alloc(m, m->scratch_bytes);
-        if (ce_fusable_producer(m)) {
-            m->ce_parts = gemm_ce_parts(m->vals[m->out_val].cols);
-            m->d_cepart = PA(float2, R * m->ce_parts);
-            m->d_tlogit = PA(float, R);
-        }
+        if (ce_fusable_producer(m)) m->d_tlogit = PA(float, R);
         m->train_planned = true;
     }
     for (void* p : m->plan_allocs)
@@ -625,12 +619,11 @@ static int forward(ns_model* m, int M, bool train) {
                 d.ep.c16 = out.h16;
                 d.ep.ld_c16 = w.cols;
                 if (train && m->ce_fused && op.out == m->out_val) {
-                    // bf16 logits into the layer's gradient buffer (the loss
-                    // pass turns them into the seed) plus softmax partials
+                    // fp16 logits into the layer's gradient buffer (the loss
+                    // pass turns them into the bf16 seed) and the target logits
                     d.ep.c32 = nullptr;
                     d.ep.c16 = reinterpret_cast<__nv_bfloat16*>(op.dz);
-                    d.ep.ce_part = m->d_cepart;
-                    d.ep.ce_parts = m->ce_parts;
+                    d.ep.c16_half = true;  // fp16 logits, overwritten by the bf16 seed
                     d.ep.ce_tgt = m->ce_targets;
                     d.ep.ce_tlogit = m->d_tlogit;
                 }
@@ -1339,8 +1332,7 @@ static int loss_and_seed(ns_model* m, int M, const float* labels, const int* tar
     launch_counter() += 1;
     int rc;
     if (m->ce_fused) {
-        rc = cross_entropy_finish(d16, M, C, m->d_cepart, m->ce_parts, targets, m->d_tlogit, denom, m->d_rowloss,
-                                  m->stream);
+        rc = cross_entropy_finish(d16, M, C, targets, m->d_tlogit, denom, m->d_rowloss, m->stream);
     } else if (m->spec.loss == "mse") {
         if (!labels) return fail("mse loss needs dense targets");
         rc = mse_fwd_bwd(o.f32, labels, M, C, want_grad ? (float)M * C * m->world : 1.f, m->d_rowloss, d32, d16,
@@ -2036,8 +2028,7 @@ static int eval_infer_one(ns_model* m, const float* input, float* output, size_t
 
 static int train_core(ns_model* m, int M, const float* d_labels, const int* d_targets, float* loss_out, float lr,
                       bool train) {
-    m->ce_fused = train && d_targets && !d_labels && m->d_cepart && ce_fusable_producer(m) &&
-                  getenv("NS_B200_CE_UNFUSED") == nullptr;
+    m->ce_fused = train && d_targets && !d_labels && m->d_tlogit && ce_fusable_producer(m);
     m->ce_targets = d_targets;
     if (forward(m, M, train)) return -1;
     int rl = region_begin(m, m->ce_fused ? "loss.fused" : "loss");

@@ -123,13 +123,11 @@ struct ns_model {
     int last_rows = 0;       // rows of the last train step (input gradient export)
     bool seed16 = false;  // last loss seed went to the output Dense layer's bf16 dz
     // head GEMM + cross-entropy fusion (bf16 training with int32 targets):
-    // the output layer's GEMM leaves bf16 logits in its dz buffer and
-    // softmax partials here; the loss pass turns the logits into the seed
+    // the output layer's GEMM leaves bf16 logits in its dz buffer and the
+    // fp32 target logits here; the loss pass turns the logits into the seed
     bool ce_fused = false;
     const int* ce_targets = nullptr;
-    float2* d_cepart = nullptr;
     float* d_tlogit = nullptr;
-    int ce_parts = 0;
     // graph
     std::vector<nsb::Val> vals;
     std::vector<nsb::Op> ops;

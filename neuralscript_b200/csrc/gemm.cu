@@ -43,11 +43,7 @@ int num_sms() {
 // ---------------------------------------------------------------------------
 // Epilogue helpers (shared by all paths)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float ex2_fast(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
+
 __device__ __forceinline__ void epi_apply(const Epilogue& ep, int row, int col, float v) {
     v *= ep.alpha;
     if (ep.add) v += ep.add_scale * ep.add[(size_t)row * ep.ld_add + col];
@@ -571,6 +567,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             stage_store(map, g4, col0, y);
         };
+        auto out_f16 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
+            uint4 g4[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                __half2* h = reinterpret_cast<__half2*>(&g4[j]);
+#pragma unroll
+                for (int q = 0; q < 4; q++) h[q] = __floats2half2_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
+            }
+            stage_store(map, g4, col0, y);
+        };
         // TMA-store path, after epi_pre32: the pre-activation, the
         // activation and the outputs of 32 columns (col0 < N); rows >= M and
         // columns >= N of a box are clipped by the store
@@ -581,7 +587,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             epi_act32<FAST>(p.ep.act, v);
             if (p.ep.c32) out_f32(&tc32, v, col0, y);
-            if (p.ep.c16) out_bf16(&tc16, v, col0, y);
+            if (p.ep.c16) {
+                if (p.ep.c16_half) out_f16(&tc16, v, col0, y);
+                else out_bf16(&tc16, v, col0, y);
+            }
         };
         // Direct-store path: finish 32 accumulator columns (col0 < N) of
         // this thread's row.
@@ -666,9 +675,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (unit < 0) break;
             tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end);
             const int c_begin = half * HALF_COLS, c_end = (half + 1) * HALF_COLS;
-            // cross-entropy statistics of this thread's row over its columns
-            float ce_m = -INFINITY, ce_s = 0.f;
-            const int ce_t = (p.ep.ce_part && w.m0 + r_in_tile < w.row_end) ? p.ep.ce_tgt[w.m0 + r_in_tile] : -1;
+            // target column of this thread's row (head + loss fusion)
+            const int ce_t = (p.ep.ce_tgt && w.m0 + r_in_tile < w.row_end) ? p.ep.ce_tgt[w.m0 + r_in_tile] : -1;
             // the first chunk's operands load while this tile's MMAs run
             bool have = load_ahead(w, w.n0 + c_begin);
             if (!ptx::mbar_wait(&acc_full[acc], acc_phase, p.err, kErrTimeoutEpilogue)) break;
@@ -692,27 +700,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (row < w.row_end)
                         epi_pre32<FAST>(p.ep, row, col0, v, nc, have && ahead_add ? addv : nullptr,
                                         have && ahead_dz ? dzv : nullptr);
-                    if (p.ep.ce_part && row < w.row_end) {
-                        // online max / sum of exponentials in the log2 domain
-                        constexpr float kL2e = 1.4426950408889634f;
-                        float cm = -INFINITY;
+                    if (ce_t >= col0 && ce_t < col0 + nc) {  // this chunk holds the target logit
+                        float tv = 0.f;
 #pragma unroll
                         for (int j = 0; j < 32; j++)
-                            if (j < nc) cm = fmaxf(cm, v[j]);
-                        const float nm = fmaxf(ce_m, cm * kL2e);
-                        float sacc = ce_s * ex2_fast(ce_m - nm);
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (j < nc) sacc += ex2_fast(fmaf(v[j], kL2e, -nm));
-                        ce_m = nm;
-                        ce_s = sacc;
-                        if (ce_t >= col0 && ce_t < col0 + nc) {
-                            float tv = 0.f;
-#pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                if (col0 + j == ce_t) tv = v[j];
-                            p.ep.ce_tlogit[row] = tv;
-                        }
+                            if (col0 + j == ce_t) tv = v[j];
+                        p.ep.ce_tlogit[row] = tv;
                     }
                     // the next chunk's operands load while this chunk is stored
                     have = c + 32 < c_end && load_ahead(w, col0 + 32);
@@ -721,9 +714,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     finish(w, col0, v);
                 }
             }
-            if (p.ep.ce_part && w.m0 + r_in_tile < w.row_end)
-                p.ep.ce_part[(size_t)(w.m0 + r_in_tile) * p.ep.ce_parts + (w.n0 / BN) * 2 + half] =
-                    make_float2(ce_m, ce_s);
             ptx::tc_fence_before();
             ptx::mbar_arrive(&acc_empty[acc]);
             acc ^= 1;
@@ -977,12 +967,15 @@ static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner
 static bool make_out_map(CUtensorMap* m, const void* ptr, int dtype, long long cols, long long rows, long long ld) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
-    const int es = dtype == kBF16 ? 2 : 4;
+    const int es = dtype == kF32 ? 4 : 2;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
     cuuint32_t box[2] = {(cuuint32_t)(64 / es), 32};
     cuuint32_t estr[2] = {1, 1};
-    return enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+    return enc(m,
+               dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                              : (dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32),
+               2,
                const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_64B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -1040,11 +1033,6 @@ static void pick_splits(const GemmDesc& d, int bn, int& splits, int& kb_per_spli
     }
     kb_per_split = (k_blocks + splits - 1) / splits;
     splits = (k_blocks + kb_per_split - 1) / kb_per_split;
-}
-
-int gemm_ce_parts(int N) {
-    const int bn = N >= 256 ? 256 : 128;
-    return 2 * ((N + bn - 1) / bn);
 }
 
 size_t gemm_workspace_floats(const GemmDesc& d) {
@@ -1168,13 +1156,11 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
         bool okm = true;
         if (d.ep.z) okm = okm && make_out_map(&om.z, d.ep.z, d.ep.z_dtype, d.N, d.M, d.ep.ld_z);
         if (d.ep.c32) okm = okm && make_out_map(&om.c32, d.ep.c32, kF32, d.N, d.M, d.ep.ld_c32);
-        if (d.ep.c16) okm = okm && make_out_map(&om.c16, d.ep.c16, kBF16, d.N, d.M, d.ep.ld_c16);
+        if (d.ep.c16) okm = okm && make_out_map(&om.c16, d.ep.c16, d.ep.c16_half ? kF16 : kBF16, d.N, d.M, d.ep.ld_c16);
         p.tma_out = okm ? 1 : 0;
     }
-    if (d.ep.ce_part) {
-        // the statistics are gathered on the TMA-store path, two slots per n tile
-        if (!p.tma_out || d.ep.ce_parts != 2 * p.n_tiles || !d.ep.ce_tgt || !d.ep.ce_tlogit) return -6;
-    }
+    if (d.ep.ce_tgt && (!p.tma_out || !d.ep.ce_tlogit)) return -6;  // captured on the TMA-store path
+    if (d.ep.c16_half && !p.tma_out) return -6;
     cudaError_t e;
     if (bn == 256) {
         e = tf32 ? launch_tc_majors<256, true>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s)

@@ -57,10 +57,6 @@ struct GemmDesc {
 // dev_err: device int that kernels set on a bounded-wait timeout.
 int gemm(const GemmDesc& d, cudaStream_t stream, int* dev_err);
 
-// Cross-entropy statistic slots per output row (Epilogue::ce_parts) for a
-// GEMM with N output columns on the tensor-core path.
-int gemm_ce_parts(int N);
-
 // Workspace (floats) the split-K path wants for this problem (0 = none).
 size_t gemm_workspace_floats(const GemmDesc& d);
 

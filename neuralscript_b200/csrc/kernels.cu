@@ -747,56 +747,108 @@ __global__ void __launch_bounds__(256) ce_rows_vec_kernel(const float* __restric
     }
 }
 
-// Second half of the head GEMM + cross-entropy fusion: the GEMM epilogue
-// left bf16 logits in g16, per-row (max, sum of exponentials) partials in
-// log2 units and the target logit. One CTA per row: combine the partials
-// into the log-sum-exp, write the row loss lse - logit[target], and
-// overwrite the logits with the seed gradient (softmax - onehot) / denom.
-__global__ void __launch_bounds__(256) ce_finish_kernel(__nv_bfloat16* __restrict__ g16, int M, int C,
-                                                        const float2* __restrict__ part, int parts,
+// Second half of the head GEMM + cross-entropy fusion: the GEMM left the
+// logits in g16 as fp16 (a 2^-11 relative step: the softmax inputs need more
+// than bf16's 2^-8) and the fp32 target logit in tlogit. One warp per row:
+// pass 1 streams the row for its maximum and sum of exponentials (online,
+// log2 units), pass 2 re-reads it (now in L1/L2) and overwrites it with the
+// bf16 seed gradient (softmax - onehot) / denom; the row loss is
+// log-sum-exp - logit[target]. Exponentials on ex2.approx (a few ulp, far
+// inside the bf16 resolution of the seed).
+__device__ __forceinline__ float ex2_approx_f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(256) ce_finish_kernel(void* __restrict__ g16, int M, int C,
                                                         const int* __restrict__ targets,
                                                         const float* __restrict__ tlogit, float denom,
                                                         float* __restrict__ row_loss) {
-    __shared__ float sh[33];
     constexpr float kL2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
-    for (int r = blockIdx.x; r < M; r += gridDim.x) {
-        float pm = -INFINITY;
-        for (int i = threadIdx.x; i < parts; i += blockDim.x) pm = fmaxf(pm, part[(size_t)r * parts + i].x);
-        const float m2 = block_max(pm, sh);
-        float ps = 0.f;
-        for (int i = threadIdx.x; i < parts; i += blockDim.x) {
-            const float2 q = part[(size_t)r * parts + i];
-            ps += q.y * exp2f(q.x - m2);
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    const int n8 = C / 8;  // 8 bf16 per 16-byte load
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
+        uint4* row = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(g16) + (size_t)r * C);
+        float m = -INFINITY, s = 0.f;
+        int q = lane;
+        for (; q + 96 < n8; q += 128) {  // four loads in flight
+            uint4 u[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) u[k] = row[q + 32 * k];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const __half2* h = reinterpret_cast<const __half2*>(&u[k]);
+                float x[8];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float2 f = __half22float2(h[e]);
+                    x[2 * e] = f.x * kL2e;
+                    x[2 * e + 1] = f.y * kL2e;
+                }
+                float cm = fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
+                const float nm = fmaxf(m, cm);
+                s *= ex2_approx_f(m - nm);
+#pragma unroll
+                for (int e = 0; e < 8; e++) s += ex2_approx_f(x[e] - nm);
+                m = nm;
+            }
         }
-        const float s = block_sum(ps, sh);
-        const float lse2 = m2 + log2f(s);  // log-sum-exp of the row, log2 units
+        for (; q < n8; q += 32) {
+            const uint4 u = row[q];
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(h[e]);
+                x[2 * e] = f.x * kL2e;
+                x[2 * e + 1] = f.y * kL2e;
+            }
+            float cm = x[0];
+#pragma unroll
+            for (int e = 1; e < 8; e++) cm = fmaxf(cm, x[e]);
+            const float nm = fmaxf(m, cm);
+            s *= ex2_approx_f(m - nm);
+#pragma unroll
+            for (int e = 0; e < 8; e++) s += ex2_approx_f(x[e] - nm);
+            m = nm;
+        }
+        // combine the lanes' (max, sum)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+            const float nm = fmaxf(m, om);
+            s = s * ex2_approx_f(m - nm) + os * ex2_approx_f(om - nm);
+            m = nm;
+        }
+        const float lse2 = m + __log2f(s);
         const int t = targets[r];
-        if (threadIdx.x == 0) row_loss[r] = (t >= 0 && t < C) ? (lse2 - tlogit[r] * kL2e) * kLn2 : 0.f;
+        if (lane == 0) row_loss[r] = (t >= 0 && t < C) ? (lse2 - tlogit[r] * kL2e) * kLn2 : 0.f;
         const float inv = 1.f / denom;
-        uint4* row = reinterpret_cast<uint4*>(g16 + (size_t)r * C);
-        for (int q = threadIdx.x; q < C / 8; q += blockDim.x) {
-            uint4 u = row[q];
+        for (int q2 = lane; q2 < n8; q2 += 32) {
+            uint4 u = row[q2];
+            const __half2* hi = reinterpret_cast<const __half2*>(&u);
             __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const float2 x = __bfloat1622float2(h[e]);
-                const int j = 8 * q + 2 * e;
-                float a = exp2f(fmaf(x.x, kL2e, -lse2)), b = exp2f(fmaf(x.y, kL2e, -lse2));
+                const float2 x = __half22float2(hi[e]);
+                const int j = 8 * q2 + 2 * e;
+                float a = ex2_approx_f(fmaf(x.x, kL2e, -lse2)), b = ex2_approx_f(fmaf(x.y, kL2e, -lse2));
                 a -= j == t ? 1.f : 0.f;
                 b -= j + 1 == t ? 1.f : 0.f;
                 h[e] = __floats2bfloat162_rn(a * inv, b * inv);
             }
-            row[q] = u;
+            __stcs(row + q2, u);
         }
     }
 }
 
-int cross_entropy_finish(__nv_bfloat16* g16, int M, int C, const float2* part, int parts, const int* targets,
-                         const float* tlogit, float denom, float* row_loss, cudaStream_t s) {
+int cross_entropy_finish(void* g16, int M, int C, const int* targets, const float* tlogit, float denom,
+                         float* row_loss, cudaStream_t s) {
     if (M <= 0) return 0;
     if (C % 8 || (reinterpret_cast<uintptr_t>(g16) & 15)) return -1;
-    ce_finish_kernel<<<(unsigned)min(M, num_sms() * 8), 256, 0, s>>>(g16, M, C, part, parts, targets, tlogit, denom,
-                                                                     row_loss);
+    const unsigned blocks = (unsigned)min((M + 7) / 8, num_sms() * 8);
+    ce_finish_kernel<<<blocks, 256, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
     return launch_ok();
 }
 

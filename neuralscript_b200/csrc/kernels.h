@@ -34,13 +34,12 @@ int layernorm_bwd(const float* dy, const float* x, const float* add, int M, int 
 int cross_entropy_fwd_bwd(const float* logits, const float* labels, const int* targets, int M, int C, float denom,
                           float* row_loss, float* d32, __nv_bfloat16* d16, cudaStream_t s);
 
-// Completes the head GEMM + cross-entropy fusion: g16 holds the bf16
-// logits [M, C] and part the GEMM epilogue's per-row (max, sum exp) partials
-// (log2 units, `parts` per row), tlogit the target logits. Writes row_loss =
-// log-sum-exp - logit[target] and overwrites g16 with (softmax - onehot) /
-// denom in bf16. C a multiple of 8, g16 16-byte aligned.
-int cross_entropy_finish(__nv_bfloat16* g16, int M, int C, const float2* part, int parts, const int* targets,
-                         const float* tlogit, float denom, float* row_loss, cudaStream_t s);
+// Completes the head GEMM + cross-entropy fusion: g16 holds the fp16
+// logits [M, C] and tlogit the fp32 target logits. Writes row_loss =
+// log-sum-exp - logit[target] and overwrites g16 in place with the bf16
+// seed (softmax - onehot) / denom. C a multiple of 8, g16 16-byte aligned.
+int cross_entropy_finish(void* g16, int M, int C, const int* targets, const float* tlogit, float denom,
+                         float* row_loss, cudaStream_t s);
 
 // Mean squared error (sum of squares per row) and seed d = 2 (p - y) / denom.
 int mse_fwd_bwd(const float* p, const float* y, int M, int C, float denom, float* row_loss, float* d32,

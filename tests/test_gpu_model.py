@@ -414,5 +414,6 @@ def test_fused_head_cross_entropy_tracks_oracle_for_60_steps():
         exp.append(ref.train_step(tok, y, 3e-3))
     got, base, exp = (np.array(v, np.float64) for v in (got, base, exp))
     assert exp[-1] < 0.8 * exp[0]
-    assert np.max(np.abs(got - exp) / exp) < 1e-3, (got[-1], exp[-1])
-    assert np.max(np.abs(got - base) / base) < 1e-3
+    e_fused, e_plain = np.max(np.abs(got - exp) / exp), np.max(np.abs(base - exp) / exp)
+    print(f"max relative loss deviation from the oracle: fused {e_fused:.2e}, unfused {e_plain:.2e}")
+    assert e_fused < 1e-3 and e_plain < 1e-3, (e_fused, e_plain)
