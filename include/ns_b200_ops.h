@@ -127,6 +127,18 @@ int nsb_op_moe_route(const float* x, const float* Wg, const unsigned char* activ
 int nsb_op_act_fwd(const float* x, size_t n, int act, float* out32, void* out16, void* stream);
 int nsb_op_act_bwd(const float* dy, const float* z, int act, size_t n, float* out32, void* stream);
 
+/* Y[M,512] = LayerNorm(alpha * A[M,K] B[K,512] + add) row by row (no affine,
+ * eps 1e-5), the LayerNorm in the GEMM's epilogue: a 128 x 512 tile holds
+ * whole rows. A K-major (element (i,k) at A[i*lda + k]), B row-major
+ * [K, 512] (B[k*ldb + n]), both bf16 or both fp32 (TF32); add fp32 (may be
+ * NULL); c32 / c16 receive Y (either may be NULL), rstd[M] the rows'
+ * 1 / sqrt(var + eps). Replaces a Dense / attention output GEMM, the
+ * residual ns_binop and ns_layernorm_kernel in sequence
+ * (cuda_backend.cpp:58-79, 408-431). */
+int nsb_op_gemm_layernorm(int M, int K, const void* A, int dtype, long long lda, const void* B, long long ldb,
+                          float alpha, const float* add, long long ld_add, float* c32, long long ldc32, void* c16,
+                          long long ldc16, float* rstd, int* dev_err, void* stream);
+
 /* Row softmax (max-subtracted, exp, normalised). Replaces ns_softmax_kernel
  * (cuda_backend.cpp:432-441) / ns_softmax (codegen.cpp CPU helper). */
 int nsb_op_softmax(const float* x, int M, int C, float* out32, void* out16, void* stream);

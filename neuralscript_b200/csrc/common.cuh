@@ -140,6 +140,11 @@ struct Epilogue {
     long long col_block_stride = 0;
     // c16 holds IEEE fp16 instead of bf16 (TMA-store path only)
     bool c16_half = false;
+    // LayerNorm of every output row (no affine, eps 1e-5) after alpha and
+    // the residual add: c32 / c16 receive the normalised rows and
+    // ln_rstd[row] the row's 1 / sqrt(var + eps). Tensor-core path with
+    // N = 512 (one CTA owns whole rows).
+    float* ln_rstd = nullptr;
     // Head GEMM + loss fusion (TMA-store path): the fp32 logit of column
     // ce_tgt[row] of every row goes to ce_tlogit[row] (the stored logits
     // are bf16; the loss takes the target's logit at full precision).

@@ -217,12 +217,29 @@ static bool build_graph(ns_model* m, std::string& err) {
     // a copy in inference).
     for (auto& op : m->ops)
         if (op.kind == OP_DROPOUT && op.drop_rate == 0.f) m->vals[op.out].alias_of = op.in;
+    // LayerNorm over a residual sum that a Dense (no activation) or attention
+    // GEMM produces, 512 wide, the sum feeding nothing else: the GEMM can
+    // normalise whole rows in its epilogue (a 128 x 512 tile holds them)
+    for (size_t li = 0; li < m->ops.size(); li++) {
+        Op& l = m->ops[li];
+        if (l.kind != OP_LN) continue;
+        const Val& r = m->vals[l.in];
+        if (r.producer < 0 || r.cols != 512 || r.consumers.size() != 1 || l.in == m->out_val) continue;
+        Op& p = m->ops[r.producer];
+        if (p.skip || p.out != l.in || p.fused_res < 0 || p.ln_op >= 0) continue;
+        if (!((p.kind == OP_DENSE && p.act == 0) || p.kind == OP_ATTN)) continue;
+        p.ln_op = (int)li;
+        l.ln_from = r.producer;
+    }
     return true;
 }
 
 // Which forms each value must be stored in.
 static void decide_storage(ns_model* m) {
     const bool bf = m->precision == 2;
+    // LayerNorm fusion runs on the tensor-core path (TF32 / bf16 modes)
+    m->ln_fusion = m->precision != 0;
+    for (auto& v : m->vals) v.ln_hidden = false;
     for (size_t vi = 0; vi < m->vals.size(); vi++) {
         Val& v = m->vals[vi];
         v.need_f32 = (int)vi == m->out_val || vi == 0;
@@ -251,6 +268,14 @@ static void decide_storage(ns_model* m) {
             m->vals[op.in].need_f32 = true;
             if (bf) m->vals[op.in].need_h16 = true;
         }
+    if (m->ln_fusion)
+        for (auto& op : m->ops)
+            if (op.ln_from >= 0) {
+                // the sum is normalised in the producer's epilogue; the
+                // backward works from the LayerNorm output (kept in fp32)
+                m->vals[op.in].ln_hidden = true;
+                m->vals[op.out].need_f32 = true;
+            }
 }
 
 // ---------------------------------------------------------------------------
@@ -385,6 +410,7 @@ static void free_plan(ns_model* m) {
     for (auto& op : m->ops) {
         op.z = op.dz = op.qkv = op.ctx = op.dqkv = op.dctx = op.dout_w = nullptr;
         op.dz32 = op.lse = op.dvec = nullptr;
+        op.ln_rstd = nullptr;
         moe_release(op);
     }
     m->d_in = m->d_labels = m->d_rowloss = m->d_loss = nullptr;
@@ -416,10 +442,13 @@ static int plan(ns_model* m, int M, bool train) {
     if (!m->d_in) return fail("device allocation failed");
     for (size_t vi = 1; vi < m->vals.size(); vi++) {
         Val& v = m->vals[vi];
-        if (!v.materialized || v.alias_of >= 0) continue;
+        if (!v.materialized || v.alias_of >= 0 || v.ln_hidden) continue;
         if (v.need_f32) v.f32 = PA(float, R * v.cols);
         if (v.need_h16) v.h16 = PA(__nv_bfloat16, R * v.cols);
     }
+    if (m->ln_fusion)
+        for (auto& op : m->ops)
+            if (op.ln_op >= 0) op.ln_rstd = PA(float, R);
     m->vals[0].f32 = m->d_in;
     if (m->vals[0].need_h16) m->vals[0].h16 = PA(__nv_bfloat16, R * s.in_cols);
     for (size_t vi = 1; vi < m->vals.size(); vi++) {
@@ -590,6 +619,7 @@ static int forward(ns_model* m, int M, bool train) {
     for (size_t oi = 0; oi < m->ops.size(); oi++) {
         Op& op = m->ops[oi];
         if (op.skip) continue;
+        if (m->ln_fusion && op.ln_from >= 0) continue;  // normalised by its producer's GEMM
         Val& in = m->vals[op.in];
         Val& out = m->vals[op.out];
         int rc = 0;
@@ -618,6 +648,13 @@ static int forward(ns_model* m, int M, bool train) {
                 d.ep.ld_c32 = w.cols;
                 d.ep.c16 = out.h16;
                 d.ep.ld_c16 = w.cols;
+                if (m->ln_fusion && op.ln_op >= 0) {
+                    // the residual sum's LayerNorm in this GEMM's epilogue
+                    const Val& n = m->vals[m->ops[op.ln_op].out];
+                    d.ep.c32 = n.f32;
+                    d.ep.c16 = n.h16;
+                    d.ep.ln_rstd = op.ln_rstd;
+                }
                 if (train && m->ce_fused && op.out == m->out_val) {
                     // fp16 logits into the layer's gradient buffer (the loss
                     // pass turns them into the bf16 seed) and the target logits
@@ -697,6 +734,12 @@ static int forward(ns_model* m, int M, bool train) {
                 o.ep.ld_c32 = D;
                 o.ep.c16 = out.h16;
                 o.ep.ld_c16 = D;
+                if (m->ln_fusion && op.ln_op >= 0) {
+                    const Val& n = m->vals[m->ops[op.ln_op].out];
+                    o.ep.c32 = n.f32;
+                    o.ep.c16 = n.h16;
+                    o.ep.ln_rstd = op.ln_rstd;
+                }
                 int r3 = region_begin(m, "fwd:" + lname + ".out");
                 rc = run_gemm(m, o);
                 region_end(m, r3);
@@ -1180,7 +1223,11 @@ static int backward(ns_model* m, int M) {
                     else if (P->kind == OP_ATTN && P->dout_w) dx16 = reinterpret_cast<__nv_bfloat16*>(P->dout_w);
                 }
                 launch_counter() += 1;
-                rc = layernorm_bwd(dv, in.f32, in.gcur, M, in.cols, in.gbuf, dx16, m->stream);
+                if (m->ln_fusion && op.ln_from >= 0)  // from the output and the GEMM's rstd
+                    rc = layernorm_bwd_from_output(dv, out.f32, m->ops[op.ln_from].ln_rstd, in.gcur, M, in.cols,
+                                                   in.gbuf, dx16, m->stream);
+                else
+                    rc = layernorm_bwd(dv, in.f32, in.gcur, M, in.cols, in.gbuf, dx16, m->stream);
                 in.gcur = in.gbuf;
                 if (dx16) P->g16_ready = true;
                 break;

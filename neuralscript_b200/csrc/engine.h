@@ -31,6 +31,7 @@ struct Val {
     bool need_f32 = true, need_h16 = false;
     bool materialized = true;  // false: a dense output folded into a residual add
     int alias_of = -1;         // dropout: storage shared with its input
+    bool ln_hidden = false;    // a residual sum normalised inside its producer's GEMM: never stored
     float* f32 = nullptr;
     __nv_bfloat16* h16 = nullptr;
     // backward
@@ -75,6 +76,12 @@ struct Op {
     int64_t* d_idx = nullptr;
     float drop_rate = 0.f;  // dropout layers
     int drop_site = 0;      // dropout: index among the network's dropout ops
+    // LayerNorm fused into this op's GEMM (the op's output r = residual sum
+    // feeds only a LayerNorm, N = 512): ln_op is that LayerNorm's index, the
+    // GEMM writes its output and ln_rstd; on the LayerNorm, ln_from is the
+    // producer's index (forward skipped, backward from the output)
+    int ln_op = -1, ln_from = -1;
+    float* ln_rstd = nullptr;
     bool dz_ready = false;  // backward: dz already holds act'(z) * dout (written by the consumer's GEMM)
     bool g16_ready = false;  // backward: dz / dout_w already holds the bf16 output gradient
 };
@@ -122,6 +129,7 @@ struct ns_model {
     uint32_t drop_step = 0;  // advances every training step (fresh masks per step)
     int last_rows = 0;       // rows of the last train step (input gradient export)
     bool seed16 = false;  // last loss seed went to the output Dense layer's bf16 dz
+    bool ln_fusion = false;  // LayerNorms fused into their producers' GEMMs (tensor-core modes)
     // head GEMM + cross-entropy fusion (bf16 training with int32 targets):
     // the output layer's GEMM leaves bf16 logits in its dz buffer and the
     // fp32 target logits here; the loss pass turns the logits into the seed

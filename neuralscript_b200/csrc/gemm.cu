@@ -246,8 +246,12 @@ struct TcCfg {
     static constexpr int A_BYTES = BM * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (BN == 256) ? 4 : 6;
-    static constexpr int TMEM_COLS = 2 * BN;
+    // BN = 512 (whole-row LayerNorm mode): one accumulator spanning all of
+    // TMEM, filled by two N = 256 MMAs per k step
+    static constexpr int NACC = BN == 512 ? 1 : 2;
+    static constexpr int NMMA = BN == 512 ? 256 : BN;  // N of one MMA instruction
+    static constexpr int STAGES = BN == 512 ? 2 : (BN == 256 ? 4 : 6);
+    static constexpr int TMEM_COLS = NACC * BN;
     // MN-major operands: 128-byte chunks along M/N, BK k-rows each. bf16 uses
     // the 16-byte-granule 128B swizzle (8-row atoms, SBO 1024); tf32 needs the
     // 32-byte-granule variant (4-row atoms, SBO 512).
@@ -255,7 +259,8 @@ struct TcCfg {
     static constexpr uint32_t MN_SBO = TF32 ? 512 : 1024;
     // epilogue staging: per epilogue warp two 2 KB buffers (32 rows x 64 B)
     static constexpr int STAGING = 8 * 2 * 2048;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 512 /*barriers, queue*/;
+    static constexpr int SMEM =
+        STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 512 /*barriers, queue*/ + 2048 /*row statistics*/;
 };
 
 // Decode a work unit into (m0, n0, kb0, kb1, split, group); returns false
@@ -317,7 +322,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    const __grid_constant__ CUtensorMap tc16, const TcParams p) {
     using C = TcCfg<BN, TF32>;
     static_assert(kEpiWarps == 8, "staging is sized for 8 epilogue warps");
-    constexpr uint32_t IDESC = ptx::instr_desc(TF32 ? 2 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0, C::BM, BN);
+    constexpr uint32_t IDESC = ptx::instr_desc(TF32 ? 2 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0, C::BM, C::NMMA);
+    static_assert(BN != 512 || (!A_MN && B_MN), "the 512-wide mode takes a K-major A and an MN-major B");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;
@@ -329,8 +335,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* clc_bar = acc_empty + 2;
     uint64_t* q_full = clc_bar + 1;
     uint64_t* q_empty = q_full + kQueue;
-    int* unit_q = reinterpret_cast<int*>(q_empty + kQueue);
+    uint64_t* ln_bar = q_empty + kQueue;  // LayerNorm mode: epilogue row-statistics exchange
+    int* unit_q = reinterpret_cast<int*>(ln_bar + 1);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(unit_q + kQueue);
+    float* ln_xch = reinterpret_cast<float*>(staging + C::STAGING + 512);  // [2 passes][2 halves][128 rows]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -347,6 +355,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ptx::mbar_init(&q_full[q], 1);
             ptx::mbar_init(&q_empty[q], 1 + kEpiWarps);  // the MMA thread + one lane per epilogue warp
         }
+        ptx::mbar_init(ln_bar, 32 * kEpiWarps);
         ptx::fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -498,16 +507,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const uint32_t sa = ptx::smem_u32(smem + stage * C::STAGE_BYTES);
                     const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        uint64_t ad =
-                            A_MN ? ptx::smem_desc(sa + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
-                                 : ptx::smem_desc(sa + k * 32, 16, 1024, 2);
-                        uint64_t bd =
-                            B_MN ? ptx::smem_desc(sb + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
-                                 : ptx::smem_desc(sb + k * 32, 16, 1024, 2);
-                        uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
-                        if (TF32) ptx::mma_tf32(d, ad, bd, IDESC, accum);
-                        else ptx::mma_bf16(d, ad, bd, IDESC, accum);
+                    for (int h = 0; h < BN / C::NMMA; h++) {
+                        // N-slice h of the tile: MN-major B in 128-byte column chunks,
+                        // K-major B in 128-byte rows
+                        const uint32_t sbh =
+                            sb + h * (B_MN ? (C::NMMA / C::CHUNK) * C::BK * 128 : C::NMMA * 128);
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            uint64_t ad =
+                                A_MN ? ptx::smem_desc(sa + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
+                                     : ptx::smem_desc(sa + k * 32, 16, 1024, 2);
+                            uint64_t bd =
+                                B_MN ? ptx::smem_desc(sbh + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
+                                     : ptx::smem_desc(sbh + k * 32, 16, 1024, 2);
+                            uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+                            if (TF32) ptx::mma_tf32(d + h * C::NMMA, ad, bd, IDESC, accum);
+                            else ptx::mma_bf16(d + h * C::NMMA, ad, bd, IDESC, accum);
+                        }
                     }
                     ptx::mma_commit(&empty[stage]);
                     if (++stage == C::STAGES) {
@@ -516,7 +532,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
                 ptx::mma_commit(&acc_full[acc]);
-                acc ^= 1;
+                if (C::NACC == 2) acc ^= 1;
                 if (acc == 0) acc_phase ^= 1;
             }
         mma_done:;
@@ -658,6 +674,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t ln_phase = 0;
         int qslot = 0;
         uint32_t qphase = 0;
         Work w;
@@ -674,6 +691,90 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (unit < 0) break;
             tc_decode(p, unit, BN, w.m0, w.n0, w.kb0, w.kb1, w.split, w.g, w.row_end);
+            if constexpr (BN == 512) {
+                // ---- whole-row LayerNorm (N = 512) ----
+                // This warp owns 256 columns (half `half`) of its 32 rows; the
+                // two halves of a row meet through shared memory twice (the
+                // sum, then the centred sum of squares), each time on an
+                // mbarrier with a bounded wait. Three passes over TMEM; the
+                // residual is re-read from L2 in passes 2 and 3.
+                const int row = w.m0 + r_in_tile;
+                const bool rvalid = row < w.row_end;
+                const int cb = half * 256;
+                const bool okw = ptx::mbar_wait(&acc_full[0], acc_phase, p.err, kErrTimeoutEpilogue);
+                ptx::tc_fence_after();
+                auto ld_row = [&](int c, float* v) {  // alpha * acc + add_scale * residual, 32 columns
+                    if (!okw) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = 0.f;
+                        return;
+                    }
+                    uint32_t r[32];
+                    ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + cb + c, r);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * p.ep.alpha;
+                    if (p.ep.add && rvalid) {
+                        const float4* a = reinterpret_cast<const float4*>(p.ep.add + (size_t)row * p.ep.ld_add + cb + c);
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const float4 t = a[j];
+                            v[4 * j] += p.ep.add_scale * t.x;
+                            v[4 * j + 1] += p.ep.add_scale * t.y;
+                            v[4 * j + 2] += p.ep.add_scale * t.z;
+                            v[4 * j + 3] += p.ep.add_scale * t.w;
+                        }
+                    }
+                };
+                float s1 = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32) {
+                    float v[32];
+                    ld_row(c, v);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) s1 += v[j];
+                }
+                ln_xch[half * 128 + r_in_tile] = s1;
+                ptx::mbar_arrive(ln_bar);
+                const bool ok1 = ptx::mbar_wait(ln_bar, ln_phase, p.err, kErrTimeoutEpilogue);
+                ln_phase ^= 1;
+                const float mean = (ln_xch[r_in_tile] + ln_xch[128 + r_in_tile]) * (1.f / 512.f);
+                float s2 = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32) {
+                    float v[32];
+                    ld_row(c, v);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const float dv = v[j] - mean;
+                        s2 += dv * dv;
+                    }
+                }
+                ln_xch[256 + half * 128 + r_in_tile] = s2;
+                ptx::mbar_arrive(ln_bar);
+                const bool ok2 = ptx::mbar_wait(ln_bar, ln_phase, p.err, kErrTimeoutEpilogue);
+                ln_phase ^= 1;
+                const float var = (ln_xch[256 + r_in_tile] + ln_xch[384 + r_in_tile]) * (1.f / 512.f);
+                const float rstd = 1.f / sqrtf(var + 1e-5f);
+                const int y0 = w.m0 + lane_grp * 32;
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32) {
+                    float v[32];
+                    ld_row(c, v);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] = (v[j] - mean) * rstd;
+                    if (okw && y0 < p.M) {  // rows >= M of the box are clipped by the store
+                        if (p.ep.c32) out_f32(&tc32, v, cb + c, y0);
+                        if (p.ep.c16) out_bf16(&tc16, v, cb + c, y0);
+                    }
+                }
+                if (half == 0 && rvalid && okw) p.ep.ln_rstd[row] = rstd;
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&acc_empty[0]);
+                acc_phase ^= 1;
+                if (!okw || !ok1 || !ok2) break;
+                continue;
+            }
             const int c_begin = half * HALF_COLS, c_end = (half + 1) * HALF_COLS;
             // target column of this thread's row (head + loss fusion)
             const int ce_t = (p.ep.ce_tgt && w.m0 + r_in_tile < w.row_end) ? p.ep.ce_tgt[w.m0 + r_in_tile] : -1;
@@ -716,7 +817,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             ptx::tc_fence_before();
             ptx::mbar_arrive(&acc_empty[acc]);
-            acc ^= 1;
+            if (C::NACC == 2) acc ^= 1;
             if (acc == 0) acc_phase ^= 1;
         }
         if (p.tma_out && lane == 0) ptx::bulk_wait_all();
@@ -1016,11 +1117,14 @@ bool gemm_uses_tensor_cores(const GemmDesc& d) {
 // 256-wide tiles whenever N allows; grouped GEMMs only when N is a whole
 // number of tiles (a K-major B stacked along N must not straddle groups).
 // (128-wide tiles for the N = 512 layers measured slower: ff2 49 -> 62 us.)
-static int pick_bn(const GemmDesc& d) { return d.N >= 256 && (d.groups == 1 || d.N % 256 == 0) ? 256 : 128; }
+static int pick_bn(const GemmDesc& d) {
+    if (d.ep.ln_rstd) return 512;  // whole-row LayerNorm mode
+    return d.N >= 256 && (d.groups == 1 || d.N % 256 == 0) ? 256 : 128;
+}
 
 static void pick_splits(const GemmDesc& d, int bn, int& splits, int& kb_per_split, int k_blocks) {
     splits = 1;
-    if (d.groups == 1) {
+    if (d.groups == 1 && !d.ep.ln_rstd) {  // (a row's LayerNorm needs its whole K sum)
         const int tiles = ((d.M + 127) / 128) * ((d.N + bn - 1) / bn);
         const int sms = num_sms();
         if (d.splits > 0) splits = d.splits;
@@ -1161,8 +1265,16 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     }
     if (d.ep.ce_tgt && (!p.tma_out || !d.ep.ce_tlogit)) return -6;  // captured on the TMA-store path
     if (d.ep.c16_half && !p.tma_out) return -6;
+    if (d.ep.ln_rstd) {
+        // whole-row LayerNorm: N = 512, K-major A, MN-major B, no split, TMA stores
+        if (d.N != 512 || d.groups != 1 || d.a.mn_major || !d.b.mn_major || p.splits != 1 || !p.tma_out ||
+            d.ep.z || d.ep.act || d.ep.dz || d.ep.row_scale || d.ep.ce_tgt || d.ep.c16_half)
+            return -7;
+    }
     cudaError_t e;
-    if (bn == 256) {
+    if (bn == 512) {
+        e = tf32 ? launch_tc<512, true, false, true>(ta, tb, om, p, s) : launch_tc<512, false, false, true>(ta, tb, om, p, s);
+    } else if (bn == 256) {
         e = tf32 ? launch_tc_majors<256, true>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s)
                  : launch_tc_majors<256, false>(ta, tb, om, p, d.a.mn_major, d.b.mn_major, s);
     } else {

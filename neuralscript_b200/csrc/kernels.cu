@@ -563,10 +563,13 @@ __global__ void layernorm_bwd_kernel(const float* __restrict__ dy, const float* 
     }
 }
 
-template <int NV>
+// FROM_Y: x holds the LayerNorm OUTPUT y and rstd[r] the row's
+// 1 / sqrt(var + eps) (a LayerNorm fused into its producer's GEMM); the
+// centred input is then y / rstd, so the pre-LayerNorm sum is never needed.
+template <int NV, bool FROM_Y>
 __global__ void layernorm_bwd_vec_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                                         const float* __restrict__ add, int M, float* __restrict__ dx32,
-                                         __nv_bfloat16* __restrict__ dx16) {
+                                         const float* __restrict__ rstd, const float* __restrict__ add, int M,
+                                         float* __restrict__ dx32, __nv_bfloat16* __restrict__ dx16) {
     constexpr int D = NV * 128;
     const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
     for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < M; r += gridDim.x * warps) {
@@ -581,7 +584,21 @@ __global__ void layernorm_bwd_vec_kernel(const float* __restrict__ dy, const flo
             sx += (xv[i].x + xv[i].y) + (xv[i].z + xv[i].w);
             sd += (dv[i].x + dv[i].y) + (dv[i].z + dv[i].w);
         }
-        const float mean_x = warp_sum(sx) / (float)D;
+        float mean_x = 0.f, inv;
+        if (FROM_Y) {
+            // x - mean(x) = y * sigma
+            inv = rstd[r];
+            const float sig = 1.f / inv;
+#pragma unroll
+            for (int i = 0; i < NV; i++) {
+                xv[i].x *= sig;
+                xv[i].y *= sig;
+                xv[i].z *= sig;
+                xv[i].w *= sig;
+            }
+        } else {
+            mean_x = warp_sum(sx) / (float)D;
+        }
         const float mean_d = warp_sum(sd) / (float)D;
         float vq = 0.f, gq = 0.f;
 #pragma unroll
@@ -590,9 +607,11 @@ __global__ void layernorm_bwd_vec_kernel(const float* __restrict__ dy, const flo
             vq += (a * a + b * b) + (c * c + d * d);
             gq += (a * dv[i].x + b * dv[i].y) + (c * dv[i].z + d * dv[i].w);
         }
-        const float var = warp_sum(vq) / (float)D;
         const float gamma = warp_sum(gq) / (float)D;
-        const float inv = 1.f / sqrtf(var + 1e-5f);
+        if (!FROM_Y) {
+            const float var = warp_sum(vq) / (float)D;
+            inv = 1.f / sqrtf(var + 1e-5f);
+        }
 #pragma unroll
         for (int i = 0; i < NV; i++) {
             const int c = 4 * (lane + 32 * i);
@@ -625,14 +644,31 @@ int layernorm_bwd(const float* dy, const float* x, const float* add, int M, int 
     unsigned g = grid_for((size_t)M, 8);
     if (vec) {
         switch (D / 128) {
-            case 1: layernorm_bwd_vec_kernel<1><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
-            case 2: layernorm_bwd_vec_kernel<2><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
-            case 4: layernorm_bwd_vec_kernel<4><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
-            case 8: layernorm_bwd_vec_kernel<8><<<g, 256, 0, s>>>(dy, x, add, M, dx32, dx16); break;
+            case 1: layernorm_bwd_vec_kernel<1, false><<<g, 256, 0, s>>>(dy, x, nullptr, add, M, dx32, dx16); break;
+            case 2: layernorm_bwd_vec_kernel<2, false><<<g, 256, 0, s>>>(dy, x, nullptr, add, M, dx32, dx16); break;
+            case 4: layernorm_bwd_vec_kernel<4, false><<<g, 256, 0, s>>>(dy, x, nullptr, add, M, dx32, dx16); break;
+            case 8: layernorm_bwd_vec_kernel<8, false><<<g, 256, 0, s>>>(dy, x, nullptr, add, M, dx32, dx16); break;
             default: layernorm_bwd_kernel<<<g, 256, 0, s>>>(dy, x, add, M, D, dx32, dx16);
         }
     } else {
         layernorm_bwd_kernel<<<g, 256, 0, s>>>(dy, x, add, M, D, dx32, dx16);
+    }
+    return launch_ok();
+}
+
+int layernorm_bwd_from_output(const float* dy, const float* y, const float* rstd, const float* add, int M, int D,
+                              float* dx32, __nv_bfloat16* dx16, cudaStream_t s) {
+    if (M <= 0) return 0;
+    const bool vec = D % 128 == 0 && D <= 1024 && aligned16(y) && aligned16(dy) && (!add || aligned16(add)) &&
+                     (!dx32 || aligned16(dx32)) && (!dx16 || (reinterpret_cast<uintptr_t>(dx16) & 7) == 0);
+    if (!vec || !rstd) return -1;
+    unsigned g = grid_for((size_t)M, 8);
+    switch (D / 128) {
+        case 1: layernorm_bwd_vec_kernel<1, true><<<g, 256, 0, s>>>(dy, y, rstd, add, M, dx32, dx16); break;
+        case 2: layernorm_bwd_vec_kernel<2, true><<<g, 256, 0, s>>>(dy, y, rstd, add, M, dx32, dx16); break;
+        case 4: layernorm_bwd_vec_kernel<4, true><<<g, 256, 0, s>>>(dy, y, rstd, add, M, dx32, dx16); break;
+        case 8: layernorm_bwd_vec_kernel<8, true><<<g, 256, 0, s>>>(dy, y, rstd, add, M, dx32, dx16); break;
+        default: return -1;
     }
     return launch_ok();
 }

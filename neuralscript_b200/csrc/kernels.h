@@ -26,6 +26,11 @@ int layernorm_fwd(const float* x, int M, int D, float* out32, __nv_bfloat16* out
 // dx += add (if given). Writes fp32 and/or bf16.
 int layernorm_bwd(const float* dy, const float* x, const float* add, int M, int D, float* dx32, __nv_bfloat16* dx16,
                   cudaStream_t s);
+// The same gradient from the LayerNorm's output y and the row's rstd =
+// 1 / sqrt(var + eps) (a LayerNorm fused into its producer's GEMM): the
+// centred input x - mean(x) is y / rstd. D a multiple of 128, at most 1024.
+int layernorm_bwd_from_output(const float* dy, const float* y, const float* rstd, const float* add, int M, int D,
+                              float* dx32, __nv_bfloat16* dx16, cudaStream_t s);
 
 // Fused softmax cross-entropy forward + seed gradient, one row per CTA:
 //   loss_r = sum_{j: y_j > 0} -log softmax(x)_j      (one-hot labels [M,C])

@@ -253,4 +253,21 @@ int nsb_op_scatter(const float* in, int axis, int rows, int cols, const long lon
     return scatter_cols(in, rows, cols, ix, L, upd, out, nullptr, (cudaStream_t)stream);
 }
 
+int nsb_op_gemm_layernorm(int M, int K, const void* A, int dtype, long long lda, const void* B, long long ldb,
+                          float alpha, const float* add, long long ld_add, float* c32, long long ldc32, void* c16,
+                          long long ldc16, float* rstd, int* dev_err, void* stream) {
+    if (M < 0 || K <= 0 || !A || !B || !rstd || (!c32 && !c16)) return -1;
+    GemmDesc d = make_desc(M, 512, K, A, dtype, lda, 0, B, dtype, ldb, 1, kEngineTensor);
+    d.ep.alpha = alpha;
+    d.ep.add = add;
+    d.ep.ld_add = (int)ld_add;
+    d.ep.c32 = c32;
+    d.ep.ld_c32 = (int)ldc32;
+    d.ep.c16 = reinterpret_cast<__nv_bfloat16*>(c16);
+    d.ep.ld_c16 = (int)ldc16;
+    d.ep.ln_rstd = rstd;
+    launch_counter() += 1;
+    return gemm(d, (cudaStream_t)stream, dev_err);
+}
+
 }  // extern "C"

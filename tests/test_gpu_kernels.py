@@ -339,3 +339,45 @@ def test_activations():
         torch.cuda.synchronize()
         np.testing.assert_allclose(y.cpu().numpy(), R.act(x, code), rtol=2e-6, atol=1e-6)
         np.testing.assert_allclose(d.cpu().numpy(), R.act_grad(dy, x, code), rtol=2e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype,M,K", [("bf16", 16384, 512), ("bf16", 1000, 2048), ("tf32", 300, 512)])
+def test_gemm_layernorm_epilogue(dtype, M, K):
+    """LayerNorm in the GEMM epilogue (N = 512, whole rows per tile): the
+    normalised rows and 1/sigma against fp64 on the same rounded operands;
+    a partial last tile (M not a multiple of 128) included."""
+    import ctypes as C
+    L = O.L()
+    L.nsb_op_gemm_layernorm.restype = C.c_int
+    vp, ll = C.c_void_p, C.c_longlong
+    L.nsb_op_gemm_layernorm.argtypes = [C.c_int, C.c_int, vp, C.c_int, ll, vp, ll, C.c_float, vp, ll, vp, ll, vp,
+                                        ll, vp, vp, vp]
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    g = torch.Generator(device=DEV).manual_seed(7)
+    A = torch.randn(M, K, device=DEV, generator=g).to(tdt)
+    B = (torch.randn(K, 512, device=DEV, generator=g) * 0.05).to(tdt)
+    add = torch.randn(M, 512, device=DEV, generator=g)
+    c32 = torch.empty(M, 512, device=DEV)
+    c16 = torch.empty(M, 512, device=DEV, dtype=torch.bfloat16)
+    rstd = torch.empty(M, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    P = lambda t: C.c_void_p(t.data_ptr())
+    rc = L.nsb_op_gemm_layernorm(M, K, P(A), 1 if dtype == "bf16" else 0, K, P(B), 512, 0.5, P(add), 512, P(c32), 512,
+                                 P(c16), 512, P(rstd), P(err), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    if dtype == "tf32":  # TF32 rounds the fp32 operands to 10 mantissa bits
+        Ar = A.view(torch.int32).add(0x1000).bitwise_and(~0x1FFF).view(torch.float32)
+        Br = B.view(torch.int32).add(0x1000).bitwise_and(~0x1FFF).view(torch.float32)
+    else:
+        Ar, Br = A.float(), B.float()
+    x = 0.5 * (Ar.double() @ Br.double()) + add.double()
+    mu = x.mean(dim=1, keepdim=True)
+    var = ((x - mu) ** 2).mean(dim=1, keepdim=True)
+    y = (x - mu) / torch.sqrt(var + 1e-5)
+    tol = 1e-4 if dtype == "bf16" else 2e-3
+    e = float(torch.linalg.norm(c32.double() - y) / torch.linalg.norm(y))
+    assert e < tol, e
+    assert torch.allclose(rstd.double(), (1.0 / torch.sqrt(var + 1e-5)).squeeze(1), rtol=1e-4)
+    assert torch.equal(c16, c32.to(torch.bfloat16))
