@@ -259,8 +259,9 @@ struct TcCfg {
     static constexpr uint32_t MN_SBO = TF32 ? 512 : 1024;
     // epilogue staging: per epilogue warp two 2 KB buffers (32 rows x 64 B)
     static constexpr int STAGING = 8 * 2 * 2048;
-    static constexpr int SMEM =
-        STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 512 /*barriers, queue*/ + 2048 /*row statistics*/;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 512 /*barriers, queue*/ +
+                                (BN == 512 ? 2048 : 0) /*LayerNorm row statistics*/;
+    static_assert(SMEM <= 227 * 1024, "dynamic shared memory above the 227 KB per-block limit");
 };
 
 // Decode a work unit into (m0, n0, kb0, kb1, split, group); returns false
