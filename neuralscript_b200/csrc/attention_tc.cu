@@ -264,6 +264,255 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
 }
 
+__device__ __forceinline__ void store_row_bf16x64(__nv_bfloat16* dst, const uint32_t* v, float mul) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        uint4 pk;
+        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            h2[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * e]) * mul,
+                                          __uint_as_float(v[8 * g + 2 * e + 1]) * mul);
+        d[g] = pk;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Paired-tile forward for 128 < S <= 256 (the configuration's S = 256): one
+// persistent CTA walks (sequence b, head h) items and computes BOTH 128-query
+// tiles of an item, one per 4-warp group, so K and V are loaded once per item
+// and every thread owns a whole query row (no exchange between warps):
+//   warp 8 (one lane)  TMA loads (Q0 | Q1 | K | V, double-buffered by item)
+//                      and every MMA:
+//       S_g = Q_g K^T          (M=128, N=256, K=64) -> TMEM cols [256g, 256g+256)
+//       O_g = P_g V            (M=128, N=64, K=256) -> TMEM cols [256g+128, +64),
+//                              P_g read from TMEM (the .ts form: A in TMEM)
+//   warps 4g..4g+3     softmax of tile g: row max over the 256 scores, then
+//                      P = 2^(s*scale*log2e - max) rounded to bf16 and stored
+//                      back into TMEM over the scores already read (two keys
+//                      per 32-bit column, key 2j in the low half of column j),
+//                      row sums in fp32 from the unrounded values; epilogue
+//                      ctx = O / rowsum (bf16) and lse = max + log(rowsum).
+// The groups run staggered (S_1 is issued after S_0), so one group's softmax
+// overlaps the other's MMA waits and epilogue. All waits are bounded and
+// report through the error word; after a timeout every role stops waiting.
+namespace {
+constexpr int kPairThreads = 288;                    // 8 softmax warps + 1 load/MMA warp
+constexpr int kPairBuf = 2 * kQBytes + 2 * kKBytes;  // Q0 | Q1 | K | V = 96 KB
+constexpr int kPairSmem = 2 * kPairBuf + 1024 + 128;
+static_assert(kPairSmem <= 227 * 1024, "paired attention: shared memory above the per-block limit");
+}  // namespace
+
+__global__ void __launch_bounds__(kPairThreads, 1)
+    attn_tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tqkv, int B, int S, int H, int D, float scale,
+                            __nv_bfloat16* __restrict__ ctx, long long ld_ctx, float* __restrict__ lse, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* ld_bar = reinterpret_cast<uint64_t*>(smem + 2 * kPairBuf);  // [2] by buffer
+    uint64_t* s_bar = ld_bar + 2;     // [2] by group: S_g of the current item in TMEM
+    uint64_t* p_bar = s_bar + 2;      // [2] P_g stored (128 arrivals)
+    uint64_t* o_bar = p_bar + 2;      // [2] O_g of the current item in TMEM
+    uint64_t* free_bar = o_bar + 2;   // [2] O_g read, the group's columns are free (128 arrivals)
+    uint64_t* drain_bar = free_bar + 2;  // error path: all MMAs of this CTA complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+    const int t = threadIdx.x, warp = t >> 5;
+    const int items = B * H;
+
+    if (t == 0) {
+        for (int i = 0; i < 2; i++) {
+            ptx::mbar_init(&ld_bar[i], 1);
+            ptx::mbar_init(&s_bar[i], 1);
+            ptx::mbar_init(&p_bar[i], 128);
+            ptx::mbar_init(&o_bar[i], 1);
+            ptx::mbar_init(&free_bar[i], 128);
+        }
+        ptx::mbar_init(drain_bar, 1);
+        ptx::fence_mbar_init();
+    }
+    if (warp == 8) {
+        ptx::tmem_alloc(tmem_slot, 512);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 8) {
+        if ((t & 31) == 0) {
+            ptx::prefetch_tmap(&tqkv);
+            auto issue_load = [&](int it, int buf) {
+                const int h = it % H, b = it / H;
+                const int row0 = b * S;
+                uint8_t* sQ = smem + buf * kPairBuf;
+                uint8_t* sK = sQ + 2 * kQBytes;
+                uint8_t* sV = sK + kKBytes;
+                ptx::mbar_arrive_expect_tx(&ld_bar[buf], kPairBuf);
+                ptx::tma_load_2d(sQ, &tqkv, &ld_bar[buf], h * kDh, row0);
+                ptx::tma_load_2d(sQ + kQBytes, &tqkv, &ld_bar[buf], h * kDh, row0 + kQ);
+                ptx::tma_load_2d(sK, &tqkv, &ld_bar[buf], D + h * kDh, row0);
+                ptx::tma_load_2d(sK + kKBytes / 2, &tqkv, &ld_bar[buf], D + h * kDh, row0 + 128);
+                ptx::tma_load_2d(sV, &tqkv, &ld_bar[buf], 2 * D + h * kDh, row0);
+                ptx::tma_load_2d(sV + kKBytes / 2, &tqkv, &ld_bar[buf], 2 * D + h * kDh, row0 + 128);
+            };
+            // loads issued and not yet waited for, by buffer (drained on exit)
+            int pending[2] = {0, 0};
+            uint32_t ld_phase[2] = {0, 0};
+            if ((int)blockIdx.x < items) {
+                issue_load(blockIdx.x, 0);
+                pending[0] = 1;
+            }
+            if ((int)(blockIdx.x + gridDim.x) < items) {
+                issue_load(blockIdx.x + gridDim.x, 1);
+                pending[1] = 1;
+            }
+            int li = 0;
+#pragma unroll 1
+            for (int it = blockIdx.x; it < items && ok; it += gridDim.x, li++) {
+                const int buf = li & 1;
+                ok = ptx::mbar_wait(&ld_bar[buf], ld_phase[buf], err, kErrTimeoutAttn);
+                if (!ok) break;
+                ld_phase[buf] ^= 1;
+                pending[buf] = 0;
+                ptx::tc_fence_after();
+                const uint32_t aQ = ptx::smem_u32(smem + buf * kPairBuf);
+                const uint32_t aK = aQ + 2 * kQBytes, aV = aK + kKBytes;
+                for (int g = 0; g < 2 && ok; g++) {
+                    if (li > 0) {
+                        ok = ptx::mbar_wait(&free_bar[g], (li - 1) & 1, err, kErrTimeoutAttn);
+                        if (!ok) break;
+                        ptx::tc_fence_after();
+                    }
+#pragma unroll
+                    for (int st = 0; st < kDh / 16; st++)
+                        ptx::mma_bf16(tmem + 256 * g, ptx::smem_desc(aQ + g * kQBytes + st * 32, 16, 1024, 2),
+                                      ptx::smem_desc(aK + st * 32, 16, 1024, 2), kIdescS, st > 0);
+                    ptx::mma_commit(&s_bar[g]);
+                }
+                if (!ok) break;
+                // both groups have read O of the previous item, so every MMA of
+                // that item is complete and its buffer takes the item after this
+                if (li > 0 && it + (int)gridDim.x < items) {
+                    issue_load(it + gridDim.x, buf ^ 1);
+                    pending[buf ^ 1] = 1;
+                }
+                for (int g = 0; g < 2 && ok; g++) {
+                    ok = ptx::mbar_wait(&p_bar[g], li & 1, err, kErrTimeoutAttn);
+                    if (!ok) break;
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int s = 0; s < kKeys / 16; s++)
+                        ptx::mma_bf16_ts(tmem + 256 * g + 128, tmem + 256 * g + 8 * s,
+                                         ptx::smem_desc(aV + s * 16 * 128, kKBytes, 1024, 2), kIdescO, s > 0);
+                    ptx::mma_commit(&o_bar[g]);
+                }
+            }
+            // drain: no TMA write or MMA of this CTA may be in flight at exit
+            // (no error word here, so these waits do not return early once
+            // another role has recorded a timeout; each is still bounded)
+            for (int i = 0; i < 2; i++)
+                if (pending[i]) ptx::mbar_wait(&ld_bar[i], ld_phase[i], nullptr, 0);
+            if (!ok) {
+                ptx::mma_commit(drain_bar);
+                ptx::mbar_wait(drain_bar, 0, nullptr, 0);
+            }
+        }
+    } else {
+        const int g = warp >> 2, lg = warp & 3;
+        const int r = lg * 32 + (t & 31);  // query row within tile g = TMEM lane
+        const uint32_t base = tmem + ((uint32_t)(lg * 32) << 16) + 256 * g;
+        const float sl2 = scale * kLog2e;  // score -> log2 units
+        const bool full = S >= kKeys;      // every key valid: no masking
+        int li = 0;
+#pragma unroll 1
+        for (int it = blockIdx.x; it < items; it += gridDim.x, li++) {
+            const int h = it % H, b = it / H;
+            ok = ptx::mbar_wait(&s_bar[g], li & 1, err, kErrTimeoutAttn);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            // ---- row max, 64 columns per TMEM round trip ----
+            // (nine warps leave 168 registers a thread, so the row is read
+            // twice rather than held)
+            uint32_t c64[64];
+            float m8[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) m8[q] = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < kKeys; c += 64) {
+                ptx::tmem_ld32(base + c, c64);
+                ptx::tmem_ld32(base + c + 32, c64 + 32);
+                ptx::tmem_ld_wait();
+                if (full) {
+#pragma unroll
+                    for (int j = 0; j < 64; j++) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(c64[j]));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 64; j++)
+                        if (c + j < S) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(c64[j]));
+                }
+            }
+            float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            mx *= sl2;  // scale > 0: the max of the scaled scores (key 0 is always valid)
+            // ---- P = 2^(s*sl2 - mx), bf16 pairs into TMEM column key/2 ----
+            // P of keys [c, c+64) lands in columns [c/2, c/2+32), all of which
+            // this thread has already read (c/2 + 32 <= c + 64)
+            float s8[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) s8[q] = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < kKeys; c += 64) {
+                ptx::tmem_ld32(base + c, c64);
+                ptx::tmem_ld32(base + c + 32, c64 + 32);
+                ptx::tmem_ld_wait();
+                uint32_t pk[32];
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    const int j = 2 * e;
+                    const float p0 = (full || c + j < S) ? ex2_approx(fmaf(__uint_as_float(c64[j]), sl2, -mx)) : 0.f;
+                    const float p1 =
+                        (full || c + j + 1 < S) ? ex2_approx(fmaf(__uint_as_float(c64[j + 1]), sl2, -mx)) : 0.f;
+                    s8[j & 7] += p0;
+                    s8[(j + 1) & 7] += p1;
+                    __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+                    pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                ptx::tmem_st16(base + c / 2, pk);
+                ptx::tmem_st16(base + c / 2 + 16, pk + 16);
+            }
+            const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+            ptx::tmem_st_wait();
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&p_bar[g]);
+            // ---- epilogue: O_g row r ----
+            ok = ptx::mbar_wait(&o_bar[g], li & 1, err, kErrTimeoutAttn);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            uint32_t v[64];
+            ptx::tmem_ld32(base + 128, v);
+            ptx::tmem_ld32(base + 160, v + 32);
+            ptx::tmem_ld_wait();
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&free_bar[g]);
+            const int qi = g * kQ + r;
+            if (qi < S) {
+                const int row = b * S + qi;
+                const float inv = 1.f / sum;
+                store_row_bf16x64(ctx + (size_t)row * ld_ctx + h * kDh, v, inv);
+                if (lse) lse[((size_t)b * H + h) * S + qi] = mx * kLn2 + logf(sum);
+            }
+        }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, 512);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Tensor-core attention backward (bf16, head dim 64, S <= 256), the flash
 // recomputation form of the reference's ns_attention_grad_kernel
@@ -667,6 +916,18 @@ int attention_tc_fwd(const AttnArgs& a, cudaStream_t s, int* err) {
     if (!attr[dev]) {
         cudaFuncSetAttribute(attn_tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         attr[dev] = true;
+    }
+    if (a.S > kQ) {  // two query tiles per sequence: the paired kernel
+        static bool pattr[kMaxDevices] = {};
+        if (!pattr[dev]) {
+            cudaFuncSetAttribute(attn_tc_fwd_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+            pattr[dev] = true;
+        }
+        const int items = a.B * a.H;
+        const int grid = items < num_sms() ? items : num_sms();
+        attn_tc_fwd_pair_kernel<<<grid, kPairThreads, kPairSmem, s>>>(
+            m, a.B, a.S, a.H, a.D, a.scale, reinterpret_cast<__nv_bfloat16*>(a.ctx), a.ld_ctx, a.lse, err);
+        return cudaGetLastError() == cudaSuccess ? 0 : -5;
     }
     const int items = a.B * a.H * ((a.S + kQ - 1) / kQ);
     const int grid = items < num_sms() ? items : num_sms();

@@ -237,8 +237,10 @@ static bool build_graph(ns_model* m, std::string& err) {
 // Which forms each value must be stored in.
 static void decide_storage(ns_model* m) {
     const bool bf = m->precision == 2;
-    // LayerNorm fusion runs on the tensor-core path (TF32 / bf16 modes)
-    m->ln_fusion = m->precision != 0;
+    // LayerNorm fusion runs on the tensor-core path (TF32 / bf16 modes);
+    // NS_B200_LN_FUSION=0 keeps the separate LayerNorm kernels
+    const char* lf = getenv("NS_B200_LN_FUSION");
+    m->ln_fusion = m->precision != 0 && !(lf && lf[0] == '0');
     for (auto& v : m->vals) v.ln_hidden = false;
     for (size_t vi = 0; vi < m->vals.size(); vi++) {
         Val& v = m->vals[vi];
