@@ -139,6 +139,12 @@ int nsb_op_gemm_layernorm(int M, int K, const void* A, int dtype, long long lda,
                           float alpha, const float* add, long long ld_add, float* c32, long long ldc32, void* c16,
                           long long ldc16, float* rstd, int* dev_err, void* stream);
 
+/* y = 2^x for x <= 0 by the FMA-pipe exponential the attention softmax and
+ * the loss pass use for part of their exponentials (Cody-Waite reduction and
+ * a fitted cubic; relative error <= 7.5e-5; x below -125 gives 2^-125).
+ * No reference counterpart: exposed so its error bound can be tested. */
+int nsb_op_exp2_poly3(const float* x, float* y, size_t n, void* stream);
+
 /* Row softmax (max-subtracted, exp, normalised). Replaces ns_softmax_kernel
  * (cuda_backend.cpp:432-441) / ns_softmax (codegen.cpp CPU helper). */
 int nsb_op_softmax(const float* x, int M, int C, float* out32, void* out16, void* stream);

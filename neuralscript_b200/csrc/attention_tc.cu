@@ -433,54 +433,76 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             ok = ptx::mbar_wait(&s_bar[g], li & 1, err, kErrTimeoutAttn);
             if (!ok) break;
             ptx::tc_fence_after();
-            // ---- row max, 64 columns per TMEM round trip ----
-            // (nine warps leave 168 registers a thread, so the row is read
-            // twice rather than held)
-            uint32_t c64[64];
+            // ---- row max: two round trips of 128 columns ----
             float m8[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) m8[q] = -INFINITY;
 #pragma unroll 1
-            for (int c = 0; c < kKeys; c += 64) {
-                ptx::tmem_ld32(base + c, c64);
-                ptx::tmem_ld32(base + c + 32, c64 + 32);
-                ptx::tmem_ld_wait();
+            for (int c = 0; c < kKeys; c += 128) {
+                uint32_t a[128];
+#pragma unroll
+                for (int k = 0; k < 4; k++) ptx::tmem_ld32(base + c + 32 * k, a + 32 * k);
+#pragma unroll
+                for (int k = 0; k < 4; k++) ptx::tmem_ld_wait_regs32(a + 32 * k);
                 if (full) {
 #pragma unroll
-                    for (int j = 0; j < 64; j++) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(c64[j]));
+                    for (int j = 0; j < 128; j++) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(a[j]));
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 64; j++)
-                        if (c + j < S) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(c64[j]));
+                    for (int j = 0; j < 128; j++)
+                        if (c + j < S) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(a[j]));
                 }
             }
             float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             mx *= sl2;  // scale > 0: the max of the scaled scores (key 0 is always valid)
             // ---- P = 2^(s*sl2 - mx), bf16 pairs into TMEM column key/2 ----
-            // P of keys [c, c+64) lands in columns [c/2, c/2+32), all of which
-            // this thread has already read (c/2 + 32 <= c + 64)
+            // 32-column chunks, the next chunk's TMEM load in flight while
+            // this one is exponentiated. P of keys [c, c+32) lands in columns
+            // [c/2, c/2+16), all already read (c/2 + 16 <= c + 32). One pair
+            // in four takes the FMA-pipe exponential (exp2_poly3), the rest
+            // ex2.approx, so the two pipes share the work.
             float s8[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) s8[q] = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < kKeys; c += 64) {
-                ptx::tmem_ld32(base + c, c64);
-                ptx::tmem_ld32(base + c + 32, c64 + 32);
-                ptx::tmem_ld_wait();
-                uint32_t pk[32];
+            auto emit = [&](const uint32_t* sv, int c) {
+                uint32_t pk[16];
 #pragma unroll
-                for (int e = 0; e < 32; e++) {
+                for (int e = 0; e < 16; e++) {
                     const int j = 2 * e;
-                    const float p0 = (full || c + j < S) ? ex2_approx(fmaf(__uint_as_float(c64[j]), sl2, -mx)) : 0.f;
-                    const float p1 =
-                        (full || c + j + 1 < S) ? ex2_approx(fmaf(__uint_as_float(c64[j + 1]), sl2, -mx)) : 0.f;
+                    const float x0 = fmaf(__uint_as_float(sv[j]), sl2, -mx);
+                    const float x1 = fmaf(__uint_as_float(sv[j + 1]), sl2, -mx);
+                    float p0, p1;
+                    if ((e & 3) == 3) {
+                        p0 = exp2_poly3(x0);
+                        p1 = exp2_poly3(x1);
+                    } else {
+                        p0 = ex2_approx(x0);
+                        p1 = ex2_approx(x1);
+                    }
+                    if (!full) {
+                        p0 = c + j < S ? p0 : 0.f;
+                        p1 = c + j + 1 < S ? p1 : 0.f;
+                    }
                     s8[j & 7] += p0;
                     s8[(j + 1) & 7] += p1;
                     __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
                     pk[e] = *reinterpret_cast<uint32_t*>(&h2);
                 }
                 ptx::tmem_st16(base + c / 2, pk);
-                ptx::tmem_st16(base + c / 2 + 16, pk + 16);
+            };
+            {
+                uint32_t ca[32], cb[32];
+                ptx::tmem_ld32(base, ca);
+                ptx::tmem_ld_wait_regs32(ca);
+#pragma unroll 1
+                for (int c = 0; c < kKeys; c += 64) {
+                    ptx::tmem_ld32(base + c + 32, cb);
+                    emit(ca, c);
+                    ptx::tmem_ld_wait_regs32(cb);
+                    if (c + 64 < kKeys) ptx::tmem_ld32(base + c + 64, ca);
+                    emit(cb, c + 32);
+                    if (c + 64 < kKeys) ptx::tmem_ld_wait_regs32(ca);
+                }
             }
             const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
             ptx::tmem_st_wait();

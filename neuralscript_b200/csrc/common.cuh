@@ -80,6 +80,23 @@ __host__ __device__ __forceinline__ float act_deriv(float x, int code) {
 // path produces, at a third of the instructions; the fp32 and TF32 modes keep
 // the exact erff form of the reference. The derivative is that of the same
 // tanh form, so forward and backward agree.
+// 2^x for x <= 0 on the FMA/ALU pipes, without the special-function unit, so
+// kernels whose exponentials saturate that unit (attention softmax, the
+// cross-entropy pass) can move a share of them to the FP32 pipe.
+// Cody-Waite range reduction: x = n + f with n = round(x) (adding 1.5 * 2^23
+// leaves n in the low mantissa bits of t) and f in [-1/2, 1/2]; 2^f by a
+// cubic fitted for this code (Lawson-weighted least squares on [-1/2, 1/2],
+// maximum relative error 7.5e-5, below half a bf16 ulp); 2^n is added to the
+// exponent field. x is clamped at -125 so the result stays a normal number
+// (results there are about 2^-125, far under anything the callers keep).
+__device__ __forceinline__ float exp2_poly3(float x) {
+    x = fmaxf(x, -125.f);
+    const float t = x + 12582912.f;
+    const float f = x - (t - 12582912.f);
+    const float p = fmaf(fmaf(fmaf(0.0551716648f, f, 0.2426111251f), f, 0.6932609677f), f, 0.9999280572f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ float tanh_approx(float x) {
     float y;
     asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -697,58 +697,77 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // This warp owns 256 columns (half `half`) of its 32 rows; the
                 // two halves of a row meet through shared memory twice (the
                 // sum, then the centred sum of squares), each time on an
-                // mbarrier with a bounded wait. Three passes over TMEM; the
-                // residual is re-read from L2 in passes 2 and 3.
+                // mbarrier with a bounded wait. Pass 1 forms x = alpha*acc +
+                // add_scale*residual (the residual read once, the next 32
+                // columns' loads in flight while this chunk is summed) and
+                // writes x back over the accumulator in TMEM; passes 2 and 3
+                // read x from TMEM only.
                 const int row = w.m0 + r_in_tile;
                 const bool rvalid = row < w.row_end;
                 const int cb = half * 256;
+                const uint32_t tb = tmem_base + ((uint32_t)(lane_grp * 32) << 16) + cb;
                 const bool okw = ptx::mbar_wait(&acc_full[0], acc_phase, p.err, kErrTimeoutEpilogue);
                 ptx::tc_fence_after();
-                auto ld_row = [&](int c, float* v) {  // alpha * acc + add_scale * residual, 32 columns
-                    if (!okw) {
-#pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] = 0.f;
-                        return;
-                    }
-                    uint32_t r[32];
-                    ptx::tmem_ld32(tmem_base + ((uint32_t)(lane_grp * 32) << 16) + cb + c, r);
-                    ptx::tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]) * p.ep.alpha;
-                    if (p.ep.add && rvalid) {
-                        const float4* a = reinterpret_cast<const float4*>(p.ep.add + (size_t)row * p.ep.ld_add + cb + c);
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            const float4 t = a[j];
-                            v[4 * j] += p.ep.add_scale * t.x;
-                            v[4 * j + 1] += p.ep.add_scale * t.y;
-                            v[4 * j + 2] += p.ep.add_scale * t.z;
-                            v[4 * j + 3] += p.ep.add_scale * t.w;
-                        }
-                    }
-                };
+                const bool has_add = okw && p.ep.add != nullptr && rvalid;
+                const float4* addp =
+                    has_add ? reinterpret_cast<const float4*>(p.ep.add + (size_t)row * p.ep.ld_add + cb) : nullptr;
                 float s1 = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < 256; c += 32) {
-                    float v[32];
-                    ld_row(c, v);
+                if (okw) {
+                    float4 nxt[8];
+                    if (has_add) {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) s1 += v[j];
+                        for (int j = 0; j < 8; j++) nxt[j] = addp[j];
+                    }
+#pragma unroll 1
+                    for (int c = 0; c < 256; c += 32) {
+                        float4 cur[8];
+#pragma unroll
+                        for (int j = 0; j < 8; j++) cur[j] = nxt[j];
+                        if (has_add && c + 32 < 256) {
+#pragma unroll
+                            for (int j = 0; j < 8; j++) nxt[j] = addp[(c + 32) / 4 + j];
+                        }
+                        uint32_t r[32];
+                        ptx::tmem_ld32(tb + c, r);
+                        ptx::tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            float v = __uint_as_float(r[j]) * p.ep.alpha;
+                            if (has_add) {
+                                const float4 t = cur[j / 4];
+                                const float a = (j & 3) == 0 ? t.x : (j & 3) == 1 ? t.y : (j & 3) == 2 ? t.z : t.w;
+                                v = fmaf(p.ep.add_scale, a, v);
+                            }
+                            s1 += v;
+                            r[j] = __float_as_uint(v);
+                        }
+                        ptx::tmem_st16(tb + c, r);
+                        ptx::tmem_st16(tb + c + 16, r + 16);
+                    }
+                    ptx::tmem_st_wait();
                 }
+                // x of 64 columns from TMEM (passes 2 and 3)
+                auto ld_x64 = [&](int c, uint32_t* r) {
+                    ptx::tmem_ld32(tb + c, r);
+                    ptx::tmem_ld32(tb + c + 32, r + 32);
+                    ptx::tmem_ld_wait();
+                };
                 ln_xch[half * 128 + r_in_tile] = s1;
                 ptx::mbar_arrive(ln_bar);
                 const bool ok1 = ptx::mbar_wait(ln_bar, ln_phase, p.err, kErrTimeoutEpilogue);
                 ln_phase ^= 1;
                 const float mean = (ln_xch[r_in_tile] + ln_xch[128 + r_in_tile]) * (1.f / 512.f);
                 float s2 = 0.f;
+                if (okw) {
 #pragma unroll 1
-                for (int c = 0; c < 256; c += 32) {
-                    float v[32];
-                    ld_row(c, v);
+                    for (int c = 0; c < 256; c += 64) {
+                        uint32_t r[64];
+                        ld_x64(c, r);
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const float dv = v[j] - mean;
-                        s2 += dv * dv;
+                        for (int j = 0; j < 64; j++) {
+                            const float dv = __uint_as_float(r[j]) - mean;
+                            s2 = fmaf(dv, dv, s2);
+                        }
                     }
                 }
                 ln_xch[256 + half * 128 + r_in_tile] = s2;
@@ -758,13 +777,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const float var = (ln_xch[256 + r_in_tile] + ln_xch[384 + r_in_tile]) * (1.f / 512.f);
                 const float rstd = 1.f / sqrtf(var + 1e-5f);
                 const int y0 = w.m0 + lane_grp * 32;
+                if (okw && y0 < p.M) {  // rows >= M of the box are clipped by the store
 #pragma unroll 1
-                for (int c = 0; c < 256; c += 32) {
-                    float v[32];
-                    ld_row(c, v);
+                    for (int c = 0; c < 256; c += 32) {
+                        uint32_t r[32];
+                        ptx::tmem_ld32(tb + c, r);
+                        ptx::tmem_ld_wait();
+                        float v[32];
 #pragma unroll
-                    for (int j = 0; j < 32; j++) v[j] = (v[j] - mean) * rstd;
-                    if (okw && y0 < p.M) {  // rows >= M of the box are clipped by the store
+                        for (int j = 0; j < 32; j++) v[j] = (__uint_as_float(r[j]) - mean) * rstd;
                         if (p.ep.c32) out_f32(&tc32, v, cb + c, y0);
                         if (p.ep.c16) out_bf16(&tc16, v, cb + c, y0);
                     }

@@ -180,6 +180,80 @@ __global__ void emb_fill_kernel(const float* __restrict__ ids, int M, int V, con
     }
 }
 
+// Counting sort of the ids by vocabulary row in ONE CTA, for vocabularies
+// that fit shared memory: bucket counts by shared-memory atomics, exclusive
+// offsets by a block scan, then every row is appended to its bucket (order
+// inside a bucket arbitrary: the reduce orders by row). Writes count[],
+// offset[] and rows[] as the four-kernel path does, and any_big = 1 when a
+// bucket holds more than kEmbWarpRows rows (the bitmap kernel then has work).
+constexpr int kEmbSortThreads = 1024;
+constexpr int kEmbSortMaxVocab = 16384;  // 2 ints per vocabulary row: 128 KB of shared memory
+__global__ void __launch_bounds__(kEmbSortThreads) emb_sort_block_kernel(const float* __restrict__ ids, int M, int V,
+                                                                         int* __restrict__ count,
+                                                                         int* __restrict__ offset,
+                                                                         int* __restrict__ rows, int* any_big,
+                                                                         int big_rows) {
+    extern __shared__ int esm[];
+    int* s_cnt = esm;      // [V]
+    int* s_cur = esm + V;  // [V]: offsets, then the append cursors
+    __shared__ int warp_tot[32];
+    __shared__ int big;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    for (int i = tid; i < 2 * V; i += kEmbSortThreads) esm[i] = 0;
+    if (tid == 0) big = 0;
+    __syncthreads();
+    for (int r = tid; r < M; r += kEmbSortThreads) {
+        const long long v = (long long)ids[r];
+        if (v >= 0 && v < V) atomicAdd(&s_cnt[v], 1);
+    }
+    __syncthreads();
+    const int per = (V + kEmbSortThreads - 1) / kEmbSortThreads;
+    const int b0 = tid * per;
+    int local = 0, mx = 0;
+    for (int i = 0; i < per; i++)
+        if (b0 + i < V) {
+            const int c = s_cnt[b0 + i];
+            local += c;
+            mx = max(mx, c);
+        }
+    if (mx > big_rows) big = 1;  // benign race: every writer stores 1
+    int x = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int t = warp_tot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, t, o);
+            if (lane >= o) t += y;
+        }
+        warp_tot[lane] = t;
+    }
+    __syncthreads();
+    int excl = x - local + (w > 0 ? warp_tot[w - 1] : 0);
+    for (int i = 0; i < per; i++) {
+        const int k = b0 + i;
+        if (k < V) {
+            const int c = s_cnt[k];
+            s_cur[k] = excl;
+            offset[k] = excl;
+            count[k] = c;
+            excl += c;
+        }
+    }
+    __syncthreads();
+    for (int r = tid; r < M; r += kEmbSortThreads) {
+        const long long v = (long long)ids[r];
+        if (v >= 0 && v < V) rows[atomicAdd(&s_cur[v], 1)] = r;
+    }
+    if (tid == 0) *any_big = big;
+}
+
 // Sum of the listed dOut rows (ascending row order) into dst for D = 128*CH:
 // each lane owns CH float4 columns; four rows are loaded before any is
 // added, so a warp keeps 4*CH independent 16-byte loads in flight while the
@@ -298,8 +372,9 @@ __global__ void __launch_bounds__(kEmbBigThreads) emb_big_kernel(const float* __
                                                                const int* __restrict__ count,
                                                                const int* __restrict__ offset,
                                                                const int* __restrict__ rows, float* __restrict__ dW,
-                                                               int vec) {
+                                                               int vec, const int* any_big) {
     __shared__ unsigned bits[kEmbBitmapRows / 32];
+    if (any_big && *any_big == 0) return;  // no bucket above kEmbWarpRows rows (uniform)
     const int tid = threadIdx.x;
     const int slots = vec ? D / 4 : D;  // float4 or scalar columns
     for (int v = blockIdx.x; v < V; v += gridDim.x) {
@@ -374,17 +449,34 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     int* offset = count + V;
     int* cursor = offset + V;
     int* rows = cursor + V;
-    zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3);
-    if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count);
-    scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
-    if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
+    const int* any_big = nullptr;
+    if (V <= kEmbSortMaxVocab && M <= (1 << 20)) {
+        // one CTA sorts in shared memory; cursor[] is unused, its first word
+        // carries the large-bucket flag
+        const int smem = 2 * V * (int)sizeof(int);
+        static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to the current one
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+        if (!attr[dev]) {
+            cudaFuncSetAttribute(emb_sort_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 2 * kEmbSortMaxVocab * (int)sizeof(int));
+            attr[dev] = true;
+        }
+        emb_sort_block_kernel<<<1, kEmbSortThreads, smem, s>>>(ids, M, V, count, offset, rows, cursor, kEmbWarpRows);
+        any_big = cursor;
+    } else {
+        zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3);
+        if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count);
+        scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
+        if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
+    }
     int vec = (D % 4 == 0) && aligned16(dout) && aligned16(dW);
     emb_reduce_kernel<<<grid_for((size_t)V, 8), 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
     if (M > kEmbWarpRows) {
         // a few CTAs per SM walk the vocabulary; buckets of <= 32 rows are
         // skipped after one read of their count
         const unsigned big = (unsigned)(V < 148 * 4 ? V : 148 * 4);
-        emb_big_kernel<<<big, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec);
+        emb_big_kernel<<<big, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec, any_big);
     }
     return launch_ok();
 }

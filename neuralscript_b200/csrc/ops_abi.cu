@@ -31,6 +31,14 @@ static GemmDesc make_desc(int M, int N, int K, const void* A, int a_dtype, long 
     return d;
 }
 
+namespace {
+__global__ void exp2_poly3_kernel(const float* __restrict__ x, float* __restrict__ y, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = exp2_poly3(x[i]);
+}
+
+}  // namespace
+
 extern "C" {
 
 int nsb_op_gemm(int M, int N, int K, const void* A, int a_dtype, long long lda, int a_mn, const void* B, int b_dtype,
@@ -171,6 +179,15 @@ int nsb_op_act_bwd(const float* dy, const float* z, int act, size_t n, float* ou
     return act_bwd(dy, z, kF32, act, nullptr, n, out32, nullptr, (cudaStream_t)stream);
 }
 
+
+int nsb_op_exp2_poly3(const float* x, float* y, size_t n, void* stream) {
+    if (!x || !y) return -1;
+    if (n == 0) return 0;
+    launch_counter() += 1;
+    const unsigned blocks = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    exp2_poly3_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(x, y, n);
+    return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
 
 int nsb_op_softmax(const float* x, int M, int C, float* out32, void* out16, void* stream) {
     if (!x || M < 0 || C <= 0) return -1;

@@ -171,7 +171,9 @@ def test_layernorm_fwd_bwd():
         assert relerr(dx.cpu(), R.layernorm_grad(dy, x) + add) < 2e-6
 
 
-@pytest.mark.parametrize("V,D,M", [(1000, 512, 16384), (16, 8, 24), (50, 6, 300), (7, 132, 500)])
+# V <= 16384 sorts the ids in one CTA's shared memory; (20000, ...) takes the
+# four-kernel path (global counts, scan, fill)
+@pytest.mark.parametrize("V,D,M", [(1000, 512, 16384), (16, 8, 24), (50, 6, 300), (7, 132, 500), (20000, 64, 30000)])
 def test_embedding_fwd_bwd_deterministic_and_exact(V, D, M):
     rng = np.random.default_rng(1)
     W = rng.normal(0, 1, (V, D)).astype(np.float32)
@@ -191,6 +193,22 @@ def test_embedding_fwd_bwd_deterministic_and_exact(V, D, M):
     ref = R.embedding_grad_w(dout, ids, V)
     assert np.array_equal(dW1.cpu().numpy(), ref)  # same row order, same additions
     assert torch.equal(dW1, dW2)
+
+
+def test_embedding_grad_uniform_ids_exact():
+    """Uniform ids over 8192 rows (the c4 shape): no bucket above 32 rows, so
+    the bitmap kernel returns on the sort's flag; bit-exact against the
+    oracle."""
+    M, V, D = 16384, 8192, 512
+    rng = np.random.default_rng(12)
+    ids = rng.integers(0, V, M).astype(np.float32)
+    assert np.bincount(ids.astype(np.int64), minlength=V).max() <= 32
+    dout = rng.normal(0, 1, (M, D)).astype(np.float32)
+    idd, dd = torch.from_numpy(ids).to(DEV), torch.from_numpy(dout).to(DEV)
+    dW = torch.empty(V, D, device=DEV)
+    O.embedding_bwd(dd, idd, V, dW)
+    torch.cuda.synchronize()
+    assert np.array_equal(dW.cpu().numpy(), R.embedding_grad_w(dout, ids, V))
 
 
 @pytest.mark.parametrize("M,V,D,hot", [(16384, 8192, 512, 0.25), (131072, 8192, 512, 0.05), (5000, 300, 96, 0.6)])
@@ -384,3 +402,28 @@ def test_gemm_layernorm_epilogue(dtype, M, K):
     # 2e-3 as the rows
     assert torch.allclose(rstd.double(), (1.0 / torch.sqrt(var + 1e-5)).squeeze(1), rtol=tol)
     assert torch.equal(c16, c32.to(torch.bfloat16))
+
+
+def test_exp2_poly3_error_bound():
+    """The FMA-pipe exponential against fp64 2^x: relative error within the
+    fitted cubic's 7.5e-5 (plus fp32 rounding) on [-125, 0]; about 2^-125
+    below."""
+    import ctypes as C
+    L = O.L()
+    L.nsb_op_exp2_poly3.restype = C.c_int
+    L.nsb_op_exp2_poly3.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
+    x = torch.cat([torch.linspace(-125.0, 0.0, 1 << 20), torch.rand(1 << 20) * -8.0,
+                   torch.tensor([0.0, -0.5, -1.0, -124.5, -125.0])]).to(DEV)
+    y = torch.empty_like(x)
+    assert L.nsb_op_exp2_poly3(C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), x.numel(),
+                               C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    ref = torch.exp2(x.double())
+    rel = ((y.double() - ref).abs() / ref).max().item()
+    assert rel < 8e-5, rel
+    low = torch.tensor([-126.0, -200.0, -1e30], device=DEV)
+    yl = torch.empty_like(low)
+    assert L.nsb_op_exp2_poly3(C.c_void_p(low.data_ptr()), C.c_void_p(yl.data_ptr()), 3,
+                               C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    assert torch.all((yl > 0) & (yl <= 2.0 ** -124)), yl
