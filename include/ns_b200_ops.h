@@ -101,6 +101,14 @@ int nsb_op_attention_bwd(int B, int S, int H, int D, int dtype, const void* qkv,
  * (codegen.cpp:1582-1613). */
 int nsb_op_cross_entropy(const float* logits, const float* labels, const int* targets, int M, int C, float denom,
                          float* row_loss, float* d32, void* d16, void* stream);
+/* Second half of the fused head loss: logits16 holds fp16 logits [M,C]
+ * (16-byte aligned, C % 8 == 0) as the head GEMM writes them, tlogit the
+ * fp32 target logit of each row; writes row_loss[r] = lse - tlogit[r] (0 for
+ * a target outside [0,C)) and overwrites the row in place with the bf16 seed
+ * (softmax - onehot) / denom. Same arithmetic as nsb_op_cross_entropy with
+ * targets (ns_ce_row_kernel + ns_loss_grad_kernel, cuda_backend.cpp:690-719). */
+int nsb_op_cross_entropy_finish(void* logits16, int M, int C, const int* targets, const float* tlogit, float denom,
+                                float* row_loss, void* stream);
 /* out[0] = scale * sum(x[0..n)), fixed reduction order. */
 int nsb_op_reduce_sum(const float* x, int n, float scale, float* out, void* stream);
 

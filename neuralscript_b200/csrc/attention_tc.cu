@@ -264,20 +264,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
 }
 
-__device__ __forceinline__ void store_row_bf16x64(__nv_bfloat16* dst, const uint32_t* v, float mul) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int g = 0; g < 8; g++) {
-        uint4 pk;
-        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-        for (int e = 0; e < 4; e++)
-            h2[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * e]) * mul,
-                                          __uint_as_float(v[8 * g + 2 * e + 1]) * mul);
-        d[g] = pk;
-    }
-}
-
 // ---------------------------------------------------------------------------
 // Paired-tile forward for 128 < S <= 256 (the configuration's S = 256): one
 // persistent CTA walks (sequence b, head h) items and computes BOTH 128-query
@@ -294,15 +280,36 @@ __device__ __forceinline__ void store_row_bf16x64(__nv_bfloat16* dst, const uint
 //                      per 32-bit column, key 2j in the low half of column j),
 //                      row sums in fp32 from the unrounded values; epilogue
 //                      ctx = O / rowsum (bf16) and lse = max + log(rowsum).
-// The groups run staggered (S_1 is issued after S_0), so one group's softmax
-// overlaps the other's MMA waits and epilogue. All waits are bounded and
-// report through the error word; after a timeout every role stops waiting.
+// Ping-pong: a token passed between the groups lets only one group run its
+// softmax at a time (it then has the exponential unit and the issue slots of
+// the SM to itself) while the other waits for its PV product, writes its
+// epilogue and receives its next S. The MMA lane issues each group's next S
+// as soon as that group has read its O, ahead of the other group's PV.
+// The softmax does its arithmetic on packed fp32 pairs (fma/add .f32x2) and
+// takes the exponential of one pair in three on the FMA pipe (exp2_poly3),
+// the rest on ex2.approx. All waits are bounded and report through the error
+// word; after a timeout every role stops waiting.
 namespace {
 constexpr int kPairThreads = 288;                    // 8 softmax warps + 1 load/MMA warp
 constexpr int kPairBuf = 2 * kQBytes + 2 * kKBytes;  // Q0 | Q1 | K | V = 96 KB
 constexpr int kPairSmem = 2 * kPairBuf + 1024 + 128;
 static_assert(kPairSmem <= 227 * 1024, "paired attention: shared memory above the per-block limit");
+
 }  // namespace
+
+__device__ __forceinline__ void store_row_bf16x64(__nv_bfloat16* dst, const uint32_t* v, float mul) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        uint4 pk;
+        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            h2[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * g + 2 * e]) * mul,
+                                          __uint_as_float(v[8 * g + 2 * e + 1]) * mul);
+        d[g] = pk;
+    }
+}
 
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tqkv, int B, int S, int H, int D, float scale,
@@ -314,7 +321,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     uint64_t* p_bar = s_bar + 2;      // [2] P_g stored (128 arrivals)
     uint64_t* o_bar = p_bar + 2;      // [2] O_g of the current item in TMEM
     uint64_t* free_bar = o_bar + 2;   // [2] O_g read, the group's columns are free (128 arrivals)
-    uint64_t* drain_bar = free_bar + 2;  // error path: all MMAs of this CTA complete
+    uint64_t* tok_bar = free_bar + 2; // [2] softmax token handed to group g (128 arrivals)
+    uint64_t* drain_bar = tok_bar + 2;  // error path: all MMAs of this CTA complete
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
 
     const int t = threadIdx.x, warp = t >> 5;
@@ -327,6 +335,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             ptx::mbar_init(&p_bar[i], 128);
             ptx::mbar_init(&o_bar[i], 1);
             ptx::mbar_init(&free_bar[i], 128);
+            ptx::mbar_init(&tok_bar[i], 128);
         }
         ptx::mbar_init(drain_bar, 1);
         ptx::fence_mbar_init();
@@ -358,56 +367,77 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                 ptx::tma_load_2d(sV, &tqkv, &ld_bar[buf], 2 * D + h * kDh, row0);
                 ptx::tma_load_2d(sV + kKBytes / 2, &tqkv, &ld_bar[buf], 2 * D + h * kDh, row0 + 128);
             };
+            auto issue_s = [&](int g, int buf) {
+                const uint32_t aQ = ptx::smem_u32(smem + buf * kPairBuf) + g * kQBytes;
+                const uint32_t aK = ptx::smem_u32(smem + buf * kPairBuf) + 2 * kQBytes;
+#pragma unroll
+                for (int st = 0; st < kDh / 16; st++)
+                    ptx::mma_bf16(tmem + 256 * g, ptx::smem_desc(aQ + st * 32, 16, 1024, 2),
+                                  ptx::smem_desc(aK + st * 32, 16, 1024, 2), kIdescS, st > 0);
+                ptx::mma_commit(&s_bar[g]);
+            };
+            auto issue_o = [&](int g, int buf) {
+                const uint32_t aV = ptx::smem_u32(smem + buf * kPairBuf) + 2 * kQBytes + kKBytes;
+#pragma unroll
+                for (int s = 0; s < kKeys / 16; s++)
+                    ptx::mma_bf16_ts(tmem + 256 * g + 128, tmem + 256 * g + 8 * s,
+                                     ptx::smem_desc(aV + s * 16 * 128, kKBytes, 1024, 2), kIdescO, s > 0);
+                ptx::mma_commit(&o_bar[g]);
+            };
             // loads issued and not yet waited for, by buffer (drained on exit)
             int pending[2] = {0, 0};
             uint32_t ld_phase[2] = {0, 0};
-            if ((int)blockIdx.x < items) {
-                issue_load(blockIdx.x, 0);
-                pending[0] = 1;
-            }
-            if ((int)(blockIdx.x + gridDim.x) < items) {
-                issue_load(blockIdx.x + gridDim.x, 1);
-                pending[1] = 1;
-            }
-            int li = 0;
-#pragma unroll 1
-            for (int it = blockIdx.x; it < items && ok; it += gridDim.x, li++) {
-                const int buf = li & 1;
+            const int n = items > (int)blockIdx.x ? (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+            auto item = [&](int li) { return (int)blockIdx.x + li * (int)gridDim.x; };
+            auto wait_ld = [&](int buf) {
                 ok = ptx::mbar_wait(&ld_bar[buf], ld_phase[buf], err, kErrTimeoutAttn);
-                if (!ok) break;
                 ld_phase[buf] ^= 1;
                 pending[buf] = 0;
                 ptx::tc_fence_after();
-                const uint32_t aQ = ptx::smem_u32(smem + buf * kPairBuf);
-                const uint32_t aK = aQ + 2 * kQBytes, aV = aK + kKBytes;
-                for (int g = 0; g < 2 && ok; g++) {
-                    if (li > 0) {
-                        ok = ptx::mbar_wait(&free_bar[g], (li - 1) & 1, err, kErrTimeoutAttn);
-                        if (!ok) break;
-                        ptx::tc_fence_after();
-                    }
-#pragma unroll
-                    for (int st = 0; st < kDh / 16; st++)
-                        ptx::mma_bf16(tmem + 256 * g, ptx::smem_desc(aQ + g * kQBytes + st * 32, 16, 1024, 2),
-                                      ptx::smem_desc(aK + st * 32, 16, 1024, 2), kIdescS, st > 0);
-                    ptx::mma_commit(&s_bar[g]);
-                }
+                return ok;
+            };
+            if (n > 0) {
+                issue_load(item(0), 0);
+                pending[0] = 1;
+            }
+            if (n > 1) {
+                issue_load(item(1), 1);
+                pending[1] = 1;
+            }
+            if (n > 0 && wait_ld(0)) {
+                issue_s(0, 0);
+                issue_s(1, 0);
+            }
+#pragma unroll 1
+            for (int li = 0; li < n && ok; li++) {
+                const int buf = li & 1;
+                const bool more = li + 1 < n;
+                ok = ptx::mbar_wait(&p_bar[0], li & 1, err, kErrTimeoutAttn);
                 if (!ok) break;
-                // both groups have read O of the previous item, so every MMA of
-                // that item is complete and its buffer takes the item after this
-                if (li > 0 && it + (int)gridDim.x < items) {
-                    issue_load(it + gridDim.x, buf ^ 1);
-                    pending[buf ^ 1] = 1;
+                ptx::tc_fence_after();
+                issue_o(0, buf);
+                if (more) {
+                    // group 0's next scores as soon as it has read O_0
+                    ok = ptx::mbar_wait(&free_bar[0], li & 1, err, kErrTimeoutAttn);
+                    if (!ok || !wait_ld(buf ^ 1)) break;
+                    ptx::tc_fence_after();
+                    issue_s(0, buf ^ 1);
                 }
-                for (int g = 0; g < 2 && ok; g++) {
-                    ok = ptx::mbar_wait(&p_bar[g], li & 1, err, kErrTimeoutAttn);
+                ok = ptx::mbar_wait(&p_bar[1], li & 1, err, kErrTimeoutAttn);
+                if (!ok) break;
+                ptx::tc_fence_after();
+                issue_o(1, buf);
+                if (more) {
+                    ok = ptx::mbar_wait(&free_bar[1], li & 1, err, kErrTimeoutAttn);
                     if (!ok) break;
                     ptx::tc_fence_after();
-#pragma unroll
-                    for (int s = 0; s < kKeys / 16; s++)
-                        ptx::mma_bf16_ts(tmem + 256 * g + 128, tmem + 256 * g + 8 * s,
-                                         ptx::smem_desc(aV + s * 16 * 128, kKBytes, 1024, 2), kIdescO, s > 0);
-                    ptx::mma_commit(&o_bar[g]);
+                    // both groups have read O of item li: every MMA reading
+                    // its buffer is complete, so it takes item li + 2
+                    if (li + 2 < n) {
+                        issue_load(item(li + 2), buf);
+                        pending[buf] = 1;
+                    }
+                    issue_s(1, buf ^ 1);
                 }
             }
             // drain: no TMA write or MMA of this CTA may be in flight at exit
@@ -432,11 +462,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             const int h = it % H, b = it / H;
             ok = ptx::mbar_wait(&s_bar[g], li & 1, err, kErrTimeoutAttn);
             if (!ok) break;
+            // the token: group 0 takes it back from group 1's previous
+            // softmax, group 1 from group 0's softmax of this item
+            if (g == 1 || li > 0) {
+                ok = ptx::mbar_wait(&tok_bar[g], (g == 1 ? li : li - 1) & 1, err, kErrTimeoutAttn);
+                if (!ok) break;
+            }
             ptx::tc_fence_after();
             // ---- row max: two round trips of 128 columns ----
-            float m8[8];
+            float m4[4];
 #pragma unroll
-            for (int q = 0; q < 8; q++) m8[q] = -INFINITY;
+            for (int q = 0; q < 4; q++) m4[q] = -INFINITY;
 #pragma unroll 1
             for (int c = 0; c < kKeys; c += 128) {
                 uint32_t a[128];
@@ -446,35 +482,34 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                 for (int k = 0; k < 4; k++) ptx::tmem_ld_wait_regs32(a + 32 * k);
                 if (full) {
 #pragma unroll
-                    for (int j = 0; j < 128; j++) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(a[j]));
+                    for (int j = 0; j < 128; j += 2)
+                        m4[(j >> 1) & 3] = max3(m4[(j >> 1) & 3], __uint_as_float(a[j]), __uint_as_float(a[j + 1]));
                 } else {
 #pragma unroll
                     for (int j = 0; j < 128; j++)
-                        if (c + j < S) m8[j & 7] = fmaxf(m8[j & 7], __uint_as_float(a[j]));
+                        if (c + j < S) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(a[j]));
                 }
             }
-            float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            float mx = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
             mx *= sl2;  // scale > 0: the max of the scaled scores (key 0 is always valid)
             // ---- P = 2^(s*sl2 - mx), bf16 pairs into TMEM column key/2 ----
             // 32-column chunks, the next chunk's TMEM load in flight while
             // this one is exponentiated. P of keys [c, c+32) lands in columns
-            // [c/2, c/2+16), all already read (c/2 + 16 <= c + 32). One pair
-            // in four takes the FMA-pipe exponential (exp2_poly3), the rest
-            // ex2.approx, so the two pipes share the work.
-            float s8[8];
+            // [c/2, c/2+16), all already read (c/2 + 16 <= c + 32).
+            const uint64_t SL2 = f2_pack(sl2, sl2), NMX = f2_pack(-mx, -mx);
+            uint64_t s4[4];
 #pragma unroll
-            for (int q = 0; q < 8; q++) s8[q] = 0.f;
+            for (int q = 0; q < 4; q++) s4[q] = 0ull;
             auto emit = [&](const uint32_t* sv, int c) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
                     const int j = 2 * e;
-                    const float x0 = fmaf(__uint_as_float(sv[j]), sl2, -mx);
-                    const float x1 = fmaf(__uint_as_float(sv[j + 1]), sl2, -mx);
-                    float p0, p1;
-                    if ((e & 3) == 3) {
-                        p0 = exp2_poly3(x0);
-                        p1 = exp2_poly3(x1);
+                    const uint64_t X = f2_fma(f2_pack(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1])), SL2, NMX);
+                    float x0, x1, p0, p1;
+                    f2_unpack(X, x0, x1);
+                    if (e % 3 == 2) {
+                        exp2_poly3_pair(x0, x1, p0, p1);
                     } else {
                         p0 = ex2_approx(x0);
                         p1 = ex2_approx(x1);
@@ -483,8 +518,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                         p0 = c + j < S ? p0 : 0.f;
                         p1 = c + j + 1 < S ? p1 : 0.f;
                     }
-                    s8[j & 7] += p0;
-                    s8[(j + 1) & 7] += p1;
+                    s4[e & 3] = f2_add(s4[e & 3], f2_pack(p0, p1));
                     __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
                     pk[e] = *reinterpret_cast<uint32_t*>(&h2);
                 }
@@ -504,10 +538,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                     if (c + 64 < kKeys) ptx::tmem_ld_wait_regs32(ca);
                 }
             }
-            const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+            const uint64_t s2 = f2_add(f2_add(s4[0], s4[1]), f2_add(s4[2], s4[3]));
+            float sa, sb;
+            f2_unpack(s2, sa, sb);
+            const float sum = sa + sb;
             ptx::tmem_st_wait();
             ptx::tc_fence_before();
             ptx::mbar_arrive(&p_bar[g]);
+            ptx::mbar_arrive(&tok_bar[g ^ 1]);  // the other group's softmax may start
             // ---- epilogue: O_g row r ----
             ok = ptx::mbar_wait(&o_bar[g], li & 1, err, kErrTimeoutAttn);
             if (!ok) break;

@@ -97,6 +97,49 @@ __device__ __forceinline__ float exp2_poly3(float x) {
     return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// Packed fp32 pairs (sm_100 fma/add .f32x2: two lanes of arithmetic per
+// instruction), for the exponential-heavy loops of the softmax and the loss.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// exp2_poly3 of a pair (x <= 0), the polynomial on packed fp32 pairs
+__device__ __forceinline__ void exp2_poly3_pair(float x0, float x1, float& y0, float& y1) {
+    x0 = fmaxf(x0, -125.f);
+    x1 = fmaxf(x1, -125.f);
+    const uint64_t X = f2_pack(x0, x1);
+    const uint64_t T = f2_add(X, f2_pack(12582912.f, 12582912.f));
+    const uint64_t N = f2_add(T, f2_pack(-12582912.f, -12582912.f));
+    const uint64_t F = f2_fma(N, f2_pack(-1.f, -1.f), X);
+    uint64_t P = f2_fma(f2_pack(0.0551716648f, 0.0551716648f), F, f2_pack(0.2426111251f, 0.2426111251f));
+    P = f2_fma(P, F, f2_pack(0.6932609677f, 0.6932609677f));
+    P = f2_fma(P, F, f2_pack(0.9999280572f, 0.9999280572f));
+    float p0, p1, t0, t1;
+    f2_unpack(P, p0, p1);
+    f2_unpack(T, t0, t1);
+    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 __device__ __forceinline__ float tanh_approx(float x) {
     float y;
     asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));

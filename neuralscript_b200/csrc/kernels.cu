@@ -180,113 +180,35 @@ __global__ void emb_fill_kernel(const float* __restrict__ ids, int M, int V, con
     }
 }
 
-// Counting sort of the ids by vocabulary row in ONE CTA, for vocabularies
-// that fit shared memory: bucket counts by shared-memory atomics, exclusive
-// offsets by a block scan, then every row is appended to its bucket (order
-// inside a bucket arbitrary: the reduce orders by row). Writes count[],
-// offset[] and rows[] as the four-kernel path does, and any_big = 1 when a
-// bucket holds more than kEmbWarpRows rows (the bitmap kernel then has work).
-constexpr int kEmbSortThreads = 1024;
-constexpr int kEmbSortMaxVocab = 16384;  // 2 ints per vocabulary row: 128 KB of shared memory
-__global__ void __launch_bounds__(kEmbSortThreads) emb_sort_block_kernel(const float* __restrict__ ids, int M, int V,
-                                                                         int* __restrict__ count,
-                                                                         int* __restrict__ offset,
-                                                                         int* __restrict__ rows, int* any_big,
-                                                                         int big_rows) {
-    extern __shared__ int esm[];
-    int* s_cnt = esm;      // [V]
-    int* s_cur = esm + V;  // [V]: offsets, then the append cursors
-    __shared__ int warp_tot[32];
-    __shared__ int big;
-    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    for (int i = tid; i < 2 * V; i += kEmbSortThreads) esm[i] = 0;
-    if (tid == 0) big = 0;
-    __syncthreads();
-    for (int r = tid; r < M; r += kEmbSortThreads) {
-        const long long v = (long long)ids[r];
-        if (v >= 0 && v < V) atomicAdd(&s_cnt[v], 1);
-    }
-    __syncthreads();
-    const int per = (V + kEmbSortThreads - 1) / kEmbSortThreads;
-    const int b0 = tid * per;
-    int local = 0, mx = 0;
-    for (int i = 0; i < per; i++)
-        if (b0 + i < V) {
-            const int c = s_cnt[b0 + i];
-            local += c;
-            mx = max(mx, c);
-        }
-    if (mx > big_rows) big = 1;  // benign race: every writer stores 1
-    int x = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(kFull, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_tot[w] = x;
-    __syncthreads();
-    if (w == 0) {
-        int t = warp_tot[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(kFull, t, o);
-            if (lane >= o) t += y;
-        }
-        warp_tot[lane] = t;
-    }
-    __syncthreads();
-    int excl = x - local + (w > 0 ? warp_tot[w - 1] : 0);
-    for (int i = 0; i < per; i++) {
-        const int k = b0 + i;
-        if (k < V) {
-            const int c = s_cnt[k];
-            s_cur[k] = excl;
-            offset[k] = excl;
-            count[k] = c;
-            excl += c;
-        }
-    }
-    __syncthreads();
-    for (int r = tid; r < M; r += kEmbSortThreads) {
-        const long long v = (long long)ids[r];
-        if (v >= 0 && v < V) rows[atomicAdd(&s_cur[v], 1)] = r;
-    }
-    if (tid == 0) *any_big = big;
-}
-
 // Sum of the listed dOut rows (ascending row order) into dst for D = 128*CH:
-// each lane owns CH float4 columns; four rows are loaded before any is
-// added, so a warp keeps 4*CH independent 16-byte loads in flight while the
-// sums stay in row order (bit-identical to a one-row-at-a-time loop).
-template <int CH>
+// each lane owns CH float4 columns; rows are loaded G at a time (the loads of
+// a partial last group predicated off) before any is added, so a warp keeps
+// up to G*CH independent 16-byte loads in flight while the sums stay in row
+// order (bit-identical to a one-row-at-a-time loop).
+template <int CH, int G>
 __device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int D, const int* rows_sorted, int n,
                                              float* __restrict__ dst, int lane) {
     float4 acc[CH];
 #pragma unroll
     for (int c = 0; c < CH; c++) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-    int q = 0;
-    for (; q + 3 < n; q += 4) {
-        float4 t[4][CH];
+    for (int q = 0; q < n; q += G) {
+        float4 t[G][CH];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const float4* r = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q + u] * D) + lane;
+        for (int u = 0; u < G; u++) {
+            if (q + u < n) {
+                const float4* r = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q + u] * D) + lane;
 #pragma unroll
-            for (int c = 0; c < CH; c++) t[u][c] = __ldcs(r + 32 * c);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-#pragma unroll
-            for (int c = 0; c < CH; c++) {
-                acc[c].x += t[u][c].x; acc[c].y += t[u][c].y; acc[c].z += t[u][c].z; acc[c].w += t[u][c].w;
+                for (int c = 0; c < CH; c++) t[u][c] = __ldcs(r + 32 * c);
             }
-    }
-    for (; q < n; q++) {
-        const float4* r0 = reinterpret_cast<const float4*>(dout + (size_t)rows_sorted[q] * D) + lane;
-#pragma unroll
-        for (int c = 0; c < CH; c++) {
-            const float4 t = __ldcs(r0 + 32 * c);
-            acc[c].x += t.x; acc[c].y += t.y; acc[c].z += t.z; acc[c].w += t.w;
         }
+#pragma unroll
+        for (int u = 0; u < G; u++)
+            if (q + u < n) {
+#pragma unroll
+                for (int c = 0; c < CH; c++) {
+                    acc[c].x += t[u][c].x; acc[c].y += t[u][c].y; acc[c].z += t[u][c].z; acc[c].w += t[u][c].w;
+                }
+            }
     }
     float4* d4 = reinterpret_cast<float4*>(dst) + lane;
 #pragma unroll
@@ -300,9 +222,14 @@ __device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int
 // active for narrow rows) never shuffle across inactive lanes. Larger
 // buckets are left to emb_big_kernel.
 constexpr int kEmbWarpRows = 32;
-__global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, const int* __restrict__ count,
-                                  const int* __restrict__ offset, const int* __restrict__ rows,
-                                  float* __restrict__ dW, int vec) {
+// CH > 0: D = 128*CH with 16-byte aligned rows (one instantiation per width,
+// so each gets its own register budget); CH = 0: any D.
+template <int CH>
+__global__ void __launch_bounds__(256) emb_reduce_kernel(const float* __restrict__ dout, int D, int V,
+                                                         const int* __restrict__ count,
+                                                         const int* __restrict__ offset,
+                                                         const int* __restrict__ rows, float* __restrict__ dW,
+                                                         int vec) {
     __shared__ int sorted[8][32];  // blockDim.x == 256
     const int warps = blockDim.x >> 5;
     const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
@@ -330,14 +257,8 @@ __global__ void emb_reduce_kernel(const float* __restrict__ dout, int D, int V, 
         }
         sorted[wi][lane] = key;
         __syncwarp();
-        if (vec && D == 512) {
-            emb_sum_rows<4>(dout, D, sorted[wi], n, dst, lane);
-        } else if (vec && D == 256) {
-            emb_sum_rows<2>(dout, D, sorted[wi], n, dst, lane);
-        } else if (vec && D == 128) {
-            emb_sum_rows<1>(dout, D, sorted[wi], n, dst, lane);
-        } else if (vec && D == 1024) {
-            emb_sum_rows<8>(dout, D, sorted[wi], n, dst, lane);
+        if constexpr (CH > 0) {
+            emb_sum_rows<CH, (CH <= 2 ? 4 : (CH == 4 ? 2 : 1))>(dout, D, sorted[wi], n, dst, lane);
         } else if (vec) {
             for (int c = lane * 4; c < D; c += 128) {
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -372,9 +293,8 @@ __global__ void __launch_bounds__(kEmbBigThreads) emb_big_kernel(const float* __
                                                                const int* __restrict__ count,
                                                                const int* __restrict__ offset,
                                                                const int* __restrict__ rows, float* __restrict__ dW,
-                                                               int vec, const int* any_big) {
+                                                               int vec) {
     __shared__ unsigned bits[kEmbBitmapRows / 32];
-    if (any_big && *any_big == 0) return;  // no bucket above kEmbWarpRows rows (uniform)
     const int tid = threadIdx.x;
     const int slots = vec ? D / 4 : D;  // float4 or scalar columns
     for (int v = blockIdx.x; v < V; v += gridDim.x) {
@@ -449,34 +369,22 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     int* offset = count + V;
     int* cursor = offset + V;
     int* rows = cursor + V;
-    const int* any_big = nullptr;
-    if (V <= kEmbSortMaxVocab && M <= (1 << 20)) {
-        // one CTA sorts in shared memory; cursor[] is unused, its first word
-        // carries the large-bucket flag
-        const int smem = 2 * V * (int)sizeof(int);
-        static bool attr[kMaxDevices] = {};  // per device: the attribute belongs to the current one
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
-        if (!attr[dev]) {
-            cudaFuncSetAttribute(emb_sort_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 2 * kEmbSortMaxVocab * (int)sizeof(int));
-            attr[dev] = true;
-        }
-        emb_sort_block_kernel<<<1, kEmbSortThreads, smem, s>>>(ids, M, V, count, offset, rows, cursor, kEmbWarpRows);
-        any_big = cursor;
-    } else {
-        zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3);
-        if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count);
-        scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
-        if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
-    }
+    zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3);
+    if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count);
+    scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
+    if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
     int vec = (D % 4 == 0) && aligned16(dout) && aligned16(dW);
-    emb_reduce_kernel<<<grid_for((size_t)V, 8), 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    const unsigned rg = grid_for((size_t)V, 8);
+    if (vec && D == 512) emb_reduce_kernel<4><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    else if (vec && D == 256) emb_reduce_kernel<2><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    else if (vec && D == 128) emb_reduce_kernel<1><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    else if (vec && D == 1024) emb_reduce_kernel<8><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
+    else emb_reduce_kernel<0><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
     if (M > kEmbWarpRows) {
         // a few CTAs per SM walk the vocabulary; buckets of <= 32 rows are
         // skipped after one read of their count
         const unsigned big = (unsigned)(V < 148 * 4 ? V : 148 * 4);
-        emb_big_kernel<<<big, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec, any_big);
+        emb_big_kernel<<<big, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec);
     }
     return launch_ok();
 }

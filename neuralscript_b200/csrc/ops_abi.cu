@@ -144,6 +144,13 @@ int nsb_op_cross_entropy(const float* logits, const float* labels, const int* ta
                                  reinterpret_cast<__nv_bfloat16*>(d16), (cudaStream_t)stream);
 }
 
+int nsb_op_cross_entropy_finish(void* logits16, int M, int C, const int* targets, const float* tlogit, float denom,
+                                float* row_loss, void* stream) {
+    if (!logits16 || !targets || !tlogit || !row_loss || M < 0 || C <= 0) return -1;
+    launch_counter() += 1;
+    return cross_entropy_finish(logits16, M, C, targets, tlogit, denom, row_loss, (cudaStream_t)stream);
+}
+
 int nsb_op_reduce_sum(const float* x, int n, float scale, float* out, void* stream) {
     return reduce_sum(x, n, scale, out, (cudaStream_t)stream);
 }

@@ -171,8 +171,6 @@ def test_layernorm_fwd_bwd():
         assert relerr(dx.cpu(), R.layernorm_grad(dy, x) + add) < 2e-6
 
 
-# V <= 16384 sorts the ids in one CTA's shared memory; (20000, ...) takes the
-# four-kernel path (global counts, scan, fill)
 @pytest.mark.parametrize("V,D,M", [(1000, 512, 16384), (16, 8, 24), (50, 6, 300), (7, 132, 500), (20000, 64, 30000)])
 def test_embedding_fwd_bwd_deterministic_and_exact(V, D, M):
     rng = np.random.default_rng(1)
@@ -196,9 +194,8 @@ def test_embedding_fwd_bwd_deterministic_and_exact(V, D, M):
 
 
 def test_embedding_grad_uniform_ids_exact():
-    """Uniform ids over 8192 rows (the c4 shape): no bucket above 32 rows, so
-    the bitmap kernel returns on the sort's flag; bit-exact against the
-    oracle."""
+    """Uniform ids over 8192 rows (the c4 shape, no bucket above 32 rows: the
+    warp-per-row reduce alone); bit-exact against the oracle."""
     M, V, D = 16384, 8192, 512
     rng = np.random.default_rng(12)
     ids = rng.integers(0, V, M).astype(np.float32)
@@ -427,3 +424,43 @@ def test_exp2_poly3_error_bound():
                                C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
     torch.cuda.synchronize()
     assert torch.all((yl > 0) & (yl <= 2.0 ** -124)), yl
+
+
+@pytest.mark.parametrize("M,C", [(300, 8192), (257, 4096), (130, 1000)])
+def test_cross_entropy_finish_from_fp16_logits(M, C):
+    """The loss pass of the fused head (fp16 logits in, bf16 seed written in
+    place) against fp64 on the same fp16 values: row losses within 2e-5, the
+    seed within bf16 rounding; an out-of-range target gives
+    loss 0 and no -1 term."""
+    import ctypes as C_
+    L = O.L()
+    L.nsb_op_cross_entropy_finish.restype = C_.c_int
+    L.nsb_op_cross_entropy_finish.argtypes = [C_.c_void_p, C_.c_int, C_.c_int, C_.c_void_p, C_.c_void_p, C_.c_float,
+                                              C_.c_void_p, C_.c_void_p]
+    rng = np.random.default_rng(C + M)
+    logits = torch.from_numpy(rng.normal(0, 3, (M, C)).astype(np.float32)).half()
+    t = rng.integers(0, C, M).astype(np.int32)
+    t[5] = -1
+    t[7] = C  # out of range
+    tl = logits.float().numpy()[np.arange(M), np.clip(t, 0, C - 1)].astype(np.float32)
+    g = logits.clone().to(DEV)
+    td, tld = torch.from_numpy(t).to(DEV), torch.from_numpy(tl).to(DEV)
+    rl = torch.empty(M, device=DEV)
+    denom = float(M)
+    P = lambda x: C_.c_void_p(x.data_ptr())
+    assert L.nsb_op_cross_entropy_finish(P(g), M, C, P(td), P(tld), denom, P(rl),
+                                         C_.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    x = logits.double().numpy()
+    mx = x.max(1, keepdims=True)
+    lse = mx[:, 0] + np.log(np.exp(x - mx).sum(1))
+    valid = (t >= 0) & (t < C)
+    ref_loss = np.where(valid, lse - x[np.arange(M), np.clip(t, 0, C - 1)], 0.0)
+    np.testing.assert_allclose(rl.cpu().numpy(), ref_loss, rtol=2e-5, atol=2e-5)
+    seed = np.exp(x - lse[:, None])
+    seed[np.arange(M)[valid], t[valid]] -= 1.0
+    seed /= denom
+    got = g.view(torch.bfloat16).float().cpu().numpy()
+    assert relerr(got, seed) < 4e-3
+    # each element within bf16 rounding of the fp64 value
+    assert np.all(np.abs(got - seed) <= np.abs(seed) * (2.0 ** -8 + 1e-4) + 1e-12)
