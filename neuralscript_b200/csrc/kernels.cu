@@ -132,15 +132,27 @@ __global__ void emb_count_kernel(const float* __restrict__ ids, int M, int V, in
 }
 
 // Exclusive prefix sum of n ints, one block of 1024 threads: each thread
-// owns a contiguous run, runs are combined by warp-shuffle scans.
+// owns a contiguous run, runs are combined by warp-shuffle scans. Runs of up
+// to kScanRun elements (n <= 16384) are read into registers in one batch of
+// independent loads and written from there; longer runs loop over global.
+constexpr int kScanRun = 16;
 __global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ in, int* __restrict__ out, int n) {
     __shared__ int warp_tot[32];
     const int per = (n + 1023) / 1024;
     const int b0 = threadIdx.x * per;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const bool small = per <= kScanRun;
+    int vals[kScanRun];
     int local = 0;
-    for (int i = 0; i < per; i++)
-        if (b0 + i < n) local += in[b0 + i];
+    if (small) {
+#pragma unroll
+        for (int i = 0; i < kScanRun; i++) vals[i] = (i < per && b0 + i < n) ? in[b0 + i] : 0;
+#pragma unroll
+        for (int i = 0; i < kScanRun; i++) local += vals[i];
+    } else {
+        for (int i = 0; i < per; i++)
+            if (b0 + i < n) local += in[b0 + i];
+    }
     int x = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -160,11 +172,20 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ in, 
     }
     __syncthreads();
     int excl = x - local + (w > 0 ? warp_tot[w - 1] : 0);
-    for (int i = 0; i < per; i++) {
-        const int k = b0 + i;
-        if (k < n) {
-            out[k] = excl;
-            excl += in[k];
+    if (small) {
+#pragma unroll
+        for (int i = 0; i < kScanRun; i++)
+            if (i < per && b0 + i < n) {
+                out[b0 + i] = excl;
+                excl += vals[i];
+            }
+    } else {
+        for (int i = 0; i < per; i++) {
+            const int k = b0 + i;
+            if (k < n) {
+                out[k] = excl;
+                excl += in[k];
+            }
         }
     }
 }
@@ -861,8 +882,7 @@ __global__ void __launch_bounds__(256) ce_finish_kernel(void* __restrict__ g16, 
         const int t = targets[r];
         if (lane == 0) row_loss[r] = (t >= 0 && t < C) ? (lse2 - tlogit[r] * kL2e) * kLn2 : 0.f;
         const float inv = 1.f / denom;
-        for (int q2 = lane; q2 < n8; q2 += 32) {
-            uint4 u = row[q2];
+        auto seed_word = [&](uint4 u, int q2) {
             const __half2* hi = reinterpret_cast<const __half2*>(&u);
             __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
@@ -875,7 +895,17 @@ __global__ void __launch_bounds__(256) ce_finish_kernel(void* __restrict__ g16, 
                 h[e] = __floats2bfloat162_rn(a * inv, b * inv);
             }
             __stcs(row + q2, u);
+        };
+        // the second pass also keeps four 16-byte loads in flight per lane
+        int q2 = lane;
+        for (; q2 + 96 < n8; q2 += 128) {
+            uint4 u[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) u[k] = row[q2 + 32 * k];
+#pragma unroll
+            for (int k = 0; k < 4; k++) seed_word(u[k], q2 + 32 * k);
         }
+        for (; q2 < n8; q2 += 32) seed_word(row[q2], q2);
     }
 }
 
