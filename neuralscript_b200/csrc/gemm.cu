@@ -139,8 +139,18 @@ __device__ __forceinline__ void epi_pre32(const Epilogue& ep, int row, int col0,
                 for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], kRelu);
                 break;
             case kGelu:
+                if constexpr (FAST) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] *= FAST ? gelu_fast_deriv(z[j]) : act_deriv(z[j], kGelu);
+                    for (int j = 0; j < 32; j += 2) {
+                        float d0, d1;
+                        gelu_fast_deriv2(z[j], z[j + 1], d0, d1);
+                        v[j] *= d0;
+                        v[j + 1] *= d1;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) v[j] *= act_deriv(z[j], kGelu);
+                }
                 break;
             default:
 #pragma unroll
@@ -159,8 +169,13 @@ __device__ __forceinline__ void epi_act32(int act, float* v) {
             for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], kRelu);
             break;
         case kGelu:
+            if constexpr (FAST) {
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = FAST ? gelu_fast(v[j]) : act_fwd(v[j], kGelu);
+                for (int j = 0; j < 32; j += 2) gelu_fast2(v[j], v[j + 1]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] = act_fwd(v[j], kGelu);
+            }
             break;
         case kGeluMoe:
 #pragma unroll
