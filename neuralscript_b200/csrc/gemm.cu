@@ -872,6 +872,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // consecutive columns per thread when N % 4 == 0 and the workspace is aligned.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N, Epilogue ep, int vec4) {
     const size_t total = (size_t)M * N;
+    if (vec4 == 2) {
+        // Plain fp32 output (weight gradients): alpha, an optional fp32
+        // residual, column blocks of a multiple of 4; the splits' partials are
+        // loaded four at a time and summed in split order, one 16-byte store.
+        const size_t i4 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        if (4 * i4 >= total) return;
+        const float4* w4 = reinterpret_cast<const float4*>(ws) + i4;
+        const size_t stride4 = total / 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        int s = 0;
+        for (; s + 4 <= splits; s += 4) {
+            float4 w[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[k] = __ldcs(w4 + (size_t)(s + k) * stride4);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                v.x += w[k].x;
+                v.y += w[k].y;
+                v.z += w[k].z;
+                v.w += w[k].w;
+            }
+        }
+        for (; s < splits; s++) {
+            const float4 w = __ldcs(w4 + (size_t)s * stride4);
+            v.x += w.x;
+            v.y += w.y;
+            v.z += w.z;
+            v.w += w.w;
+        }
+        const int row = (int)(4 * i4 / N), col = (int)(4 * i4 % N);
+        v.x *= ep.alpha;
+        v.y *= ep.alpha;
+        v.z *= ep.alpha;
+        v.w *= ep.alpha;
+        if (ep.add) {
+            const float4 a = *reinterpret_cast<const float4*>(ep.add + (size_t)row * ep.ld_add + col);
+            v.x += ep.add_scale * a.x;
+            v.y += ep.add_scale * a.y;
+            v.z += ep.add_scale * a.z;
+            v.w += ep.add_scale * a.w;
+        }
+        float* dst;
+        if (ep.col_block) {
+            const int b = col / ep.col_block;
+            dst = ep.c32 + b * ep.col_block_stride + (size_t)row * ep.ld_c32 + (col - b * ep.col_block);
+        } else {
+            dst = ep.c32 + (size_t)row * ep.ld_c32 + col;
+        }
+        *reinterpret_cast<float4*>(dst) = v;
+        return;
+    }
     if (vec4) {
         const size_t i4 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
         if (4 * i4 >= total) return;
@@ -1321,7 +1372,15 @@ static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     if (e != cudaSuccess) return -5;
     if (p.splits > 1) {
         size_t total = (size_t)d.M * d.N;
-        const int vec4 = d.N % 4 == 0 && !(reinterpret_cast<uintptr_t>(p.workspace) & 15);
+        int vec4 = d.N % 4 == 0 && !(reinterpret_cast<uintptr_t>(p.workspace) & 15);
+        // the plain fp32-output form (every 16-byte group of a row in one
+        // column block, 16-byte aligned rows) takes the vector path
+        const Epilogue& e2 = d.ep;
+        if (vec4 && e2.c32 && !e2.c16 && !e2.z && !e2.dz && !e2.act && !e2.row_scale && !e2.out_rows &&
+            (e2.col_block % 4) == 0 && (e2.col_block_stride % 4) == 0 && (e2.ld_c32 % 4) == 0 &&
+            !(reinterpret_cast<uintptr_t>(e2.c32) & 15) &&
+            (!e2.add || ((e2.ld_add % 4) == 0 && !(reinterpret_cast<uintptr_t>(e2.add) & 15))))
+            vec4 = 2;
         const size_t threads = vec4 ? total / 4 : total;
         splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(p.workspace, p.splits, d.M, d.N, d.ep,
                                                                              vec4);
