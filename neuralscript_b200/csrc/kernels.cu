@@ -116,18 +116,25 @@ int embedding_fwd(const float* W, const float* ids, int M, int V, int D, float* 
 }
 
 size_t embedding_bwd_scratch_bytes(int M, int V) {
-    // count[V], offset[V], cursor[V], rows[M]
+    // count[V], offset[V], cursor[V], rows[M], then the large-bucket flag
     return sizeof(int) * ((size_t)3 * V + M) + 64;
 }
 
-__global__ void zero_ints_kernel(int* p, size_t n) {
+// Zeroes p[0, n) and, when given, the flag word.
+__global__ void zero_ints_kernel(int* p, size_t n, int* flag = nullptr) {
+    if (flag && blockIdx.x == 0 && threadIdx.x == 0) *flag = 0;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = 0;
 }
 
-__global__ void emb_count_kernel(const float* __restrict__ ids, int M, int V, int* count) {
+// Bucket sizes; *big becomes 1 when some bucket grows past kEmbWarpRows rows
+// (the bitmap kernel then has work).
+constexpr int kEmbWarpRows = 32;
+__global__ void emb_count_kernel(const float* __restrict__ ids, int M, int V, int* count, int* big) {
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
         long long v = (long long)ids[r];
-        if (v >= 0 && v < V) atomicAdd(&count[v], 1);  // integer counts: order-independent
+        if (v >= 0 && v < V) {
+            if (atomicAdd(&count[v], 1) == kEmbWarpRows) *big = 1;  // integer counts: order-independent
+        }
     }
 }
 
@@ -242,7 +249,6 @@ __device__ __forceinline__ void emb_sum_rows(const float* __restrict__ dout, int
 // staged in shared memory so the column loops (where only some lanes may be
 // active for narrow rows) never shuffle across inactive lanes. Larger
 // buckets are left to emb_big_kernel.
-constexpr int kEmbWarpRows = 32;
 // CH > 0: D = 128*CH with 16-byte aligned rows (one instantiation per width,
 // so each gets its own register budget); CH = 0: any D.
 template <int CH>
@@ -314,8 +320,9 @@ __global__ void __launch_bounds__(kEmbBigThreads) emb_big_kernel(const float* __
                                                                const int* __restrict__ count,
                                                                const int* __restrict__ offset,
                                                                const int* __restrict__ rows, float* __restrict__ dW,
-                                                               int vec) {
+                                                               int vec, const int* __restrict__ big) {
     __shared__ unsigned bits[kEmbBitmapRows / 32];
+    if (*big == 0) return;  // no bucket above kEmbWarpRows rows (uniform)
     const int tid = threadIdx.x;
     const int slots = vec ? D / 4 : D;  // float4 or scalar columns
     for (int v = blockIdx.x; v < V; v += gridDim.x) {
@@ -390,8 +397,9 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     int* offset = count + V;
     int* cursor = offset + V;
     int* rows = cursor + V;
-    zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3);
-    if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count);
+    int* big = rows + M;  // in the 64 bytes past the row list
+    zero_ints_kernel<<<grid_for((size_t)V * 3, 256), 256, 0, s>>>(count, (size_t)V * 3, big);
+    if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count, big);
     scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
     if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
     int vec = (D % 4 == 0) && aligned16(dout) && aligned16(dW);
@@ -402,10 +410,11 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     else if (vec && D == 1024) emb_reduce_kernel<8><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
     else emb_reduce_kernel<0><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
     if (M > kEmbWarpRows) {
-        // a few CTAs per SM walk the vocabulary; buckets of <= 32 rows are
-        // skipped after one read of their count
-        const unsigned big = (unsigned)(V < 148 * 4 ? V : 148 * 4);
-        emb_big_kernel<<<big, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec);
+        // a few CTAs per SM walk the vocabulary (all return at once when the
+        // count kernel saw no bucket above 32 rows); buckets of <= 32 rows
+        // are skipped after one read of their count
+        const unsigned nbig = (unsigned)(V < 148 * 4 ? V : 148 * 4);
+        emb_big_kernel<<<nbig, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec, big);
     }
     return launch_ok();
 }
@@ -422,7 +431,7 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
 // it (kNoAllocScratchBytes) until the process exits.
 constexpr int kNoAllocMaxRows = 262144;
 constexpr int kNoAllocMaxVocab = 65536;
-constexpr size_t kNoAllocScratchBytes = sizeof(int) * ((size_t)3 * kNoAllocMaxVocab + kNoAllocMaxRows);
+constexpr size_t kNoAllocScratchBytes = sizeof(int) * ((size_t)3 * kNoAllocMaxVocab + kNoAllocMaxRows) + 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of g_noalloc_scratch per device. In host code the symbol
