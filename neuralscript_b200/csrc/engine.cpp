@@ -19,6 +19,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <chrono>
 #include <condition_variable>
 #include <functional>
@@ -1841,6 +1842,7 @@ void nsb_free(ns_model* m) {
         for (auto& ev : r.pool) { cudaEventDestroy(ev.first); cudaEventDestroy(ev.second); }
     }
     if (m->h_loss) cudaFreeHost(m->h_loss);
+    if (m->h_targets) cudaFreeHost(m->h_targets);
     if (m->comm_stream) cudaStreamSynchronize(m->comm_stream);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
     if (m->ev_out) cudaEventDestroy(m->ev_out);
@@ -2120,6 +2122,134 @@ static int train_core(ns_model* m, int M, const float* d_labels, const int* d_ta
     return 0;
 }
 
+// ---------------------------------------------------------------------------
+// One-hot labels read on the host. ns_runtime_train_step / ns_objective_loss
+// take dense fp32 labels [M, C]; for the cross-entropy of the reference
+// (loss = sum over y > 0 of -log p, seed = (p - y) / denom) a row holding a
+// single 1.0 and zeros elsewhere is exactly the class index t, and an all-zero
+// row is an index outside [0, C) (loss 0, seed p / denom). Host threads read
+// the labels once; when every row is of these two kinds only the M indices
+// cross PCIe (64 KB instead of 537 MB for c4) and the step takes the
+// integer-target path. Any other row (smoothed or soft labels, a single
+// value other than 1.0) keeps the dense copy and the dense loss kernel.
+// ---------------------------------------------------------------------------
+namespace {
+struct ScanPool {
+    std::vector<std::thread> th;
+    std::mutex mu, job_mu;
+    std::condition_variable cv, done_cv;
+    std::function<void(int, int)> fn;  // (worker, workers)
+    long long gen = 0;
+    int pending = 0, n = 0;
+    ScanPool() {
+        // one worker per hardware thread up to 64; NS_B200_SCAN_THREADS overrides
+        const unsigned hc = std::thread::hardware_concurrency();
+        n = hc == 0 ? 4 : (int)(hc < 64u ? hc : 64u);
+        if (const char* e = getenv("NS_B200_SCAN_THREADS")) {
+            const int v = atoi(e);
+            if (v > 0 && v <= 256) n = v;
+        }
+        for (int i = 0; i < n; i++) th.emplace_back([this, i] { loop(i); });
+    }
+    void loop(int i) {
+        long long seen = 0;
+        for (;;) {
+            std::function<void(int, int)> f;
+            {
+                std::unique_lock<std::mutex> l(mu);
+                cv.wait(l, [&] { return gen != seen; });
+                seen = gen;
+                f = fn;
+            }
+            f(i, n);
+            std::lock_guard<std::mutex> l(mu);
+            if (--pending == 0) done_cv.notify_all();
+        }
+    }
+    // runs f on every worker and returns when all are done (one job at a time)
+    void run(std::function<void(int, int)> f) {
+        std::lock_guard<std::mutex> jl(job_mu);
+        std::unique_lock<std::mutex> l(mu);
+        fn = std::move(f);
+        pending = n;
+        gen++;
+        cv.notify_all();
+        done_cv.wait(l, [&] { return pending == 0; });
+    }
+};
+// Created on first use and never destroyed: its threads wait on a condition
+// variable until the process exits.
+ScanPool& scan_pool() {
+    static ScanPool* p = new ScanPool();
+    return *p;
+}
+
+// The class of a one-hot row: its column, -1 for an all-zero row, -2 for any
+// other row. Zero is tested on the magnitude bits (-0.0 counts as zero); the
+// row is streamed 64 bytes at a time (eight 64-bit words OR-ed together), and
+// only a block with a nonzero value is looked at element by element.
+int onehot_col(const float* x, int C) {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(x);
+    int col = -1;
+    auto one = [&](int k) -> bool {
+        const uint32_t b = u[k];
+        if ((b & 0x7fffffffu) == 0) return true;
+        if (b != 0x3f800000u || col >= 0) return false;  // not 1.0f, or a second nonzero
+        col = k;
+        return true;
+    };
+    int c = 0;
+    // unaligned head up to an 8-byte boundary
+    while (c < C && (reinterpret_cast<uintptr_t>(u + c) & 7))
+        if (!one(c++)) return -2;
+    const uint64_t kMag = 0x7fffffff7fffffffull;
+    for (; c + 16 <= C; c += 16) {
+        const uint64_t* w = reinterpret_cast<const uint64_t*>(u + c);
+        const uint64_t o = ((w[0] | w[1]) | (w[2] | w[3])) | ((w[4] | w[5]) | (w[6] | w[7]));
+        if (!(o & kMag)) continue;
+        for (int k = 0; k < 16; k++)
+            if (!one(c + k)) return -2;
+    }
+    for (; c < C; c++)
+        if (!one(c)) return -2;
+    return col;
+}
+}  // namespace
+
+// Reads M label rows into m->h_targets; true when every row is one-hot or
+// all-zero.
+static bool labels_as_targets(ns_model* m, const float* labels, int M) {
+    const char* e = getenv("NS_B200_LABEL_SCAN");
+    if ((e && e[0] == '0') || m->spec.loss == "mse") return false;
+    const int C = m->spec.out_cols;
+    if (C < 16) return false;  // small rows: the dense copy costs nothing
+    if (m->h_targets_cap < M) {
+        if (m->h_targets) cudaFreeHost(m->h_targets);
+        m->h_targets = nullptr;
+        m->h_targets_cap = 0;
+        if (cudaMallocHost(&m->h_targets, sizeof(int) * (size_t)M) != cudaSuccess) {
+            cudaGetLastError();
+            m->h_targets = nullptr;
+            return false;
+        }
+        m->h_targets_cap = M;
+    }
+    int* tg = m->h_targets;
+    std::atomic<int> dense{0};
+    scan_pool().run([&](int w, int nw) {
+        const int r0 = (int)((long long)M * w / nw), r1 = (int)((long long)M * (w + 1) / nw);
+        for (int r = r0; r < r1 && !dense.load(std::memory_order_relaxed); r++) {
+            const int t = onehot_col(labels + (size_t)r * C, C);
+            if (t == -2) {
+                dense.store(1, std::memory_order_relaxed);
+                return;
+            }
+            tg[r] = t;
+        }
+    });
+    return dense.load() == 0;
+}
+
 static int train_entry(ns_model* m, const float* input, const float* labels, const int* targets, size_t input_numel,
                        float* loss_out, float lr, bool train, bool device_ptrs, void* stream) {
     if (!m) return -1;
@@ -2141,7 +2271,11 @@ static int train_entry(ns_model* m, const float* input, const float* labels, con
     cudaMemcpyAsync(m->d_in, input, sizeof(float) * (size_t)M * m->spec.in_cols, k, m->stream);
     const float* dl = nullptr;
     const int* dt = nullptr;
-    if (labels) {
+    if (labels && !device_ptrs && labels_as_targets(m, labels, M)) {
+        // every label row is one-hot (or all zero): send the class indices
+        cudaMemcpyAsync(m->d_targets, m->h_targets, sizeof(int) * (size_t)M, cudaMemcpyHostToDevice, m->stream);
+        dt = m->d_targets;
+    } else if (labels) {
         cudaMemcpyAsync(m->d_labels, labels, sizeof(float) * (size_t)M * m->spec.out_cols, k, m->stream);
         dl = m->d_labels;
     } else {

@@ -147,6 +147,8 @@ struct ns_model {
     float* d_in = nullptr;
     float* d_labels = nullptr;
     int* d_targets = nullptr;
+    int* h_targets = nullptr;  // pinned: one-hot label rows read back as class indices
+    int h_targets_cap = 0;
     float* d_rowloss = nullptr;
     float* d_loss = nullptr;
     float* h_loss = nullptr;  // pinned

@@ -396,12 +396,12 @@ def test_config4_full_size_step_matches_reference():
 TC4W = TC4.replace("layer head dense in=128 out=128", "layer head dense in=128 out=512")
 
 
-def test_fused_head_cross_entropy_tracks_oracle_for_60_steps():
+def test_fused_head_cross_entropy_tracks_oracle_for_60_steps(monkeypatch):
     """bf16 training with int32 targets runs the fused head GEMM + loss
-    (bf16 logits, softmax partials from the GEMM epilogue, then one pass for
-    the loss and the seed). Losses within 1e-3 of the fp32 oracle at every
-    step, and within 1e-3 of the same model trained through the unfused
-    one-hot path."""
+    (fp16 logits and the fp32 target logit from the GEMM epilogue, then one
+    pass for the loss and the seed). Losses within 1e-3 of the fp32 oracle at
+    every step, and within 1e-3 of the same model trained through the unfused
+    dense-label path (the host label scan switched off)."""
     w = make_weights(TC4W, 1501, default_sd=0.05)
     tok = synth.tokens(2 * 128, 1502, 128)
     tgt = synth.tokens(2 * 128, 1503, 512).astype(np.int32)
@@ -412,10 +412,44 @@ def test_fused_head_cross_entropy_tracks_oracle_for_60_steps():
     got, base, exp = [], [], []
     for _ in range(60):
         got.append(fused.train_step_idx(tok, tgt, 3e-3))
+        monkeypatch.setenv("NS_B200_LABEL_SCAN", "0")
         base.append(plain.train_step(tok, y, 3e-3))  # dense labels: the unfused loss kernel
+        monkeypatch.delenv("NS_B200_LABEL_SCAN")
         exp.append(ref.train_step(tok, y, 3e-3))
     got, base, exp = (np.array(v, np.float64) for v in (got, base, exp))
     assert exp[-1] < 0.8 * exp[0]
     e_fused, e_plain = np.max(np.abs(got - exp) / exp), np.max(np.abs(base - exp) / exp)
     print(f"max relative loss deviation from the oracle: fused {e_fused:.2e}, unfused {e_plain:.2e}")
     assert e_fused < 1e-3 and e_plain < 1e-3, (e_fused, e_plain)
+
+
+def test_one_hot_labels_take_the_target_path_exactly(monkeypatch):
+    """ns_runtime_train_step reads one-hot label rows on the host and sends
+    class indices: the losses and weights equal the integer-target step bit
+    for bit (an all-zero row acts as a target outside the classes). A label
+    row that is not one-hot keeps the dense path: that run equals the run
+    with the host scan switched off."""
+    w = make_weights(TC4W, 1511, default_sd=0.05)
+    tok = synth.tokens(2 * 128, 1512, 128)
+    tgt = synth.tokens(2 * 128, 1513, 512).astype(np.int32)
+    y = synth.one_hot(tgt, 512)
+    y[7] = 0.0
+    tgt_z = tgt.copy()
+    tgt_z[7] = -1  # the all-zero row
+    a = nsb.Model(TC4W, w, precision="bf16")
+    b = nsb.Model(TC4W, w, precision="bf16")
+    la = [a.train_step(tok, y, 3e-3) for _ in range(3)]
+    lb = [b.train_step_idx(tok, tgt_z, 3e-3) for _ in range(3)]
+    assert la == lb
+    assert np.array_equal(a.get_weights(), b.get_weights())
+    soft = y.copy()
+    soft[3] = 0.0
+    soft[3, 5] = soft[3, 9] = 0.5  # not one-hot: the whole batch stays dense
+    c = nsb.Model(TC4W, w, precision="bf16")
+    d = nsb.Model(TC4W, w, precision="bf16")
+    lc = [c.train_step(tok, soft, 3e-3) for _ in range(2)]
+    monkeypatch.setenv("NS_B200_LABEL_SCAN", "0")
+    ld = [d.train_step(tok, soft, 3e-3) for _ in range(2)]
+    monkeypatch.delenv("NS_B200_LABEL_SCAN")
+    assert lc == ld
+    assert np.array_equal(c.get_weights(), d.get_weights())
