@@ -402,6 +402,7 @@ static const Op* ce_fusable_producer(const ns_model* m) {
 // ---------------------------------------------------------------------------
 static void free_plan(ns_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->wstream) cudaStreamSynchronize(m->wstream);
     for (void* p : m->plan_allocs) cudaFree(p);
     m->plan_allocs.clear();
     for (auto& v : m->vals) {
@@ -420,6 +421,8 @@ static void free_plan(ns_model* m) {
     m->d_targets = nullptr;
     m->d_stage = nullptr;
     m->d_ws = nullptr;
+    m->d_ws2 = nullptr;
+    m->ws2_floats = 0;
     m->ws_floats = 0;
     m->d_scratch = nullptr;
     m->scratch_bytes = 0;
@@ -530,6 +533,29 @@ static int run_gemm(ns_model* m, GemmDesc& d) {
     launch_counter() += gemm_uses_tensor_cores(d) && need ? 2 : 1;
     int r = gemm(d, m->stream, m->d_err);
     if (r) return fail("gemm launch failed (code " + std::to_string(r) + ")");
+    return 0;
+}
+
+// A weight-gradient GEMM: on the side stream when this backward uses it
+// (after everything issued so far on the main stream), else as run_gemm.
+static int run_gemm_w(ns_model* m, GemmDesc& d) {
+    if (!m->side_w) return run_gemm(m, d);
+    size_t need = gemm_workspace_floats(d);
+    if (need > m->ws2_floats) {
+        cudaStreamSynchronize(m->wstream);
+        void* p = plan_alloc(m, need * sizeof(float));
+        if (!p) return fail("workspace allocation failed");
+        m->d_ws2 = reinterpret_cast<float*>(p);
+        m->ws2_floats = need;
+    }
+    d.workspace = m->d_ws2;
+    d.workspace_floats = m->ws2_floats;
+    cudaEventRecord(m->ev_ms, m->stream);
+    cudaStreamWaitEvent(m->wstream, m->ev_ms, 0);
+    launch_counter() += gemm_uses_tensor_cores(d) && need ? 2 : 1;
+    int r = gemm(d, m->wstream, m->d_err);
+    if (r) return fail("gemm launch failed (code " + std::to_string(r) + ")");
+    m->side_used = true;
     return 0;
 }
 
@@ -1020,7 +1046,24 @@ static void layer_weights(const ns_model* m, int layer, int& w0, int& w1) {
     if (w0 < 0) w0 = w1 = 0;
 }
 
+static int backward_ops(ns_model* m, int M);
+
 static int backward(ns_model* m, int M) {
+    // weight gradients on the side stream: bf16 (every dW GEMM reads a bf16
+    // operand buffer of its own op), one rank (the data-parallel path reduces
+    // gradient buckets in issue order), not while regions are timed
+    m->side_w = m->wstream && m->wdt == kBF16 && m->world == 1 && !m->timing;
+    m->side_used = false;
+    const int rc = backward_ops(m, M);
+    if (m->side_used) {  // the optimizer and the next step follow every dW GEMM
+        cudaEventRecord(m->ev_sm, m->wstream);
+        cudaStreamWaitEvent(m->stream, m->ev_sm, 0);
+    }
+    m->side_w = false;
+    return rc;
+}
+
+static int backward_ops(ns_model* m, int M) {
     const Spec& s = m->spec;
     for (int oi = (int)m->ops.size() - 1; oi >= 0; oi--) {
         Op& op = m->ops[oi];
@@ -1069,7 +1112,7 @@ static int backward(ns_model* m, int M) {
                 gw.b = opnd(dz, m->wdt, w.cols, true);
                 gw.ep.c32 = m->d_g + w.off;
                 gw.ep.ld_c32 = w.cols;
-                if ((rc = run_gemm(m, gw))) break;
+                if ((rc = run_gemm_w(m, gw))) break;
                 if (in.gbuf) {
                     GemmDesc gx;
                     gx.M = M;
@@ -1137,7 +1180,7 @@ static int backward(ns_model* m, int M) {
                 go.b = opnd(dout, m->wdt, D, true);
                 go.ep.c32 = m->d_g + wo.off;
                 go.ep.ld_c32 = D;
-                if ((rc = run_gemm(m, go))) break;
+                if ((rc = run_gemm_w(m, go))) break;
                 GemmDesc gc;  // dctx = dout Wo^T
                 gc.M = M;
                 gc.N = D;
@@ -1193,7 +1236,7 @@ static int backward(ns_model* m, int M) {
                     gq.ep.ld_c32 = D;
                     gq.ep.col_block = D;
                     gq.ep.col_block_stride = (long long)D * D;
-                    if ((rc = run_gemm(m, gq))) break;
+                    if ((rc = run_gemm_w(m, gq))) break;
                 }
                 if (in.gbuf) {
                     GemmDesc gx;  // dx = dQKV [Wq|Wk|Wv]^T (+ running total)
@@ -1760,6 +1803,9 @@ static ns_model* init_one(const char* spec, const float* weights, size_t num_flo
     m->wdt = m->precision == 2 ? kBF16 : kF32;
     cudaGetDevice(&m->device);
     bool ok = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithFlags(&m->wstream, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&m->ev_ms, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&m->ev_sm, cudaEventDisableTiming) == cudaSuccess;
     const size_t n = m->spec.total;
     ok = ok && (m->d_err = (int*)persist_alloc(sizeof(int)));
     ok = ok && (m->d_w = (float*)persist_alloc(sizeof(float) * n));
@@ -1854,6 +1900,12 @@ void nsb_free(ns_model* m) {
         cudaStreamDestroy(m->copy_stream);
     }
     if (m->comm_stream) cudaStreamDestroy(m->comm_stream);
+    if (m->wstream) {
+        cudaStreamSynchronize(m->wstream);
+        cudaStreamDestroy(m->wstream);
+    }
+    if (m->ev_ms) cudaEventDestroy(m->ev_ms);
+    if (m->ev_sm) cudaEventDestroy(m->ev_sm);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }

@@ -154,6 +154,15 @@ struct ns_model {
     float* h_loss = nullptr;  // pinned
     float* d_ws = nullptr;    // split-K workspace
     size_t ws_floats = 0;
+    // weight-gradient GEMMs of the backward on a second stream (bf16, one
+    // rank): they overlap the input-gradient chain and join before the
+    // optimizer; their split-K workspace is their own
+    cudaStream_t wstream = nullptr;
+    cudaEvent_t ev_ms = nullptr, ev_sm = nullptr;  // main -> side, side -> main
+    float* d_ws2 = nullptr;
+    size_t ws2_floats = 0;
+    bool side_w = false;       // this backward uses the side stream
+    bool side_used = false;    // ... and has launched on it
     void* d_scratch = nullptr;  // embedding-gradient sort scratch
     size_t scratch_bytes = 0;
     // data parallel
