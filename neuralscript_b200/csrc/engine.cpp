@@ -1054,6 +1054,29 @@ static int backward(ns_model* m, int M) {
     // gradient buckets in issue order), not while regions are timed
     m->side_w = m->wstream && m->wdt == kBF16 && m->world == 1 && !m->timing;
     m->side_used = false;
+    m->emb_sorted = -1;
+    if (m->side_w && m->d_scratch) {
+        // a single embedding layer: its gradient's counting sort needs only
+        // the ids, so it runs on the side stream while the backward starts
+        int emb = -1, n_emb = 0;
+        for (size_t oi = 0; oi < m->ops.size(); oi++)
+            if (!m->ops[oi].skip && m->ops[oi].kind == OP_EMB) {
+                emb = (int)oi;
+                n_emb++;
+            }
+        if (n_emb == 1) {
+            const Op& op = m->ops[emb];
+            const LayerSpec& l = m->spec.layers[op.layer];
+            cudaEventRecord(m->ev_ms, m->stream);  // the ids are on the device
+            cudaStreamWaitEvent(m->wstream, m->ev_ms, 0);
+            launch_counter() += 4;
+            if (embedding_bwd_sort(m->vals[op.in].f32, M, (int)l.geti("vocab", 0), m->d_scratch, m->wstream))
+                return fail("embedding sort launch failed");
+            cudaEventRecord(m->ev_emb, m->wstream);
+            m->side_used = true;
+            m->emb_sorted = emb;
+        }
+    }
     const int rc = backward_ops(m, M);
     if (m->side_used) {  // the optimizer and the next step follow every dW GEMM
         cudaEventRecord(m->ev_sm, m->wstream);
@@ -1157,9 +1180,16 @@ static int backward_ops(ns_model* m, int M) {
             case OP_EMB: {
                 const LayerSpec& l = s.layers[op.layer];
                 const WeightInfo& w = s.weights[op.widx];
-                launch_counter() += 5;
-                rc = embedding_bwd(dv, in.f32, M, (int)l.geti("vocab", 0), (int)l.geti("dim", 0), m->d_g + w.off,
-                                   m->d_scratch, m->stream);
+                if (m->emb_sorted == oi) {  // the sort ran ahead on the side stream
+                    cudaStreamWaitEvent(m->stream, m->ev_emb, 0);
+                    launch_counter() += 2;
+                    rc = embedding_bwd_sum(dv, M, (int)l.geti("vocab", 0), (int)l.geti("dim", 0), m->d_g + w.off,
+                                           m->d_scratch, m->stream);
+                } else {
+                    launch_counter() += 5;
+                    rc = embedding_bwd(dv, in.f32, M, (int)l.geti("vocab", 0), (int)l.geti("dim", 0),
+                                       m->d_g + w.off, m->d_scratch, m->stream);
+                }
                 break;
             }
             case OP_ATTN: {
@@ -1806,6 +1836,7 @@ static ns_model* init_one(const char* spec, const float* weights, size_t num_flo
     ok = ok && cudaStreamCreateWithFlags(&m->wstream, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&m->ev_ms, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&m->ev_sm, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&m->ev_emb, cudaEventDisableTiming) == cudaSuccess;
     const size_t n = m->spec.total;
     ok = ok && (m->d_err = (int*)persist_alloc(sizeof(int)));
     ok = ok && (m->d_w = (float*)persist_alloc(sizeof(float) * n));
@@ -1906,6 +1937,7 @@ void nsb_free(ns_model* m) {
     }
     if (m->ev_ms) cudaEventDestroy(m->ev_ms);
     if (m->ev_sm) cudaEventDestroy(m->ev_sm);
+    if (m->ev_emb) cudaEventDestroy(m->ev_emb);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }

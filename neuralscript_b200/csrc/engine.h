@@ -163,6 +163,8 @@ struct ns_model {
     size_t ws2_floats = 0;
     bool side_w = false;       // this backward uses the side stream
     bool side_used = false;    // ... and has launched on it
+    cudaEvent_t ev_emb = nullptr;  // the embedding gradient's sort, done on the side stream
+    int emb_sorted = -1;           // op whose sort ran ahead on the side stream (-1: none)
     void* d_scratch = nullptr;  // embedding-gradient sort scratch
     size_t scratch_bytes = 0;
     // data parallel

@@ -391,8 +391,9 @@ __global__ void __launch_bounds__(kEmbBigThreads) emb_big_kernel(const float* __
     }
 }
 
-int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, float* dW, void* scratch,
-                  cudaStream_t s) {
+// The order of the gradient's sums depends on the ids alone: the counting
+// sort (zero, count, scan, fill) can run before the gradient exists.
+int embedding_bwd_sort(const float* ids, int M, int V, void* scratch, cudaStream_t s) {
     int* count = reinterpret_cast<int*>(scratch);
     int* offset = count + V;
     int* cursor = offset + V;
@@ -402,6 +403,16 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
     if (M > 0) emb_count_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, count, big);
     scan_kernel<<<1, 1024, 0, s>>>(count, offset, V);
     if (M > 0) emb_fill_kernel<<<grid_for((size_t)M, 256), 256, 0, s>>>(ids, M, V, offset, cursor, rows);
+    return launch_ok();
+}
+
+// The ordered sums into dW from the sort embedding_bwd_sort left in scratch.
+int embedding_bwd_sum(const float* dout, int M, int V, int D, float* dW, const void* scratch, cudaStream_t s) {
+    const int* count = reinterpret_cast<const int*>(scratch);
+    const int* offset = count + V;
+    const int* cursor = offset + V;
+    const int* rows = cursor + V;
+    const int* big = rows + M;
     int vec = (D % 4 == 0) && aligned16(dout) && aligned16(dW);
     const unsigned rg = grid_for((size_t)V, 8);
     if (vec && D == 512) emb_reduce_kernel<4><<<rg, 256, 0, s>>>(dout, D, V, count, offset, rows, dW, vec);
@@ -417,6 +428,13 @@ int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, floa
         emb_big_kernel<<<nbig, kEmbBigThreads, 0, s>>>(dout, M, D, V, count, offset, rows, dW, vec, big);
     }
     return launch_ok();
+}
+
+int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, float* dW, void* scratch,
+                  cudaStream_t s) {
+    const int rc = embedding_bwd_sort(ids, M, V, scratch, s);
+    if (rc) return rc;
+    return embedding_bwd_sum(dout, M, V, D, dW, scratch, s);
 }
 
 // ---------------------------------------------------------------------------

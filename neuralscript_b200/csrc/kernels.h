@@ -17,6 +17,10 @@ int embedding_fwd(const float* W, const float* ids, int M, int V, int D, float* 
 // dout[r,:]; ids outside [0,V) are skipped; untouched rows are zero.
 // scratch: at least embedding_bwd_scratch_bytes(M, V) bytes of device memory.
 size_t embedding_bwd_scratch_bytes(int M, int V);
+// embedding_bwd = embedding_bwd_sort (depends on the ids only) followed by
+// embedding_bwd_sum on the same scratch.
+int embedding_bwd_sort(const float* ids, int M, int V, void* scratch, cudaStream_t s);
+int embedding_bwd_sum(const float* dout, int M, int V, int D, float* dW, const void* scratch, cudaStream_t s);
 int embedding_bwd(const float* dout, const float* ids, int M, int V, int D, float* dW, void* scratch,
                   cudaStream_t s);
 
