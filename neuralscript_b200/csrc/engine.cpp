@@ -892,6 +892,14 @@ static int dist_collective(ns_model* m, size_t off, size_t count, int root, bool
     if (!ev) return fail("event creation failed");
     cudaEventRecord(ev, m->stream);
     cudaStreamWaitEvent(m->comm_stream, ev, 0);
+    if (m->side_w && m->side_used) {
+        // weight gradients computed on the backward's second stream: the
+        // collective also follows everything issued there so far
+        cudaEvent_t ev2 = dist_event(m);
+        if (!ev2) return fail("event creation failed");
+        cudaEventRecord(ev2, m->wstream);
+        cudaStreamWaitEvent(m->comm_stream, ev2, 0);
+    }
     launch_counter() += 1;
     ncclResult_t r;
     if (bcast)
@@ -1050,9 +1058,9 @@ static int backward_ops(ns_model* m, int M);
 
 static int backward(ns_model* m, int M) {
     // weight gradients on the side stream: bf16 (every dW GEMM reads a bf16
-    // operand buffer of its own op), one rank (the data-parallel path reduces
-    // gradient buckets in issue order), not while regions are timed
-    m->side_w = m->wstream && m->wdt == kBF16 && m->world == 1 && !m->timing;
+    // operand buffer of its own op), not while regions are timed; under data
+    // parallelism each bucket's collective also waits for the side stream
+    m->side_w = m->wstream && m->wdt == kBF16 && !m->timing;
     m->side_used = false;
     m->emb_sorted = -1;
     if (m->side_w && m->d_scratch) {
