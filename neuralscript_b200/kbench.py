@@ -4,6 +4,7 @@ events on the launching stream after warm-up.
 
     python -m neuralscript_b200.kbench gemm --M 16384 --N 2048 --K 512 --act gelu
     python -m neuralscript_b200.kbench gemm --M 16384 --N 8192 --K 512 --out f32
+    python -m neuralscript_b200.kbench gemm_ln --M 16384 --K 2048
     python -m neuralscript_b200.kbench attention --B 64 --S 256 --H 8 --D 512
     python -m neuralscript_b200.kbench layernorm --M 16384 --D 512
     python -m neuralscript_b200.kbench ce --M 16384 --C 8192
@@ -151,9 +152,46 @@ def adamw_case(n, iters=20):
     return {"kernel": "adamw", "n": n, "us": t * 1e6, "gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_kind": kind}
 
 
+def gemm_layernorm_case(M, K, iters=20):
+    """C[M,512] = LayerNorm(A B + residual) in one GEMM (the out-projection /
+    ff2 + residual + LayerNorm of the c2/c4 block): bf16 A [M,K] K-major,
+    B [K,512] MN-major, fp32 residual; fp32 and bf16 outputs and 1/sigma.
+    Bytes: A + residual read, both outputs written (the tensor-or-HBM floor
+    is the larger of FLOPs / peak and bytes / bandwidth)."""
+    import ctypes as C
+    import torch
+    from . import ops as O
+    L = O.L()
+    L.nsb_op_gemm_layernorm.restype = C.c_int
+    vp, ll = C.c_void_p, C.c_longlong
+    L.nsb_op_gemm_layernorm.argtypes = [C.c_int, C.c_int, vp, C.c_int, ll, vp, ll, C.c_float, vp, ll, vp, ll, vp,
+                                        ll, vp, vp, vp]
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(K, 512, device="cuda") * 0.05).bfloat16()
+    add = torch.randn(M, 512, device="cuda")
+    c32 = torch.empty(M, 512, device="cuda")
+    c16 = torch.empty(M, 512, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(M, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    P = lambda t: C.c_void_p(t.data_ptr())
+
+    def run():
+        rc = L.nsb_op_gemm_layernorm(M, K, P(A), 1, K, P(B), 512, 1.0, P(add), 512, P(c32), 512, P(c16), 512,
+                                     P(rstd), P(err), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0, rc
+
+    t = _time(run, iters)
+    pk, kind = _peaks()
+    fl = 2.0 * M * 512 * K
+    by = M * K * 2 + M * 512 * 4 + M * 512 * (4 + 2) + M * 4
+    floor = max(fl / (pk["bf16_tflops"] * 1e12), by / (pk["hbm_gbs"] * 1e9))
+    return {"kernel": "gemm_layernorm", "M": M, "N": 512, "K": K, "us": t * 1e6, "tflops": fl / t / 1e12,
+            "gbs": by / t / 1e9, "floor_us": floor * 1e6, "frac_of_floor": floor / t, "peak_kind": kind}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "layernorm", "ce", "embedding", "adamw"])
+    ap.add_argument("kernel", choices=["gemm", "gemm_ln", "attention", "layernorm", "ce", "embedding", "adamw"])
     ap.add_argument("--C", type=int, default=8192)
     ap.add_argument("--V", type=int, default=8192)
     ap.add_argument("--n", type=int, default=11_534_336)
@@ -175,6 +213,8 @@ def main():
     a = ap.parse_args()
     if a.kernel == "gemm":
         r = gemm_case(a.M, a.N, a.K, a.act, a.dtype, a.iters, a.out, a.residual, a.a_mn, a.b_mn)
+    elif a.kernel == "gemm_ln":
+        r = gemm_layernorm_case(a.M, a.K, a.iters)
     elif a.kernel == "attention":
         r = attention_case(a.B, a.S, a.H, a.D, a.iters, a.backward)
     elif a.kernel == "layernorm":
