@@ -936,12 +936,126 @@ __global__ void __launch_bounds__(256) ce_finish_kernel(void* __restrict__ g16, 
     }
 }
 
+// The same pass for rows of at most 16384 classes with the row held in
+// registers: a block of TPB threads reads its row once (NV 16-byte words of
+// 8 fp16 per thread) and writes the seed once. The warp-per-row form above
+// re-reads each row, and with an SM full of warps each holding a row the
+// re-read no longer finds it in L2. Row maximum on packed halves (exact);
+// the row sum on ex2.approx (the loss needs it to fp32 accuracy); the seed
+// 2^(x log2e - lse2) on exp2_poly3 (relative error 7.5e-5, inside the bf16
+// rounding of the seed) so that each element costs one MUFU exponential.
+template <int NV, int TPB>
+__global__ void __launch_bounds__(TPB) ce_finish_reg_kernel(void* __restrict__ g16, int M, int C,
+                                                            const int* __restrict__ targets,
+                                                            const float* __restrict__ tlogit, float denom,
+                                                            float* __restrict__ row_loss) {
+    constexpr float kL2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+    constexpr int W = TPB / 32;
+    constexpr uint32_t kNegInf2 = 0xfc00fc00u;  // two fp16 -inf: padding past the row end
+    __shared__ float red[2][W];
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int n8 = C / 8;
+    const float inv = 1.f / denom;
+    for (int r = blockIdx.x; r < M; r += gridDim.x) {
+        uint4* row = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(g16) + (size_t)r * C);
+        uint4 u[NV];
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const int q = tid + TPB * k;
+            u[k] = q < n8 ? __ldcs(row + q) : make_uint4(kNegInf2, kNegInf2, kNegInf2, kNegInf2);
+        }
+        const int t = targets[r];
+        const float tl = tlogit[r];
+        __half2 hm = *reinterpret_cast<const __half2*>(&u[0].x);
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const __half2* h = reinterpret_cast<const __half2*>(&u[k]);
+#pragma unroll
+            for (int e = 0; e < 4; e++) hm = __hmax2(hm, h[e]);
+        }
+        float mx = fmaxf(__low2float(hm), __high2float(hm));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) red[0][w] = mx;
+        __syncthreads();
+        mx = red[0][0];
+#pragma unroll
+        for (int i = 1; i < W; i++) mx = fmaxf(mx, red[0][i]);
+        const float m2 = mx * kL2e;
+        float sp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const __half2* h = reinterpret_cast<const __half2*>(&u[k]);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(h[e]);
+                sp[e] += ex2_approx_f(fmaf(f.x, kL2e, -m2)) + ex2_approx_f(fmaf(f.y, kL2e, -m2));
+            }
+        }
+        float s = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) red[1][w] = s;
+        __syncthreads();
+        s = red[1][0];
+#pragma unroll
+        for (int i = 1; i < W; i++) s += red[1][i];
+        const float lse2 = m2 + __log2f(s);
+        if (tid == 0) row_loss[r] = (t >= 0 && t < C) ? (lse2 - tl * kL2e) * kLn2 : 0.f;
+        const uint64_t L2E = f2_pack(kL2e, kL2e), NL = f2_pack(-lse2, -lse2), INV = f2_pack(inv, inv);
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const int q = tid + TPB * k;
+            if (q >= n8) continue;
+            const __half2* h = reinterpret_cast<const __half2*>(&u[k]);
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(h[e]);
+                float a, b;
+                f2_unpack(f2_fma(f2_pack(f.x, f.y), L2E, NL), a, b);
+                exp2_poly3_pair(a, b, y[2 * e], y[2 * e + 1]);
+            }
+            if ((unsigned)(t - 8 * q) < 8u) {  // the target class lies in this word
+#pragma unroll
+                for (int e = 0; e < 8; e++) y[e] -= 8 * q + e == t ? 1.f : 0.f;
+            }
+            uint4 o;
+            __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float a, b;
+                f2_unpack(f2_mul(f2_pack(y[2 * e], y[2 * e + 1]), INV), a, b);
+                ob[e] = __floats2bfloat162_rn(a, b);
+            }
+            __stcs(row + q, o);
+        }
+    }
+}
+
 int cross_entropy_finish(void* g16, int M, int C, const int* targets, const float* tlogit, float denom,
                          float* row_loss, cudaStream_t s) {
     if (M <= 0) return 0;
     if (C % 8 || (reinterpret_cast<uintptr_t>(g16) & 15)) return -1;
-    const unsigned blocks = (unsigned)min((M + 7) / 8, num_sms() * 8);
-    ce_finish_kernel<<<blocks, 256, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+    const int n8 = C / 8;
+    if (n8 <= 1024) {
+        const unsigned blocks = (unsigned)min(M, num_sms() * 16);
+        const int nv = (n8 + 127) / 128;
+        if (nv == 1)
+            ce_finish_reg_kernel<1, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+        else if (nv == 2)
+            ce_finish_reg_kernel<2, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+        else if (nv <= 4)
+            ce_finish_reg_kernel<4, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+        else
+            ce_finish_reg_kernel<8, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+    } else if (n8 <= 2048) {
+        const unsigned blocks = (unsigned)min(M, num_sms() * 8);
+        ce_finish_reg_kernel<8, 256><<<blocks, 256, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+    } else {
+        const unsigned blocks = (unsigned)min((M + 7) / 8, num_sms() * 8);
+        ce_finish_kernel<<<blocks, 256, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+    }
     return launch_ok();
 }
 

@@ -120,6 +120,37 @@ def cross_entropy_case(M, C, iters=20):
             "peak_kind": kind}
 
 
+def cross_entropy_finish_case(M, C, iters=20):
+    """The loss pass of the fused head: fp16 logits [M, C] read, the bf16 seed
+    gradient written over them in place, one loss per row. The pass rewrites
+    its input, so later iterations read the previous seed as fp16 (finite
+    values; the work per element does not depend on them). Bytes: 2 read +
+    2 written per element."""
+    import ctypes as C_
+    import torch
+    from . import ops as O
+    L = O.L()
+    L.nsb_op_cross_entropy_finish.restype = C_.c_int
+    vp = C_.c_void_p
+    L.nsb_op_cross_entropy_finish.argtypes = [vp, C_.c_int, C_.c_int, vp, vp, C_.c_float, vp, vp]
+    g = (torch.randn(M, C, device="cuda") * 3).half()
+    tgt = torch.randint(0, C, (M,), device="cuda", dtype=torch.int32)
+    tl = torch.randn(M, device="cuda")
+    row = torch.empty(M, device="cuda")
+    P = lambda t: C_.c_void_p(t.data_ptr())
+
+    def run():
+        rc = L.nsb_op_cross_entropy_finish(P(g), M, C, P(tgt), P(tl), float(M), P(row),
+                                           C_.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0, rc
+
+    t = _time(run, iters)
+    pk, kind = _peaks()
+    gbs = M * C * 4 / t / 1e9
+    return {"kernel": "cross_entropy_finish", "M": M, "C": C, "us": t * 1e6, "gbs": gbs,
+            "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_kind": kind}
+
+
 def embedding_case(M, V, D, iters=20, backward=False):
     """Gather (fp32 + bf16 out) and the deterministic sort-then-segment gradient."""
     import torch
@@ -191,7 +222,7 @@ def gemm_layernorm_case(M, K, iters=20):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "gemm_ln", "attention", "layernorm", "ce", "embedding", "adamw"])
+    ap.add_argument("kernel", choices=["gemm", "gemm_ln", "attention", "layernorm", "ce", "ce_finish", "embedding", "adamw"])
     ap.add_argument("--C", type=int, default=8192)
     ap.add_argument("--V", type=int, default=8192)
     ap.add_argument("--n", type=int, default=11_534_336)
@@ -221,6 +252,8 @@ def main():
         r = layernorm_case(a.M, a.D, a.iters)
     elif a.kernel == "ce":
         r = cross_entropy_case(a.M, a.C, a.iters)
+    elif a.kernel == "ce_finish":
+        r = cross_entropy_finish_case(a.M, a.C, a.iters)
     elif a.kernel == "embedding":
         r = embedding_case(a.M, a.V, a.D, a.iters, a.backward)
     else:
