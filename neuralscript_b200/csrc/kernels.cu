@@ -956,14 +956,24 @@ __global__ void __launch_bounds__(TPB) ce_finish_reg_kernel(void* __restrict__ g
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int n8 = C / 8;
     const float inv = 1.f / denom;
+    // the next row's loads are issued before this row's reductions, so each
+    // block keeps a row in flight while it works on the other
+    uint4 nx[NV];
+    auto load_row = [&](int rr) {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(g16) + (size_t)rr * C);
+#pragma unroll
+        for (int k = 0; k < NV; k++) {
+            const int q = tid + TPB * k;
+            nx[k] = q < n8 ? __ldcs(src + q) : make_uint4(kNegInf2, kNegInf2, kNegInf2, kNegInf2);
+        }
+    };
+    if ((int)blockIdx.x < M) load_row(blockIdx.x);
     for (int r = blockIdx.x; r < M; r += gridDim.x) {
         uint4* row = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(g16) + (size_t)r * C);
         uint4 u[NV];
 #pragma unroll
-        for (int k = 0; k < NV; k++) {
-            const int q = tid + TPB * k;
-            u[k] = q < n8 ? __ldcs(row + q) : make_uint4(kNegInf2, kNegInf2, kNegInf2, kNegInf2);
-        }
+        for (int k = 0; k < NV; k++) u[k] = nx[k];
+        if (r + (int)gridDim.x < M) load_row(r + gridDim.x);
         const int t = targets[r];
         const float tl = tlogit[r];
         __half2 hm = *reinterpret_cast<const __half2*>(&u[0].x);
@@ -1033,25 +1043,39 @@ __global__ void __launch_bounds__(TPB) ce_finish_reg_kernel(void* __restrict__ g
     }
 }
 
+// One resident wave of the register-resident loss pass: each block pipelines
+// its rows, so a block that waited for a free SM would start unpipelined.
+template <int NV, int TPB>
+static void ce_finish_reg_launch(void* g16, int M, int C, const int* targets, const float* tlogit, float denom,
+                                 float* row_loss, cudaStream_t s) {
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, ce_finish_reg_kernel<NV, TPB>, TPB, 0) != cudaSuccess)
+            n = 1;
+        per_sm = n > 0 ? n : 1;
+    }
+    const unsigned blocks = (unsigned)min(M, num_sms() * per_sm);
+    ce_finish_reg_kernel<NV, TPB><<<blocks, TPB, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+}
+
 int cross_entropy_finish(void* g16, int M, int C, const int* targets, const float* tlogit, float denom,
                          float* row_loss, cudaStream_t s) {
     if (M <= 0) return 0;
     if (C % 8 || (reinterpret_cast<uintptr_t>(g16) & 15)) return -1;
     const int n8 = C / 8;
     if (n8 <= 1024) {
-        const unsigned blocks = (unsigned)min(M, num_sms() * 16);
         const int nv = (n8 + 127) / 128;
         if (nv == 1)
-            ce_finish_reg_kernel<1, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+            ce_finish_reg_launch<1, 128>(g16, M, C, targets, tlogit, denom, row_loss, s);
         else if (nv == 2)
-            ce_finish_reg_kernel<2, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+            ce_finish_reg_launch<2, 128>(g16, M, C, targets, tlogit, denom, row_loss, s);
         else if (nv <= 4)
-            ce_finish_reg_kernel<4, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+            ce_finish_reg_launch<4, 128>(g16, M, C, targets, tlogit, denom, row_loss, s);
         else
-            ce_finish_reg_kernel<8, 128><<<blocks, 128, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+            ce_finish_reg_launch<8, 128>(g16, M, C, targets, tlogit, denom, row_loss, s);
     } else if (n8 <= 2048) {
-        const unsigned blocks = (unsigned)min(M, num_sms() * 8);
-        ce_finish_reg_kernel<8, 256><<<blocks, 256, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);
+        ce_finish_reg_launch<8, 256>(g16, M, C, targets, tlogit, denom, row_loss, s);
     } else {
         const unsigned blocks = (unsigned)min((M + 7) / 8, num_sms() * 8);
         ce_finish_kernel<<<blocks, 256, 0, s>>>(g16, M, C, targets, tlogit, denom, row_loss);

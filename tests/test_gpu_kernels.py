@@ -426,12 +426,13 @@ def test_exp2_poly3_error_bound():
     assert torch.all((yl > 0) & (yl <= 2.0 ** -124)), yl
 
 
-@pytest.mark.parametrize("M,C", [(300, 8192), (257, 4096), (130, 1000)])
+@pytest.mark.parametrize("M,C", [(300, 8192), (257, 4096), (130, 1000), (2500, 4096), (3000, 1000), (1500, 8192)])
 def test_cross_entropy_finish_from_fp16_logits(M, C):
     """The loss pass of the fused head (fp16 logits in, bf16 seed written in
     place) against fp64 on the same fp16 values: row losses within 2e-5, the
     seed within bf16 rounding; an out-of-range target gives
-    loss 0 and no -1 term."""
+    loss 0 and no -1 term. The larger cases give each block of the
+    register-resident pass several rows (its next-row prefetch)."""
     import ctypes as C_
     L = O.L()
     L.nsb_op_cross_entropy_finish.restype = C_.c_int
