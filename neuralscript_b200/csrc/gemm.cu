@@ -255,17 +255,25 @@ template <int BN, bool TF32>
 struct TcCfg {
     static constexpr int BM = 128;
     static constexpr int ELEM = TF32 ? 4 : 2;
-    static constexpr int BK = 128 / ELEM;  // K elements per stage: one 128-byte row
+    // K extent of a stage in bytes. The whole-row tile (BN = 512) takes
+    // 64-byte K rows (64-byte swizzle for K-major operands), so that four
+    // 40 KB stages fit beside the epilogue staging instead of two of 80 KB.
+    static constexpr int ROW_BYTES = BN == 512 ? 64 : 128;
+    static constexpr int BK = ROW_BYTES / ELEM;  // K elements per stage
     static constexpr int CHUNK = 128 / ELEM;  // MN elements per 128-byte chunk
     static constexpr int KSTEP = TF32 ? 8 : 16;  // K per MMA instruction (32 bytes)
-    static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
+    static constexpr int KSTEPS = BK / KSTEP;    // MMA instructions per stage and N slice
+    static constexpr int A_BYTES = BM * ROW_BYTES;
+    static constexpr int B_BYTES = BN * ROW_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    // K-major operands: 8-row swizzle atoms of ROW_BYTES-byte rows
+    static constexpr uint32_t K_SBO = 8 * ROW_BYTES;
+    static constexpr uint32_t K_LAYOUT = ROW_BYTES == 128 ? 2 : 4;  // 128- or 64-byte swizzle
     // BN = 512 (whole-row LayerNorm mode): one accumulator spanning all of
     // TMEM, filled by two N = 256 MMAs per k step
     static constexpr int NACC = BN == 512 ? 1 : 2;
     static constexpr int NMMA = BN == 512 ? 256 : BN;  // N of one MMA instruction
-    static constexpr int STAGES = BN == 512 ? 2 : (BN == 256 ? 4 : 6);
+    static constexpr int STAGES = BN == 256 || BN == 512 ? 4 : 6;
     static constexpr int TMEM_COLS = NACC * BN;
     // MN-major operands: 128-byte chunks along M/N, BK k-rows each. bf16 uses
     // the 16-byte-granule 128B swizzle (8-row atoms, SBO 1024); tf32 needs the
@@ -525,17 +533,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                     for (int h = 0; h < BN / C::NMMA; h++) {
                         // N-slice h of the tile: MN-major B in 128-byte column chunks,
-                        // K-major B in 128-byte rows
+                        // K-major B in ROW_BYTES-byte rows
                         const uint32_t sbh =
-                            sb + h * (B_MN ? (C::NMMA / C::CHUNK) * C::BK * 128 : C::NMMA * 128);
+                            sb + h * (B_MN ? (C::NMMA / C::CHUNK) * C::BK * 128 : C::NMMA * C::ROW_BYTES);
 #pragma unroll
-                        for (int k = 0; k < 4; k++) {
+                        for (int k = 0; k < C::KSTEPS; k++) {
                             uint64_t ad =
                                 A_MN ? ptx::smem_desc(sa + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
-                                     : ptx::smem_desc(sa + k * 32, 16, 1024, 2);
+                                     : ptx::smem_desc(sa + k * 32, 16, C::K_SBO, C::K_LAYOUT);
                             uint64_t bd =
                                 B_MN ? ptx::smem_desc(sbh + k * C::KSTEP * 128, C::BK * 128, C::MN_SBO, C::MN_LAYOUT)
-                                     : ptx::smem_desc(sbh + k * 32, 16, 1024, 2);
+                                     : ptx::smem_desc(sbh + k * 32, 16, C::K_SBO, C::K_LAYOUT);
                             uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
                             if (TF32) ptx::mma_tf32(d + h * C::NMMA, ad, bd, IDESC, accum);
                             else ptx::mma_bf16(d + h * C::NMMA, ad, bd, IDESC, accum);
@@ -1133,9 +1141,10 @@ static EncodeTiledFn get_encode() {
 
 // 2D map over a row-major [outer, inner] array with leading dimension ld
 // (elements); box {box_inner, box_outer}; 128-byte swizzle (32-byte granules
-// when atom32: MN-major tf32 operands).
+// when atom32: MN-major tf32 operands; 64-byte swizzle when sw64: K-major
+// operands of 64-byte K rows).
 static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner, long long outer, long long ld,
-                     int box_inner, int box_outer, bool atom32 = false) {
+                     int box_inner, int box_outer, bool atom32 = false, bool sw64 = false) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return false;
     const int es = dtype == kBF16 ? 2 : 4;
@@ -1145,7 +1154,8 @@ static bool make_map(CUtensorMap* m, const void* ptr, int dtype, long long inner
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                      const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                     atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                            : (sw64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B),
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -1288,18 +1298,21 @@ static bool ep_vec_ok(const GemmDesc& d) {
 static int gemm_tc(const GemmDesc& d, cudaStream_t s, int* dev_err) {
     const bool tf32 = d.a.dtype == kF32;
     const int bn = pick_bn(d);
-    const int bk = tf32 ? 32 : 64;
+    // K elements per stage: 128-byte K rows, 64-byte rows for the whole-row
+    // tile (TcCfg::ROW_BYTES)
+    const bool row64 = bn == 512;
+    const int bk = (tf32 ? 32 : 64) / (row64 ? 2 : 1);
     const int chunk = tf32 ? 32 : 64;
     CUtensorMap ta, tb;
     // A: M x K. K-major -> array [M][ld] (inner K); MN-major -> [K][ld] (inner M)
     bool ok;
-    if (!d.a.mn_major) ok = make_map(&ta, d.a.ptr, d.a.dtype, d.K, d.M, d.a.ld, bk, 128);
+    if (!d.a.mn_major) ok = make_map(&ta, d.a.ptr, d.a.dtype, d.K, d.M, d.a.ld, bk, 128, false, row64);
     else ok = make_map(&ta, d.a.ptr, d.a.dtype, d.M, d.K, d.a.ld, chunk, bk, tf32);
     if (!ok) return -2;
     const bool b_kgroup = d.groups > 1 && !d.group_k && d.b.mn_major;
     const long long brows = (d.groups > 1 && !d.group_k && !b_kgroup) ? (long long)d.N * d.groups : d.N;
     const long long bk_rows = b_kgroup ? (long long)d.K * d.groups : d.K;
-    if (!d.b.mn_major) ok = make_map(&tb, d.b.ptr, d.b.dtype, d.K, brows, d.b.ld, bk, bn);
+    if (!d.b.mn_major) ok = make_map(&tb, d.b.ptr, d.b.dtype, d.K, brows, d.b.ld, bk, bn, false, row64);
     else ok = make_map(&tb, d.b.ptr, d.b.dtype, brows, bk_rows, d.b.ld, chunk, bk, tf32);
     if (!ok) return -2;
 
