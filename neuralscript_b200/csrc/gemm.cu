@@ -273,15 +273,17 @@ struct TcCfg {
     // TMEM, filled by two N = 256 MMAs per k step
     static constexpr int NACC = BN == 512 ? 1 : 2;
     static constexpr int NMMA = BN == 512 ? 256 : BN;  // N of one MMA instruction
-    static constexpr int STAGES = BN == 256 || BN == 512 ? 4 : 6;
+    static constexpr int STAGES = BN == 512 ? 5 : (BN == 256 ? 4 : 6);
     static constexpr int TMEM_COLS = NACC * BN;
     // MN-major operands: 128-byte chunks along M/N, BK k-rows each. bf16 uses
     // the 16-byte-granule 128B swizzle (8-row atoms, SBO 1024); tf32 needs the
     // 32-byte-granule variant (4-row atoms, SBO 512).
     static constexpr uint32_t MN_LAYOUT = TF32 ? 1 : 2;
     static constexpr uint32_t MN_SBO = TF32 ? 512 : 1024;
-    // epilogue staging: per epilogue warp two 2 KB buffers (32 rows x 64 B)
-    static constexpr int STAGING = 8 * 2 * 2048;
+    // epilogue staging: per epilogue warp two 2 KB buffers (32 rows x 64 B);
+    // one for the whole-row tile, whose fifth stage takes the difference
+    static constexpr int NSTG = BN == 512 ? 1 : 2;
+    static constexpr int STAGING = 8 * NSTG * 2048;
     static constexpr int SMEM = STAGES * STAGE_BYTES + STAGING + 1024 /*align*/ + 512 /*barriers, queue*/ +
                                 (BN == 512 ? 2048 : 0) /*LayerNorm row statistics*/;
     static_assert(SMEM <= 227 * 1024, "dynamic shared memory above the 227 KB per-block limit");
@@ -574,12 +576,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // swizzle (16-byte granule j of row r at j ^ ((r >> 1) & 3)), which is
         // also conflict-free for the row-per-thread writes. Every box (32
         // bf16 or 16 fp32 columns) fills one buffer; the buffers alternate,
-        // so writing one overlaps the store of the other.
-        uint8_t* stg = staging + (warp - 2) * 4096;
+        // so writing one overlaps the store of the other (the whole-row tile
+        // keeps one buffer per warp and waits for its previous store).
+        uint8_t* stg = staging + (warp - 2) * (C::NSTG * 2048);
         int sbuf = 0;
         auto stage_store = [&](const CUtensorMap* map, const uint4* g4, int x, int y) {
             uint8_t* buf = stg + sbuf * 2048;
-            if (lane == 0) ptx::bulk_wait_read1();
+            if (lane == 0) {
+                if (C::NSTG == 2) ptx::bulk_wait_read1();
+                else ptx::bulk_wait_read0();
+            }
             __syncwarp();
             uint8_t* rowp = buf + lane * 64;
 #pragma unroll
@@ -590,7 +596,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ptx::tma_store_2d(map, buf, x, y);
                 ptx::bulk_commit();
             }
-            sbuf ^= 1;
+            if (C::NSTG == 2) sbuf ^= 1;
         };
         auto out_f32 = [&](const CUtensorMap* map, const float* v, int col0, int y) {
             const uint4* g8 = reinterpret_cast<const uint4*>(v);
